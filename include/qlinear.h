@@ -1,0 +1,96 @@
+/*
+ * webpytorch_b200 — C ABI of the B200 (sm_100a) quantized-linear library (libqlinear.so).
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream passed as `void*`
+ * (a cudaStream_t; NULL means the legacy default stream), runs asynchronously on that
+ * stream, and returns an int status (QL_OK == 0). It never aborts and never frees what it
+ * is given; the caller owns every buffer. On failure ql_last_error() returns a message for
+ * the calling thread.
+ *
+ * Citations are to the reference project (xnetsc/webpytorch, package `webtorch`), whose
+ * operator each entry point replaces.
+ */
+#ifndef WEBPYTORCH_B200_QLINEAR_H
+#define WEBPYTORCH_B200_QLINEAR_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QL_API __attribute__((visibility("default")))
+#else
+#define QL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of activations, scales and outputs */
+enum { QL_F32 = 0, QL_F16 = 1, QL_BF16 = 2 };
+
+/* status codes */
+enum {
+  QL_OK = 0,
+  QL_ERR_ARG = 1,         /* bad size, null pointer or unsupported parameter combination */
+  QL_ERR_ALIGN = 2,       /* a pointer or stride violates the alignment a kernel needs   */
+  QL_ERR_UNSUPPORTED = 3, /* valid input this build does not implement                  */
+  QL_ERR_CUDA = 4,        /* a CUDA runtime call failed (message says which)             */
+  QL_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up                           */
+};
+
+/* Library version as major*10000 + minor*100 + patch. */
+QL_API int ql_version(void);
+
+/* Message describing the last failure on the calling thread ("" if none). */
+QL_API const char* ql_last_error(void);
+
+/*
+ * Exact GPTQ dequantisation to fp32, W[k, n] = scales[g, n] * (q[k, n] - (z[g, n] + zero_offset))
+ * with g = g_idx[k] (or k / gs when g_idx is NULL), computed in double and rounded once to
+ * fp32, so the result is bit-identical to the reference's numpy unpack.
+ *   qweight int32 [K/per, N] (per = 32/bits values packed LSB-first along K)
+ *   qzeros  int32 [K/gs, N/per] (packed LSB-first along N)
+ *   scales  [K/gs, N] of scales_dtype (QL_F32 / QL_F16 / QL_BF16)
+ *   W       fp32 [K, N]
+ * Replaces: webtorch/_core.py:4046-4072 (_gptq_matmul_np's unpack) and
+ *           webtorch/quantize.py:32-43 (dequant_int).
+ */
+QL_API int ql_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                    int scales_dtype, const int32_t* g_idx, float* W, int K, int N, int gs,
+                    int bits, float zero_offset, void* stream);
+
+/*
+ * Quantized linear y[M, N] = x[M, K] @ dequant(W) (+ bias), fp32 accumulation.
+ *   x        [M, K] of x_dtype, row stride ldx (elements)
+ *   x_perm   NULL, or int32 [K]: the kernel reads x[:, x_perm[k]] in place of x[:, k]
+ *            (the activation-order permutation that goes with ql_gptq_sort_rows)
+ *   qweight / qzeros / scales as in ql_gptq_dequant, group size gs (a multiple of 32)
+ *   bias     NULL or fp32 [N]
+ *   out      [M, N] of out_dtype, row stride ldo (elements)
+ *   zero_offset 0 (reference's own packing) or 1 (AutoGPTQ "stores zero-1" convention)
+ * Selects the kernel family from M: a register-unpacking tensor-core GEMV for small M and
+ * a tcgen05 dequant-GEMM for large M.
+ * Replaces: webtorch/_core.py:4008-4043 (_gptq_matmul), called from
+ *           QuantizedLinear.forward webtorch/_core.py:4446-4456.
+ */
+QL_API int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                   const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                   int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
+                   int M, int K, int N, int gs, int bits, float zero_offset, void* stream);
+
+/*
+ * Load-time row sort for act-order (desc_act) checkpoints: qweight_out row k' takes packed
+ * value k = perm[k'] of qweight_in (both int32 [K/per, N]). With perm = a stable argsort of
+ * g_idx, every group becomes a contiguous run of gs rows and ql_gptq_matmul(x_perm = perm)
+ * computes the same product as the unsorted weight with g_idx.
+ * Replaces: nothing in the reference (it ignores g_idx: webtorch/_core.py:4056 and
+ *           webtorch/llm.py:569-573); it is the loader-side half of desc_act support.
+ */
+QL_API int ql_gptq_sort_rows(const int32_t* qweight_in, const int32_t* perm, int32_t* qweight_out,
+                      int K, int N, int bits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WEBPYTORCH_B200_QLINEAR_H */

@@ -1,0 +1,162 @@
+"""Generate the golden fixtures in this folder by running the REFERENCE's own CPU code.
+
+Run in a container where the reference project (xnetsc/webpytorch) is importable:
+    python tests/golden/make_golden.py [path-to-reference-checkout]
+It imports `webtorch` from that checkout (no cupy there, so `_core.GPU` is False and every
+operator takes its numpy path), runs the qlinear / Q4_K / MoE paths on seeded inputs and
+saves inputs and outputs as .npz files here. Tests never import the reference; they read
+these files, which is what lets them run on a machine without it.
+
+Cases:
+  gptq_ref_*.npz   the reference's own correctness shapes (examples/gptq_int4_correctness.py:30-37):
+                   weights from the reference quantiser `_gptq_quantize`, zero offset 0,
+                   M in {1, 3, 4, 5, 32}; outputs of `QuantizedLinear(...)(Tensor(x))`.
+  gptq_autogptq_*.npz  synthetic AutoGPTQ tensors through `QuantizedLinear.from_autogptq`
+                   (zero offset 1), including the config-0 shape (K=896, N=4864, M=1) and int8.
+  gptq_fromlinear.npz  `QuantizedLinear.from_linear` with K/N padding and a bias.
+  q4k_*.npz        raw Q4_K bytes, `ggufload.dequant` output and x @ W.T.
+  moe_*.npz        `lm_engine.moe_mlp` with a stub router returning fixed logits and
+                   `QuantizedLinear.from_autogptq` experts.
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from webpytorch_b200 import synth  # noqa: E402  (seeded generators shared with bench.py)
+
+
+def _import_reference(path):
+    sys.path.insert(0, path)
+    from webtorch import _core as wt  # noqa
+    from webtorch import ggufload as G  # noqa
+    from webtorch import lm_engine as LE  # noqa
+    assert not wt.GPU, "the reference must run its numpy path here"
+    return wt, G, LE
+
+
+def gptq_ref_cases(wt):
+    rng = np.random.default_rng(0)
+    for (K, N, gs, bits) in [(128, 64, 32, 4), (256, 128, 128, 4), (512, 256, 128, 4),
+                             (128, 24, 32, 4), (256, 64, 32, 8), (384, 128, 128, 8)]:
+        W = (rng.standard_normal((K, N)) * 0.1).astype(np.float32)
+        qw, qz, sc, _, _ = wt._gptq_quantize(W, gs, bits)
+        ql = wt.QuantizedLinear(qw, qz, sc, np.zeros((N,), np.float32), K, N, K, N, gs, bits)
+        d = {"K": K, "N": N, "gs": gs, "bits": bits, "zoff": 0.0, "qweight": qw, "qzeros": qz,
+             "scales": sc}
+        # the exact weight the reference forms inside _gptq_matmul_np (_core.py:4069)
+        per = 32 // bits
+        q = np.empty((K, N), np.int32)
+        for r in range(per):
+            q[r::per] = (qw >> (bits * r)) & ((1 << bits) - 1)
+        z = np.empty((K // gs, N), np.int32)
+        for r in range(per):
+            z[:, r::per] = (qz >> (bits * r)) & ((1 << bits) - 1)
+        g = np.arange(K) // gs
+        d["W"] = (sc[g] * (q - (z[g] + 0.0))).astype(np.float32)
+        for M in (1, 3, 4, 5, 32):
+            x = (rng.standard_normal((M, K)) * 0.5).astype(np.float32)
+            d["x_%d" % M] = x
+            d["y_%d" % M] = ql(wt.Tensor(x)).numpy()
+        np.savez_compressed(os.path.join(HERE, "gptq_ref_K%d_N%d_g%d_b%d.npz" % (K, N, gs, bits)), **d)
+
+
+def gptq_autogptq_cases(wt):
+    for (K, N, gs, bits, M, seed, with_bias) in [(896, 4864, 128, 4, 1, 0, False),
+                                                 (256, 128, 128, 8, 5, 1, True),
+                                                 (512, 192, 128, 4, 16, 2, True),
+                                                 (256, 96, 32, 4, 3, 3, False)]:
+        rng = np.random.default_rng(seed)
+        w = synth.gptq_weights(K, N, bits, gs, rng=rng)
+        x = rng.standard_normal((M, K)).astype(np.float16)
+        bias = rng.standard_normal(N).astype(np.float32) if with_bias else None
+        ql = wt.QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], bias, gs, bits)
+        y = ql(wt.Tensor(x.astype(np.float32))).numpy()
+        d = {"K": K, "N": N, "gs": gs, "bits": bits, "zoff": 1.0, "x": x, "y": y,
+             "qweight": w["qweight"], "qzeros": w["qzeros"], "scales": w["scales"]}
+        if bias is not None:
+            d["bias"] = bias
+        np.savez_compressed(os.path.join(HERE, "gptq_autogptq_K%d_N%d_g%d_b%d.npz" % (K, N, gs, bits)), **d)
+
+
+def gptq_fromlinear_case(wt):
+    rng = np.random.default_rng(7)
+    K, N, gs, bits = 200, 60, 32, 4
+    lin = wt.Linear(K, N)
+    lin.weight.data[...] = (rng.standard_normal((K, N)) * 0.1).astype(np.float32)
+    lin.bias.data[...] = rng.standard_normal(N).astype(np.float32)
+    ql = wt.QuantizedLinear.from_linear(lin, group_size=gs, bits=bits)
+    x = (rng.standard_normal((2, 3, K)) * 0.5).astype(np.float32)
+    y = ql(wt.Tensor(x)).numpy()
+    np.savez_compressed(os.path.join(HERE, "gptq_fromlinear.npz"), K=K, N=N, gs=gs, bits=bits,
+                        Kp=ql.Kp, Np=ql.Np, weight=np.asarray(lin.weight.data), bias=np.asarray(lin.bias.data),
+                        qweight=np.asarray(ql.qweight), qzeros=np.asarray(ql.qzeros),
+                        scales=np.asarray(ql.scales), x=x, y=y)
+
+
+def q4k_cases(G):
+    # (a) the reference self-check's recipe (_core.py:3697-3705): random bytes, redrawn until finite
+    for seed in range(32):
+        rng = np.random.default_rng(seed)
+        raw = rng.integers(0, 256, (8, 2 * 144), dtype=np.uint8)
+        W = np.asarray(G.dequant(12, raw.tobytes(), 8 * 512), np.float32).reshape(8, 512)
+        if np.all(np.isfinite(W)) and float(np.abs(W).max()) < 1e4:
+            break
+    x = rng.standard_normal((3, 512)).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "q4k_randombytes.npz"), N=8, K=512, raw=raw, W=W, x=x,
+                        y=(x @ W.T).astype(np.float32))
+    # (b) the benchmark distribution (config 2) at a small size
+    rng = np.random.default_rng(11)
+    N, K = 64, 1024
+    raw = synth.q4k_weights(N, K, rng=rng)
+    W = np.asarray(G.dequant(12, raw.tobytes(), N * K), np.float32).reshape(N, K)
+    d = {"N": N, "K": K, "raw": raw, "W": W}
+    for M in (1, 8, 13):
+        x = rng.standard_normal((M, K)).astype(np.float32)
+        d["x_%d" % M] = x
+        d["y_%d" % M] = (x @ W.T).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "q4k_synth.npz"), **d)
+
+
+def moe_cases(wt, LE):
+    for (E, top_k, H, I, T, seed) in [(8, 2, 128, 64, 5, 0), (16, 8, 256, 128, 12, 1)]:
+        rng = np.random.default_rng(100 + seed)
+        exps = synth.moe_experts(E, H, I, bits=4, gs=64, rng=rng)
+        logits = rng.standard_normal((T, E)).astype(np.float32)
+        x = rng.standard_normal((T, H)).astype(np.float32)
+
+        class _LM:
+            pass
+        lm = _LM()
+        lm.H = H
+        experts = [{k: wt.QuantizedLinear.from_autogptq(e[k]["qweight"], e[k]["qzeros"], e[k]["scales"],
+                                                         None, 64, 4) for k in ("gate", "up", "down")}
+                   for e in exps]
+        lay = {"moe": {"gate": (lambda t, _l=logits: wt.Tensor(_l)), "top_k": top_k,
+                       "norm_topk_prob": True, "experts": experts, "shared": None}}
+        y = LE.moe_mlp(lm, lay, wt.Tensor(x)).numpy()
+        d = {"E": E, "top_k": top_k, "H": H, "I": I, "T": T, "gs": 64, "bits": 4, "logits": logits, "x": x,
+             "y": y}
+        for i, e in enumerate(exps):
+            for k in ("gate", "up", "down"):
+                for f in ("qweight", "qzeros", "scales"):
+                    d["e%d_%s_%s" % (i, k, f)] = e[k][f]
+        np.savez_compressed(os.path.join(HERE, "moe_E%d_k%d_T%d.npz" % (E, top_k, T)), **d)
+
+
+def main():
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WEBTORCH_REFERENCE", "/root/reference")
+    wt, G, LE = _import_reference(ref)
+    gptq_ref_cases(wt)
+    gptq_autogptq_cases(wt)
+    gptq_fromlinear_case(wt)
+    q4k_cases(G)
+    moe_cases(wt, LE)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,76 @@
+"""The C-ABI library loads on the host and exports exactly what include/*.h declares (CPU only).
+
+Argument validation happens on the host before any CUDA call, so bad arguments are checked
+here without a GPU.
+"""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from webpytorch_b200 import _build, _ffi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        names |= set(re.findall(r"QL_API\s+[\w\s\*]+?\b(ql_\w+)\s*\(", src))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    _build.build()
+    return _ffi.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = declared_symbols()
+    assert "ql_gptq_matmul" in names and len(names) >= 5
+    raw = ctypes.CDLL(_ffi.lib_path())
+    for n in names:
+        assert hasattr(raw, n), n
+    assert set(names) <= set(_ffi.SIGNATURES), set(names) - set(_ffi.SIGNATURES)
+
+
+def test_version_and_empty_error(lib):
+    assert lib.ql_version() >= 100
+    assert lib.ql_last_error() is not None
+
+
+def _matmul_rc(lib, **kw):
+    a = dict(x=1, x_dtype=1, ldx=128, x_perm=None, qw=16, qz=16, sc=16, sc_dtype=1, bias=None, out=16,
+             out_dtype=0, ldo=64, M=1, K=128, N=64, gs=128, bits=4, zoff=1.0)
+    a.update(kw)
+    v = ctypes.c_void_p
+    return lib.ql_gptq_matmul(v(a["x"]), a["x_dtype"], a["ldx"], v(a["x_perm"]) if a["x_perm"] else None,
+                              v(a["qw"]), v(a["qz"]), v(a["sc"]), a["sc_dtype"], a["bias"], v(a["out"]),
+                              a["out_dtype"], a["ldo"], a["M"], a["K"], a["N"], a["gs"], a["bits"],
+                              a["zoff"], None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(bits=5), 3), (dict(bits=2), 3), (dict(K=130), 1), (dict(gs=0), 1), (dict(N=60), 1),
+    (dict(x_dtype=7), 1), (dict(out_dtype=9), 1), (dict(M=-1), 1), (dict(x=0), 1), (dict(ldx=64), 1),
+    (dict(gs=16, K=128), 3), (dict(zoff=0.5), 3), (dict(qw=8), 2), (dict(N=68, ldo=68), 1),
+])
+def test_matmul_rejects_bad_arguments_on_host(lib, kw, code):
+    assert _matmul_rc(lib, **kw) == code
+    assert lib.ql_last_error()
+
+
+def test_matmul_m_zero_is_a_noop(lib):
+    assert _matmul_rc(lib, M=0) == 0
+
+
+def test_other_entry_points_reject_bad_arguments(lib):
+    v = ctypes.c_void_p
+    assert lib.ql_gptq_dequant(v(16), v(16), v(16), 1, None, v(16), 128, 64, 128, 3, 0.0, None) == 3
+    assert lib.ql_gptq_sort_rows(v(16), v(16), v(16), 128, 64, 6, None) == 3
+    assert lib.ql_gptq_sort_rows(v(16), v(16), v(16), 127, 64, 4, None) == 1
+    assert lib.ql_gptq_sort_rows(v(16), v(16), v(16), 128, 64, 4, None) == 1  # aliasing

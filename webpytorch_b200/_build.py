@@ -1,0 +1,90 @@
+"""Builds libqlinear.so (every CUDA source under csrc/) for sm_100a with nvcc.
+
+The library is built in-tree (webpytorch_b200/_lib/) so it travels with the source tree;
+nothing is JIT-compiled at import time. `python -m webpytorch_b200._build` rebuilds it.
+"""
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+LIBDIR = os.path.join(HERE, "_lib")
+LIB = os.path.join(LIBDIR, "libqlinear.so")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xcompiler", "-fPIC,-O2",
+         "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]
+
+
+def _sources():
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
+def _digest():
+    h = hashlib.sha256()
+    for p in _sources() + sorted(
+            os.path.join(d, f) for d in (CSRC, INCLUDE) for f in os.listdir(d)
+            if f.endswith((".cuh", ".h"))):
+        with open(p, "rb") as fh:
+            h.update(os.path.basename(p).encode())
+            h.update(fh.read())
+    h.update(" ".join(ARCH + FLAGS).encode())
+    return h.hexdigest()[:16]
+
+
+def _nvcc():
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found; it is needed to build webpytorch_b200's CUDA library")
+
+
+def build(force=False, verbose=False):
+    """Compile csrc/*.cu into _lib/libqlinear.so unless an up-to-date build exists."""
+    os.makedirs(LIBDIR, exist_ok=True)
+    stamp = os.path.join(LIBDIR, "libqlinear.stamp")
+    dig = _digest()
+    if not force and os.path.exists(LIB) and os.path.exists(stamp):
+        with open(stamp) as fh:
+            if fh.read().strip() == dig:
+                return LIB
+    nvcc = _nvcc()
+    objdir = os.path.join(LIBDIR, "obj")
+    os.makedirs(objdir, exist_ok=True)
+    objs = []
+    procs = []
+    for src in _sources():
+        obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
+        cmd = [nvcc] + ARCH + FLAGS + ["-I", INCLUDE, "-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)))
+        objs.append(obj)
+    errs = []
+    for src, p in procs:
+        out, _ = p.communicate()
+        if p.returncode != 0:
+            errs.append("%s:\n%s" % (src, out.decode(errors="replace")))
+        elif verbose and out:
+            print(out.decode(errors="replace"), file=sys.stderr)
+    if errs:
+        raise RuntimeError("nvcc failed:\n" + "\n".join(errs))
+    tmp = LIB + ".tmp"
+    # static cudart: the library needs no libcudart/libcuda at load time (it loads on a
+    # GPU-less host for ABI checks) and shares the primary context with torch's runtime
+    cmd = [nvcc] + ARCH + ["-shared", "-cudart", "static", "-o", tmp] + objs
+    r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)
+    if r.returncode != 0:
+        raise RuntimeError("link failed:\n" + r.stdout.decode(errors="replace"))
+    os.replace(tmp, LIB)
+    with open(stamp, "w") as fh:
+        fh.write(dig)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,87 @@
+"""ctypes binding of libqlinear.so (the C ABI declared in include/qlinear.h).
+
+There is no fallback: if the library is missing or a call fails, this raises.
+"""
+import ctypes
+import os
+
+from . import _build
+
+F32, F16, BF16 = 0, 1, 2
+_STATUS = {0: "ok", 1: "bad argument", 2: "misaligned", 3: "unsupported", 4: "CUDA error",
+           5: "device wait timed out"}
+
+_lib = None
+
+_c_int, _c_long, _c_float = ctypes.c_int, ctypes.c_long, ctypes.c_float
+_vp = ctypes.c_void_p
+
+# name -> (restype, argtypes); mirrors include/qlinear.h
+SIGNATURES = {
+    "ql_version": (_c_int, []),
+    "ql_last_error": (ctypes.c_char_p, []),
+    "ql_gptq_dequant": (_c_int, [_vp, _vp, _vp, _c_int, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                 _c_float, _vp]),
+    "ql_gptq_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_int,
+                                _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
+    "ql_gptq_sort_rows": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+}
+
+
+class QLError(RuntimeError):
+    """A libqlinear call returned a non-zero status."""
+
+    def __init__(self, fn, code, msg):
+        super().__init__("%s failed (%s): %s" % (fn, _STATUS.get(code, code), msg))
+        self.code = code
+
+
+def lib_path():
+    return _build.LIB
+
+
+def load(build_if_missing=True):
+    """Load libqlinear.so, building it first if it is absent and nvcc is available."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = _build.LIB
+    if not os.path.exists(path):
+        if not build_if_missing:
+            raise RuntimeError("libqlinear.so is not built (run webpytorch_b200._build.build())")
+        _build.build()
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def call(name, *args):
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != 0:
+        msg = lib.ql_last_error()
+        raise QLError(name, rc, msg.decode(errors="replace") if msg else "")
+    return rc
+
+
+def dtype_code(t):
+    import torch
+    m = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+    if t not in m:
+        raise TypeError("unsupported dtype %s (float32, float16 or bfloat16)" % t)
+    return m[t]
+
+
+def ptr(t):
+    """Device address of a torch tensor, or None for None."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)

@@ -1,0 +1,607 @@
+// GPTQ int4/int8 quantized linear on B200: exact dequant, act-order row sort, and the
+// decode GEMV (small M) that streams packed weights at HBM speed.
+//
+// Reference semantics (webtorch/_core.py:4046-4072, _gptq_matmul_np):
+//   q[k, n]  = (qweight[k / per, n] >> (bits * (k % per))) & (2^bits - 1)
+//   z[g, n]  = (qzeros[g, n / per] >> (bits * (n % per))) & (2^bits - 1)
+//   W[k, n]  = scales[g, n] * (q[k, n] - (z[g, n] + zero_offset)),  g = k / gs
+//   y        = x @ W (+ bias)
+//
+// GEMV design (decode, M <= 16 per launch):
+//  * A warp owns a strip of 32 output columns. Lane (gq = lane/4, t = lane%4) streams one
+//    16-byte vector per step: 4 adjacent columns of packed row 4*step + t. A warp load is
+//    therefore 4 rows x 128 contiguous bytes, fully used.
+//  * Nibbles (or bytes) become fp16 integers with one LOP3 each (magic 0x6400 = 1024.0),
+//    and the zero point (z + zero_offset) is removed with one HSUB2/HFMA2, so q - z - off
+//    is exact in fp16.
+//  * The dot product and the 4-lane K reduction run on the tensor cores with register
+//    operands (mma.sync m16n8k16): the MMA's 16 rows are the lane-quads' columns, its 8
+//    columns are tokens. Register operands keep the dequantised weights out of shared
+//    memory, which a bandwidth-bound GEMV cannot afford to write and re-read.
+//  * Each group's partial sum is scaled in fp32 (acc += scale * partial), so the only
+//    roundings are the fp16 staging of x (power-of-two scaled per row, see below) and the
+//    fp32 accumulation.
+//  * Split-K runs across a thread-block cluster; partial sums are reduced through
+//    distributed shared memory in a fixed order (deterministic, no scratch, no atomics).
+//  * Activations are staged once per CTA into shared memory as fp16, each token row scaled
+//    by an exact power of two so its largest value sits in [2^14, 2^15); the scale is undone
+//    on the partial sums. The staging also applies the act-order gather x[:, perm[k]].
+#include <cooperative_groups.h>
+
+#include "ql_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace ql {
+namespace {
+
+// ---------------------------------------------------------------------------------------
+// exact dequant (test oracle partner and load-time helper)
+// ---------------------------------------------------------------------------------------
+__global__ void gptq_dequant_kernel(const uint32_t* __restrict__ qw, const uint32_t* __restrict__ qz,
+                                    const void* __restrict__ sc, int sc_dtype,
+                                    const int32_t* __restrict__ g_idx, float* __restrict__ W, int K,
+                                    int N, int gs, int bits, double zoff) {
+  const int per = 32 / bits;
+  const uint32_t mask = (1u << bits) - 1u;
+  const long total = (long)(K / per) * N;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total;
+       i += (long)gridDim.x * blockDim.x) {
+    const int n = (int)(i % N);
+    const int r = (int)(i / N);
+    const uint32_t w = qw[i];
+    for (int j = 0; j < per; ++j) {
+      const int k = r * per + j;
+      const int g = g_idx ? g_idx[k] : k / gs;
+      const uint32_t q = (w >> (bits * j)) & mask;
+      const uint32_t z = (qz[(long)g * (N / per) + n / per] >> (bits * (n % per))) & mask;
+      const double s = (double)load_as_float(sc, sc_dtype, (long)g * N + n);
+      // numpy: float32 scale * float64 (q - (z + zoff)), then one rounding to float32
+      W[(long)k * N + n] = __double2float_rn(s * ((double)q - ((double)z + zoff)));
+    }
+  }
+}
+
+__global__ void gptq_sort_rows_kernel(const uint32_t* __restrict__ qin, const int32_t* __restrict__ perm,
+                                      uint32_t* __restrict__ qout, int K, int N, int bits) {
+  const int per = 32 / bits;
+  const uint32_t mask = (1u << bits) - 1u;
+  const long total = (long)(K / per) * N;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total;
+       i += (long)gridDim.x * blockDim.x) {
+    const int n = (int)(i % N);
+    const int r = (int)(i / N);
+    uint32_t acc = 0;
+    for (int j = 0; j < per; ++j) {
+      const int src = perm[r * per + j];
+      const uint32_t q = (qin[(long)(src / per) * N + n] >> (bits * (src % per))) & mask;
+      acc |= q << (bits * j);
+    }
+    qout[i] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// decode GEMV
+// ---------------------------------------------------------------------------------------
+constexpr int kNW = 4;           // warps per CTA, one 32-column strip each
+constexpr int kCtaCols = kNW * 32;
+
+struct GemvArgs {
+  const void* x;
+  const int32_t* x_perm;
+  long ldx;
+  int x_dtype;
+  const uint32_t* qw;
+  const uint32_t* qz;
+  const void* sc;
+  int sc_dtype;
+  const float* bias;
+  void* out;
+  long ldo;
+  int out_dtype;
+  int M, K, N;
+  int G;        // number of GS-row kernel groups (K / GS)
+  int gs_mult;  // scale/zero row = kernel group / gs_mult (checkpoint group size = GS * gs_mult)
+  int cs;       // cluster size along K (== gridDim.x)
+  float zoff;
+};
+
+// Position of value j of a packed word inside the fp16 staging of x. The register unpack
+// pairs value j with value j + per/2 in one half2, so x is stored in the same pair order.
+template <int PER>
+__device__ __forceinline__ int stage_pos(int j) {
+  return (j % (PER / 2)) * 2 + j / (PER / 2);
+}
+
+// Stage x[:, kbase : kbase + klen] for M tokens into shared memory as power-of-two-scaled
+// fp16 in unpack order. Returns nothing; writes sh_exp[m] = e with x_staged = x * 2^-e.
+template <int PER>
+__device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int* sh_exp,
+                        unsigned* sh_max) {
+  const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
+  const int M = a.M;
+  const int nblk = klen / PER;
+  if (tid < 16) sh_max[tid] = 0u;
+  __syncthreads();
+  // pass 1: per-token absolute maximum over this CTA's slice
+  for (int m = 0; m < M; ++m) {
+    float mx = 0.f;
+    for (int kk = tid; kk < klen; kk += nthr) {
+      const int k = kbase + kk;
+      const int src = a.x_perm ? a.x_perm[k] : k;
+      mx = fmaxf(mx, fabsf(load_as_float(a.x, a.x_dtype, (long)m * a.ldx + src)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) atomicMax(&sh_max[m], __float_as_uint(mx));
+  }
+  __syncthreads();
+  if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
+  __syncthreads();
+  // pass 2: scale, convert and store one packed-word block (PER values) per iteration
+  for (int i = tid; i < M * nblk; i += nthr) {
+    const int m = i / nblk;
+    const int b = i % nblk;
+    const float s = exp2i(-sh_exp[m]);
+    __align__(16) __half v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int k = kbase + b * PER + j;
+      const int src = a.x_perm ? a.x_perm[k] : k;
+      v[stage_pos<PER>(j)] = __float2half_rn(load_as_float(a.x, a.x_dtype, (long)m * a.ldx + src) * s);
+    }
+    if constexpr (PER == 8) {
+      *reinterpret_cast<uint4*>(xs + (long)m * klen + b * PER) = *reinterpret_cast<uint4*>(v);
+    } else {
+      *reinterpret_cast<uint2*>(xs + (long)m * klen + b * PER) = *reinterpret_cast<uint2*>(v);
+    }
+  }
+  __syncthreads();
+}
+
+// Unpack one int4 word (8 values along K) into 4 half2 registers P[j] = (q_j, q_{j+4}) - zz.
+__device__ __forceinline__ void unpack_int4(uint32_t w, uint32_t zlo, uint32_t zhi, uint32_t (&P)[4]) {
+  const __half2 one16 = __floats2half2_rn(0.0625f, 0.0625f);
+  const uint32_t w8 = w >> 8;
+  const uint32_t v0 = lop3_andor(w, 0x000F000Fu, kMagicF16x2);   // 1024 + q0 | 1024 + q4
+  const uint32_t v1 = lop3_andor(w, 0x00F000F0u, kMagicF16x2);   // 1024 + 16 q1 | ... q5
+  const uint32_t v2 = lop3_andor(w8, 0x000F000Fu, kMagicF16x2);  // q2 | q6
+  const uint32_t v3 = lop3_andor(w8, 0x00F000F0u, kMagicF16x2);  // 16 q3 | 16 q7
+  // zlo = 1024 + z + off (both halves); zhi = -(64 + z + off)
+  P[0] = h2_as_u32(__hsub2(u32_as_h2(v0), u32_as_h2(zlo)));
+  P[1] = h2_as_u32(__hfma2(u32_as_h2(v1), one16, u32_as_h2(zhi)));
+  P[2] = h2_as_u32(__hsub2(u32_as_h2(v2), u32_as_h2(zlo)));
+  P[3] = h2_as_u32(__hfma2(u32_as_h2(v3), one16, u32_as_h2(zhi)));
+}
+
+// Unpack one int8 word (4 values along K) into P[0] = (q0, q2) - zz, P[1] = (q1, q3) - zz.
+__device__ __forceinline__ void unpack_int8(uint32_t w, uint32_t zlo, uint32_t (&P)[2]) {
+  const uint32_t v0 = lop3_andor(w, 0x00FF00FFu, kMagicF16x2);
+  const uint32_t v1 = lop3_andor(w >> 8, 0x00FF00FFu, kMagicF16x2);
+  P[0] = h2_as_u32(__hsub2(u32_as_h2(v0), u32_as_h2(zlo)));
+  P[1] = h2_as_u32(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)));
+}
+
+template <int BITS, int GS, int MT>
+__global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a) {
+  constexpr int PER = 32 / BITS;
+  constexpr int KSTEP = 4 * PER;              // K covered by one warp step (4 packed rows)
+  static_assert(GS % KSTEP == 0, "group size must be a multiple of 4 packed rows");
+  constexpr int SPG = GS / KSTEP;             // steps per group
+  constexpr int UG = SPG >= 8 ? 1 : 8 / SPG;  // groups whose loads are in flight together
+  constexpr int MAXM = 8 * MT;
+  constexpr uint32_t MASK = (1u << BITS) - 1u;
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int sh_exp[16];
+  __shared__ unsigned sh_max[16];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int gq = lane >> 2, t = lane & 3;
+  const int rank = blockIdx.x;  // position along K inside the cluster
+  const int g0 = (int)((long)a.G * rank / a.cs);
+  const int g1 = (int)((long)a.G * (rank + 1) / a.cs);
+  const int ng = g1 - g0;
+  const int kbase = g0 * GS;
+  const int klen = ng * GS;
+  const int M = a.M, N = a.N;
+
+  __half* xs = reinterpret_cast<__half*>(smem);
+  // the partial-sum buffer sits at the same offset in every CTA of the cluster (DSMEM maps
+  // a local address to the same offset in the peer), so size the x slice for the largest rank
+  const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
+  const int xs_bytes = ((M * klen_max * 2) + 15) & ~15;
+  float* red = reinterpret_cast<float*>(smem + xs_bytes);
+
+  stage_x<PER>(a, kbase, klen, xs, sh_exp, sh_max);
+
+  const int c0 = blockIdx.y * kCtaCols + warp * 32 + gq * 4;
+  const bool col_ok = c0 < N;
+  const long rows_per_group = GS / PER;
+
+  float acc[2][MT][4];
+#pragma unroll
+  for (int p = 0; p < 2; ++p)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[p][mt][i] = 0.f;
+
+  for (int gb = 0; gb < ng; gb += UG) {
+    uint4 wv[UG][SPG];
+    float scv[UG][4];
+    uint32_t zw[UG];
+    // ---- issue every load of UG groups before touching any of them
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+      const int grp = g0 + gb + u;
+      const bool ok = col_ok && (gb + u < ng);
+      const int srow = grp / a.gs_mult;
+#pragma unroll
+      for (int s = 0; s < SPG; ++s) {
+        const long r = (long)grp * rows_per_group + s * 4 + t;
+        wv[u][s] = ok ? ldg_stream_v4(a.qw + r * N + c0) : make_uint4(0, 0, 0, 0);
+      }
+      if (ok) {
+        if (a.sc_dtype == QL_F16) {
+          const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(a.sc) + (long)srow * N + c0);
+          const float2 f0 = __half22float2(u32_as_h2(h.x));
+          const float2 f1 = __half22float2(u32_as_h2(h.y));
+          scv[u][0] = f0.x; scv[u][1] = f0.y; scv[u][2] = f1.x; scv[u][3] = f1.y;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) scv[u][i] = load_as_float(a.sc, a.sc_dtype, (long)srow * N + c0 + i);
+        }
+        zw[u] = a.qz[(long)srow * (N / PER) + c0 / PER] >> (BITS * (c0 % PER));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) scv[u][i] = 0.f;
+        zw[u] = 0;
+      }
+    }
+    // ---- consume
+#pragma unroll
+    for (int u = 0; u < UG; ++u) {
+      if (gb + u >= ng) break;  // warp-uniform
+      uint32_t zlo[4], zhi[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float z = (float)((zw[u] >> (BITS * i)) & MASK) + a.zoff;
+        zlo[i] = h2_as_u32(__float2half2_rn(1024.f + z));
+        zhi[i] = h2_as_u32(__float2half2_rn(-(64.f + z)));
+      }
+      float gacc[2][MT][4];
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) gacc[p][mt][i] = 0.f;
+
+      const int kgrp = (gb + u) * GS;  // offset of this group inside the staged slice
+#pragma unroll
+      for (int s = 0; s < SPG; ++s) {
+        const int koff = kgrp + (s * 4 + t) * PER;
+        const uint32_t wcol[4] = {wv[u][s].x, wv[u][s].y, wv[u][s].z, wv[u][s].w};
+        if constexpr (BITS == 4) {
+          uint32_t P[4][4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) unpack_int4(wcol[i], zlo[i], zhi[i], P[i]);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int tok = gq + 8 * mt;
+            uint4 xv = make_uint4(0, 0, 0, 0);
+            if (tok < M) xv = *reinterpret_cast<const uint4*>(xs + (long)tok * klen + koff);
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
+              mma_16816_f16(gacc[p][mt], P[2 * p][2], P[2 * p + 1][2], P[2 * p][3], P[2 * p + 1][3], xv.z, xv.w);
+            }
+          }
+        } else {
+          uint32_t P[4][2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) unpack_int8(wcol[i], zlo[i], P[i]);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int tok = gq + 8 * mt;
+            uint2 xv = make_uint2(0, 0);
+            if (tok < M) xv = *reinterpret_cast<const uint2*>(xs + (long)tok * klen + koff);
+#pragma unroll
+            for (int p = 0; p < 2; ++p)
+              mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
+          }
+        }
+      }
+      // C fragment: [0],[1] -> column c0+2p, tokens 2t, 2t+1; [2],[3] -> column c0+2p+1
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          acc[p][mt][0] = fmaf(scv[u][2 * p], gacc[p][mt][0], acc[p][mt][0]);
+          acc[p][mt][1] = fmaf(scv[u][2 * p], gacc[p][mt][1], acc[p][mt][1]);
+          acc[p][mt][2] = fmaf(scv[u][2 * p + 1], gacc[p][mt][2], acc[p][mt][2]);
+          acc[p][mt][3] = fmaf(scv[u][2 * p + 1], gacc[p][mt][3], acc[p][mt][3]);
+        }
+    }
+  }
+
+  // ---- epilogue: undo the activation scale, then write (single CTA) or reduce (cluster)
+  if (a.cs == 1) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tok = 8 * mt + 2 * t + (i & 1);
+          const int col = c0 + 2 * p + (i >> 1);
+          if (tok < M && col_ok) {
+            float v = acc[p][mt][i] * exp2i(sh_exp[tok]);
+            if (a.bias) v += a.bias[col];
+            store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
+          }
+        }
+    return;
+  }
+
+#pragma unroll
+  for (int p = 0; p < 2; ++p)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = 8 * mt + 2 * t + (i & 1);
+        const int lcol = warp * 32 + gq * 4 + 2 * p + (i >> 1);
+        if (tok < M) red[lcol * MAXM + tok] = acc[p][mt][i] * exp2i(sh_exp[tok]);
+      }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const int total = kCtaCols * M;
+  const int lo = (int)((long)total * rank / a.cs), hi = (int)((long)total * (rank + 1) / a.cs);
+  for (int idx = lo + tid; idx < hi; idx += blockDim.x) {
+    const int lcol = idx / M, tok = idx % M;
+    const int col = blockIdx.y * kCtaCols + lcol;
+    float v = 0.f;
+    for (int q = 0; q < a.cs; ++q) {
+      const float* rr = cluster.map_shared_rank(red, q);
+      v += rr[lcol * MAXM + tok];
+    }
+    if (col < N) {
+      if (a.bias) v += a.bias[col];
+      store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
+    }
+  }
+  cluster.sync();  // keep this CTA's partials alive until every rank has read them
+}
+
+template <int BITS, int GS, int MT>
+int launch_gemv(const GemvArgs& a, cudaStream_t st) {
+  auto kern = gptq_gemv_kernel<BITS, GS, MT>;
+  const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
+  const size_t xs_bytes = ((size_t)a.M * klen_max * 2 + 15) & ~(size_t)15;
+  const size_t smem = xs_bytes + (size_t)kCtaCols * 8 * MT * sizeof(float);
+  if (smem > 200 * 1024) {
+    set_error("ql_gptq_matmul: activation slice needs %zu bytes of shared memory (M=%d, K=%d)", smem, a.M, a.K);
+    return QL_ERR_UNSUPPORTED;
+  }
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+                         "cudaFuncSetAttribute(smem)");
+    if (rc) return rc;
+    rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
+                     "cudaFuncSetAttribute(cluster)");
+    if (rc) return rc;
+    configured_dev = dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.cs, (a.N + kCtaCols - 1) / kCtaCols, 1);
+  cfg.blockDim = dim3(kNW * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, a), "gptq_gemv launch");
+}
+
+template <int BITS, int GS>
+int dispatch_mt(const GemvArgs& a, cudaStream_t st) {
+  return a.M <= 8 ? launch_gemv<BITS, GS, 1>(a, st) : launch_gemv<BITS, GS, 2>(a, st);
+}
+
+template <int BITS>
+int dispatch_gs(const GemvArgs& a, int kgs, cudaStream_t st) {
+  switch (kgs) {
+    case 32: return dispatch_mt<BITS, 32>(a, st);
+    case 64: return dispatch_mt<BITS, 64>(a, st);
+    default: return dispatch_mt<BITS, 128>(a, st);
+  }
+}
+
+inline int pow2_floor(int v) {
+  int p = 1;
+  while (p * 2 <= v) p *= 2;
+  return p;
+}
+
+}  // namespace
+
+// Picks the K split (cluster size) so the grid holds ~16 warps per SM, then launches.
+int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+              const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
+              int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st) {
+  // kernel group: the largest of {128, 64, 32} dividing the checkpoint's group size
+  int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
+  if (bits == 8 && kgs < 16) kgs = 16;
+  GemvArgs a;
+  a.x = x; a.x_perm = x_perm; a.ldx = ldx; a.x_dtype = x_dtype;
+  a.qw = reinterpret_cast<const uint32_t*>(qweight);
+  a.qz = reinterpret_cast<const uint32_t*>(qzeros);
+  a.sc = scales; a.sc_dtype = sc_dtype; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
+  a.M = M; a.K = K; a.N = N;
+  a.G = K / kgs;
+  a.gs_mult = gs / kgs;
+  a.zoff = zoff;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int cta_cols = (N + kCtaCols - 1) / kCtaCols;
+  const int target = sms * 4;  // 4 CTAs x 4 warps per SM
+  int cs = pow2_floor(target / cta_cols > 0 ? target / cta_cols : 1);
+  if (cs > 16) cs = 16;
+  while (cs > 1 && cs > a.G) cs /= 2;
+  // keep the staged activation slice within shared memory
+  while (cs < 16 && cs < a.G && (size_t)M * ((a.G + cs - 1) / cs) * kgs * 2 > 96 * 1024) cs *= 2;
+  a.cs = cs;
+  return bits == 4 ? dispatch_gs<4>(a, kgs, st) : dispatch_gs<8>(a, kgs, st);
+}
+
+}  // namespace ql
+
+// =======================================================================================
+// C ABI
+// =======================================================================================
+using namespace ql;
+
+static int check_dtype(int d, const char* what) {
+  if (d == QL_F32 || d == QL_F16 || d == QL_BF16) return QL_OK;
+  set_error("%s: unknown dtype code %d", what, d);
+  return QL_ERR_ARG;
+}
+
+static int check_gptq_dims(const char* fn, int K, int N, int gs, int bits) {
+  if (bits != 4 && bits != 8) {
+    set_error("%s: bits must be 4 or 8 (got %d)", fn, bits);
+    return QL_ERR_UNSUPPORTED;
+  }
+  const int per = 32 / bits;
+  if (K <= 0 || N <= 0 || gs <= 0) {
+    set_error("%s: K, N and gs must be positive (K=%d N=%d gs=%d)", fn, K, N, gs);
+    return QL_ERR_ARG;
+  }
+  if (K % gs != 0 || K % per != 0 || N % per != 0) {
+    set_error("%s: dims must divide group/pack size (K=%d N=%d gs=%d bits=%d)", fn, K, N, gs, bits);
+    return QL_ERR_ARG;
+  }
+  return QL_OK;
+}
+
+extern "C" int ql_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                               int scales_dtype, const int32_t* g_idx, float* W, int K, int N, int gs,
+                               int bits, float zero_offset, void* stream) {
+  int rc = check_gptq_dims("ql_gptq_dequant", K, N, gs, bits);
+  if (rc) return rc;
+  if ((rc = check_dtype(scales_dtype, "ql_gptq_dequant(scales)"))) return rc;
+  if (!qweight || !qzeros || !scales || !W) {
+    set_error("ql_gptq_dequant: null pointer");
+    return QL_ERR_ARG;
+  }
+  const long total = (long)(K / (32 / bits)) * N;
+  const int threads = 256;
+  const long blocks = (total + threads - 1) / threads;
+  gptq_dequant_kernel<<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), threads, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint32_t*>(qweight), reinterpret_cast<const uint32_t*>(qzeros), scales,
+      scales_dtype, g_idx, W, K, N, gs, bits, (double)zero_offset);
+  return cuda_status(cudaGetLastError(), "ql_gptq_dequant launch");
+}
+
+extern "C" int ql_gptq_sort_rows(const int32_t* qweight_in, const int32_t* perm, int32_t* qweight_out,
+                                 int K, int N, int bits, void* stream) {
+  if (bits != 4 && bits != 8) {
+    set_error("ql_gptq_sort_rows: bits must be 4 or 8 (got %d)", bits);
+    return QL_ERR_UNSUPPORTED;
+  }
+  if (!qweight_in || !perm || !qweight_out || K <= 0 || N <= 0 || K % (32 / bits)) {
+    set_error("ql_gptq_sort_rows: bad arguments (K=%d N=%d bits=%d)", K, N, bits);
+    return QL_ERR_ARG;
+  }
+  if (qweight_in == qweight_out) {
+    set_error("ql_gptq_sort_rows: input and output must not alias");
+    return QL_ERR_ARG;
+  }
+  const long total = (long)(K / (32 / bits)) * N;
+  const int threads = 256;
+  const long blocks = (total + threads - 1) / threads;
+  gptq_sort_rows_kernel<<<(unsigned)(blocks < 148 * 32 ? blocks : 148 * 32), threads, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint32_t*>(qweight_in), perm, reinterpret_cast<uint32_t*>(qweight_out), K, N, bits);
+  return cuda_status(cudaGetLastError(), "ql_gptq_sort_rows launch");
+}
+
+namespace ql {
+int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
+                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff,
+                    cudaStream_t st, bool* handled);
+}
+
+extern "C" int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                              const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                              int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
+                              int M, int K, int N, int gs, int bits, float zero_offset, void* stream) {
+  int rc = check_gptq_dims("ql_gptq_matmul", K, N, gs, bits);
+  if (rc) return rc;
+  if ((rc = check_dtype(x_dtype, "ql_gptq_matmul(x)"))) return rc;
+  if ((rc = check_dtype(scales_dtype, "ql_gptq_matmul(scales)"))) return rc;
+  if ((rc = check_dtype(out_dtype, "ql_gptq_matmul(out)"))) return rc;
+  if (M < 0) {
+    set_error("ql_gptq_matmul: M must be >= 0 (got %d)", M);
+    return QL_ERR_ARG;
+  }
+  if (M == 0) return QL_OK;
+  if (!x || !qweight || !qzeros || !scales || !out) {
+    set_error("ql_gptq_matmul: null pointer");
+    return QL_ERR_ARG;
+  }
+  if (ldx < K || ldo < N) {
+    set_error("ql_gptq_matmul: row strides too small (ldx=%ld K=%d ldo=%ld N=%d)", ldx, K, ldo, N);
+    return QL_ERR_ARG;
+  }
+  if (gs % 32 != 0) {
+    set_error("ql_gptq_matmul: group size %d is not a multiple of 32", gs);
+    return QL_ERR_UNSUPPORTED;
+  }
+  if (N % 8 != 0) {
+    set_error("ql_gptq_matmul: N=%d must be a multiple of 8", N);
+    return QL_ERR_UNSUPPORTED;
+  }
+  if (!(zero_offset == 0.f || zero_offset == 1.f)) {
+    set_error("ql_gptq_matmul: zero_offset must be 0 or 1 (got %g)", (double)zero_offset);
+    return QL_ERR_UNSUPPORTED;
+  }
+  if ((reinterpret_cast<uintptr_t>(qweight) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(scales) & 15) != 0) {
+    set_error("ql_gptq_matmul: qweight and scales must be 16-byte aligned");
+    return QL_ERR_ALIGN;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  bool handled = false;
+  rc = gptq_gemm_sm100(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype,
+                       ldo, M, K, N, gs, bits, zero_offset, st, &handled);
+  if (handled || rc) return rc;
+  // decode path: chunks of up to 16 tokens per launch
+  for (int m0 = 0; m0 < M; m0 += 16) {
+    const int mc = (M - m0) < 16 ? (M - m0) : 16;
+    const char* xb = reinterpret_cast<const char*>(x) + (long)m0 * ldx * (x_dtype == QL_F32 ? 4 : 2);
+    char* ob = reinterpret_cast<char*>(out) + (long)m0 * ldo * (out_dtype == QL_F32 ? 4 : 2);
+    rc = gptq_gemv(xb, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, ob, out_dtype, ldo,
+                   mc, K, N, gs, bits, zero_offset, st);
+    if (rc) return rc;
+  }
+  return QL_OK;
+}
