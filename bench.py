@@ -228,16 +228,26 @@ def main():
         for L in lay:
             launch(L)
 
-    # ---- capture one step into a CUDA graph (launch-bound otherwise), warm up first
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    torch.cuda.synchronize()
+    # ---- capture one step into a CUDA graph (launch-bound otherwise), warm up first.
+    # Headline graph uses programmatic dependent launch (each GEMV streams its weights while
+    # the previous one finishes); the plain-launch graph is timed too, for comparison.
+    def capture(pdl):
+        _ffi.set_launch_flags(_ffi.LAUNCH_PDL if pdl else 0)
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            step()
+        torch.cuda.synchronize()
+        _ffi.set_launch_flags(0)
+        return gr
+
+    graph = capture(pdl=True)
+    graph_plain = capture(pdl=False)
     for _ in range(args.warmup):
         graph.replay()
+        graph_plain.replay()
     torch.cuda.synchronize()
 
     def timed(fn, n):
@@ -266,21 +276,35 @@ def main():
         time.sleep(0.15)
         ms, t0, t1 = timed(graph.replay, args.steps)
         clocks = sampler.summary(t0, t1)
+    ms_plain, _, _ = timed(graph_plain.replay, args.steps)
 
-    # ---- per-shape launch durations (CUDA events around each launch, separate pass)
+    # ---- per-shape launch durations: a graph of 40 launches per shape (10 passes over the
+    # 4 copies, so each launch still reads its weights from HBM), timed with CUDA events
     per_shape = {}
     for (K, N) in SHAPES:
         Ls = [L for L in lay if (L[0], L[1]) == (K, N)]
-        reps = 50
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        e0.record()
-        for i in range(reps):
-            launch(Ls[i % len(Ls)])
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / reps
-        per_shape["%dx%d" % (K, N)] = {"us": round(us, 3), "GB/s": round(gemv_bytes(K, N) / us / 1e3, 1)}
+        res = {}
+        for pdl in (False, True):
+            _ffi.set_launch_flags(_ffi.LAUNCH_PDL if pdl else 0)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for i in range(40):
+                    launch(Ls[i % len(Ls)])
+            _ffi.set_launch_flags(0)
+            gr.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / 400
+            res["pdl" if pdl else "plain"] = us
+            del gr
+        per_shape["%dx%d" % (K, N)] = {"us": round(res["pdl"], 3), "us_plain": round(res["plain"], 3),
+                                       "GB/s": round(gemv_bytes(K, N) / res["pdl"] / 1e3, 1),
+                                       "GB/s_plain": round(gemv_bytes(K, N) / res["plain"] / 1e3, 1)}
 
     # ---- e2e: public operator path with pinned host buffers, copies inside the timed region
     hx = [torch.empty(L[5].shape, dtype=L[5].dtype, pin_memory=True).copy_(L[5].cpu()) for L in lay]
@@ -301,6 +325,7 @@ def main():
 
     tot_bytes = step_bytes() * args.steps * world
     value = tot_bytes / (ms / 1e3) / 1e9
+    value_plain = tot_bytes / (ms_plain / 1e3) / 1e9
     e2e_value = step_bytes() * e2e_steps * world / (ems / 1e3) / 1e9
     hbm, _, src = peaks()
     launches_per_step = len(lay)
@@ -314,11 +339,13 @@ def main():
         "config": {"workload": "config1: int4 g128 GEMV M=1 over (K,N) in %s, %d weight copies per step "
                                "(%.0f MB/step > 2x L2, no L2 flush needed)" % (SHAPES, COPIES, step_bytes() / 1e6),
                    "bits": 4, "group_size": GS, "M": 1, "parallelism": "replicas x%d" % world,
-                   "l2": "inputs larger than L2 (rotating copies)", "cuda_graph": True},
+                   "l2": "inputs larger than L2 (rotating copies)", "cuda_graph": True,
+                   "launch": "programmatic dependent launch (QL_LAUNCH_PDL)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None,
                      "peak_source": "%s (MEASURED_PEAKS.json hbm_gbs)" % src if src == "measured" else src,
                      "avg_launch_us": round(avg_launch_us, 3)},
+        "value_without_pdl": round(value_plain, 2),
         "per_shape": per_shape,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
@@ -330,7 +357,7 @@ def main():
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if rank == 0:
         print(json.dumps(result), flush=True)
-    del graph
+    del graph, graph_plain
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -38,11 +38,24 @@ enum {
   QL_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up                           */
 };
 
+/* launch flags (bit set) for ql_set_launch_flags */
+enum {
+  /* Launch kernels as programmatic dependents of the previous kernel in the stream, so a
+     GEMV streams its weights while the previous kernel is still finishing. Activations and
+     outputs stay ordered; the previous kernel must not write this call's WEIGHTS. */
+  QL_LAUNCH_PDL = 1
+};
+
 /* Library version as major*10000 + minor*100 + patch. */
 QL_API int ql_version(void);
 
 /* Message describing the last failure on the calling thread ("" if none). */
 QL_API const char* ql_last_error(void);
+
+/* Process-wide launch flags (QL_LAUNCH_*); returns the previous value. Default 0.
+ * No counterpart in the reference (its WebGPU runtime batches dispatches itself,
+ * src/webgpu/webgpuContext.ts:35,141-201). */
+QL_API int ql_set_launch_flags(int flags);
 
 /*
  * Exact GPTQ dequantisation to fp32, W[k, n] = scales[g, n] * (q[k, n] - (z[g, n] + zero_offset))
@@ -88,6 +101,24 @@ QL_API int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x
  */
 QL_API int ql_gptq_sort_rows(const int32_t* qweight_in, const int32_t* perm, int32_t* qweight_out,
                       int K, int N, int bits, void* stream);
+
+/*
+ * Exact fp32 dequantisation of a GGUF Q4_K weight: W[n, k] for the [N, K] tensor stored as
+ * N rows of K/256 super-blocks of 144 bytes (f16 d | f16 dmin | scales[12] | qs[128]).
+ * value = (d*sc_j) * q - dmin*m_j with the products and the difference rounded like numpy.
+ * Replaces: webtorch/ggufload.py:116-131,190-202 (dequant, Q4_K branch).
+ */
+QL_API int ql_q4k_dequant(const uint8_t* raw, float* W, int N, int K, void* stream);
+
+/*
+ * y[M, N] = x[M, K] @ W[N, K]^T (+ bias) with W decoded from the raw Q4_K bytes inside the
+ * kernel (no load-time re-layout). x of x_dtype with row stride ldx; out of out_dtype with
+ * row stride ldo; bias NULL or fp32 [N]. raw must be 16-byte aligned; K % 256 == 0.
+ * Replaces: webtorch/_core.py:3720-3734 (ggml_matmul) with the Q4_K decode of
+ *           _core.py:3061-3068,3116-3133, called from GGMLLinear.forward _core.py:4399-4406.
+ */
+QL_API int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias,
+                         void* out, int out_dtype, long ldo, int M, int K, int N, void* stream);
 
 #ifdef __cplusplus
 }

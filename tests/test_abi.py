@@ -74,3 +74,17 @@ def test_other_entry_points_reject_bad_arguments(lib):
     assert lib.ql_gptq_sort_rows(v(16), v(16), v(16), 128, 64, 6, None) == 3
     assert lib.ql_gptq_sort_rows(v(16), v(16), v(16), 127, 64, 4, None) == 1
     assert lib.ql_gptq_sort_rows(v(16), v(16), v(16), 128, 64, 4, None) == 1  # aliasing
+
+
+def test_q4k_entry_points_reject_bad_arguments(lib):
+    v = ctypes.c_void_p
+    assert lib.ql_q4k_dequant(v(16), v(16), 4, 100, None) == 1                 # K % 256
+    assert lib.ql_q4k_matmul(v(16), 5, 256, v(16), None, v(16), 0, 4, 1, 256, 4, None) == 1    # dtype
+    assert lib.ql_q4k_matmul(v(16), 0, 256, v(8), None, v(16), 0, 4, 1, 256, 4, None) == 2     # raw align
+    assert lib.ql_q4k_matmul(v(16), 0, 256, v(16), None, v(16), 0, 4, 0, 256, 4, None) == 0    # M == 0
+    assert lib.ql_q4k_matmul(v(16), 0, 100, v(16), None, v(16), 0, 4, 1, 256, 4, None) == 1    # ldx < K
+
+
+def test_launch_flags_roundtrip(lib):
+    old = lib.ql_set_launch_flags(1)
+    assert lib.ql_set_launch_flags(old) == 1

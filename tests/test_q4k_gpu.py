@@ -1,0 +1,78 @@
+"""GGUF Q4_K on the GPU against the reference's dequantiser outputs (golden) and the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, max_rel_err
+from oracle import q4k as oq
+from webpytorch_b200 import synth
+from webpytorch_b200.ggml import GGMLLinear, ggml_matmul, q4k_dequant
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+DEV = "cuda"
+
+
+def _raw(a):
+    return torch.from_numpy(np.ascontiguousarray(a).reshape(-1).view(np.uint8)).to(DEV)
+
+
+@pytest.mark.parametrize("name", ["q4k_randombytes.npz", "q4k_synth.npz"])
+def test_dequant_bitexact_vs_reference(name):
+    d = golden(name)
+    N, K = int(d["N"]), int(d["K"])
+    W = q4k_dequant(_raw(d["raw"]), K, N).cpu().numpy()
+    assert np.array_equal(W.view(np.uint32), d["W"].view(np.uint32))
+
+
+def test_matmul_vs_reference_randombytes():
+    d = golden("q4k_randombytes.npz")
+    lin = GGMLLinear(d["raw"].tobytes(), "Q4_K", int(d["K"]), int(d["N"]))
+    y = lin(torch.from_numpy(d["x"]).to(DEV)).cpu().numpy()
+    assert max_rel_err(y, d["y"]) < TOL
+
+
+@pytest.mark.parametrize("M", [1, 8, 13])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.float16, torch.bfloat16])
+def test_matmul_vs_reference_synth(M, xdt):
+    d = golden("q4k_synth.npz")
+    N, K = int(d["N"]), int(d["K"])
+    lin = GGMLLinear(d["raw"], "Q4_K", K, N)
+    x = torch.from_numpy(d["x_%d" % M]).to(DEV).to(xdt)
+    y = lin(x).cpu().numpy()
+    ref = d["y_%d" % M] if xdt == torch.float32 else oq.matmul(x.float().cpu().numpy(), d["raw"].tobytes(), K, N)
+    assert max_rel_err(y, ref) < TOL
+
+
+@pytest.mark.parametrize("M", [1, 8, 16, 17, 64])
+def test_config2_full_size(M):
+    """Config 2 shape (K=4096, N=14336) against the exact dequant (bit-exact above) in fp64."""
+    N, K = 14336, 4096
+    raw = synth.q4k_weights(N, K, seed=M)
+    rd = _raw(raw)
+    W = q4k_dequant(rd, K, N).double()
+    x = torch.randn((M, K), device=DEV, generator=torch.Generator(device=DEV).manual_seed(M))
+    y = ggml_matmul(x, rd, "Q4_K", K, N)
+    ref = x.double() @ W.T
+    assert max_rel_err(y.cpu().numpy(), ref.cpu().numpy()) < TOL
+    # a slab of the exact dequant against the oracle at full size
+    ref_w = oq.dequant(raw[:64].tobytes(), 64 * K).reshape(64, K)
+    assert np.array_equal(W[:64].float().cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
+
+
+def test_bias_ragged_rows_and_host_io():
+    rng = np.random.default_rng(3)
+    N, K = 37, 768                     # N not a multiple of the 16-row warp tile
+    raw = synth.q4k_weights(N, K, rng=rng)
+    bias = rng.standard_normal(N).astype(np.float32)
+    lin = GGMLLinear(raw.tobytes(), "Q4_K", K, N, bias=bias)
+    x = rng.standard_normal((2, 3, K)).astype(np.float32)
+    y = lin(torch.from_numpy(x))
+    assert y.device.type == "cpu" and tuple(y.shape) == (2, 3, N)
+    ref = oq.matmul(x.reshape(-1, K), raw.tobytes(), K, N, bias).reshape(2, 3, N)
+    assert max_rel_err(y.numpy(), ref) < TOL
+
+
+def test_unsupported_type_raises():
+    with pytest.raises(NotImplementedError):
+        GGMLLinear(b"\x00" * 34, "Q8_0", 32, 1)

@@ -16,7 +16,7 @@ LIB = os.path.join(LIBDIR, "libqlinear.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--use_fast_math", "-Xcompiler", "-fPIC,-O2",
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O2",
          "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr"]
 
 

@@ -25,7 +25,17 @@ SIGNATURES = {
     "ql_gptq_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_int,
                                 _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
     "ql_gptq_sort_rows": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "ql_set_launch_flags": (_c_int, [_c_int]),
+    "ql_q4k_dequant": (_c_int, [_vp, _vp, _c_int, _c_int, _vp]),
+    "ql_q4k_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp]),
 }
+
+LAUNCH_PDL = 1
+
+
+def set_launch_flags(flags):
+    """Process-wide launch flags (LAUNCH_PDL); returns the previous value."""
+    return load().ql_set_launch_flags(int(flags))
 
 
 class QLError(RuntimeError):

@@ -92,6 +92,7 @@ struct GemvArgs {
   const int32_t* x_perm;
   long ldx;
   int x_dtype;
+  int x_vec;    // x rows may be read with 16-byte vector loads
   const uint32_t* qw;
   const uint32_t* qz;
   const void* sc;
@@ -113,49 +114,114 @@ template <int PER>
 __device__ __forceinline__ int stage_pos(int j) {
   return (j % (PER / 2)) * 2 + j / (PER / 2);
 }
+// the same inside an 8-value chunk (one int4 word, or two int8 words)
+template <int PER>
+__device__ __forceinline__ int chunk_pos(int j) {
+  return (j / PER) * PER + stage_pos<PER>(j % PER);
+}
+
+// 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats.
+__device__ __forceinline__ void load_x8(const GemvArgs& a, int m, int k, float (&v)[8]) {
+  const long base = (long)m * a.ldx;
+  if (a.x_perm == nullptr && a.x_vec) {
+    if (a.x_dtype == QL_F16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(a.x) + base + k);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(u32_as_h2(w[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else if (a.x_dtype == QL_BF16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) + base + k);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else {
+      const float4 f0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + base + k);
+      const float4 f1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + base + k + 4);
+      v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+      v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int src = a.x_perm ? a.x_perm[k + j] : k + j;
+      v[j] = load_as_float(a.x, a.x_dtype, base + src);
+    }
+  }
+}
 
 // Stage x[:, kbase : kbase + klen] for M tokens into shared memory as power-of-two-scaled
-// fp16 in unpack order. Returns nothing; writes sh_exp[m] = e with x_staged = x * 2^-e.
+// fp16 in unpack order; sh_exp[m] = e with x_staged = x * 2^-e. sh_max must be zero and
+// visible (a __syncthreads after zeroing) before the call.
 template <int PER>
-__device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int* sh_exp,
-                        unsigned* sh_max) {
-  const int tid = threadIdx.x;
-  const int nthr = blockDim.x;
-  const int M = a.M;
-  const int nblk = klen / PER;
-  if (tid < 16) sh_max[tid] = 0u;
-  __syncthreads();
-  // pass 1: per-token absolute maximum over this CTA's slice
-  for (int m = 0; m < M; ++m) {
-    float mx = 0.f;
-    for (int kk = tid; kk < klen; kk += nthr) {
-      const int k = kbase + kk;
-      const int src = a.x_perm ? a.x_perm[k] : k;
-      mx = fmaxf(mx, fabsf(load_as_float(a.x, a.x_dtype, (long)m * a.ldx + src)));
+__device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int* sh_exp, unsigned* sh_max) {
+  constexpr int CH = 4;  // 8-value chunks a thread keeps in registers on the one-pass path
+  const int tid = threadIdx.x, nthr = blockDim.x, M = a.M;
+  const int cpr = klen / 8;
+  const int nchunk = M * cpr;
+  if (nchunk <= nthr * CH) {
+    float v[CH][8];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (idx < nchunk) {
+        const int m = idx / cpr;
+        load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
+      }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((tid & 31) == 0) atomicMax(&sh_max[m], __float_as_uint(mx));
-  }
-  __syncthreads();
-  if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
-  __syncthreads();
-  // pass 2: scale, convert and store one packed-word block (PER values) per iteration
-  for (int i = tid; i < M * nblk; i += nthr) {
-    const int m = i / nblk;
-    const int b = i % nblk;
-    const float s = exp2i(-sh_exp[m]);
-    __align__(16) __half v[PER];
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (idx < nchunk) {
+        float mx = 0.f;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      const int k = kbase + b * PER + j;
-      const int src = a.x_perm ? a.x_perm[k] : k;
-      v[stage_pos<PER>(j)] = __float2half_rn(load_as_float(a.x, a.x_dtype, (long)m * a.ldx + src) * s);
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+        atomicMax(&sh_max[idx / cpr], __float_as_uint(mx));
+      }
     }
-    if constexpr (PER == 8) {
-      *reinterpret_cast<uint4*>(xs + (long)m * klen + b * PER) = *reinterpret_cast<uint4*>(v);
-    } else {
-      *reinterpret_cast<uint2*>(xs + (long)m * klen + b * PER) = *reinterpret_cast<uint2*>(v);
+    __syncthreads();
+    if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (idx < nchunk) {
+        const int m = idx / cpr, kc = idx - m * cpr;
+        const float s = exp2i(-sh_exp[m]);
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[chunk_pos<PER>(j)] = __float2half_rn(v[c][j] * s);
+        *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
+      }
+    }
+  } else {
+    for (int idx = tid; idx < nchunk; idx += nthr) {
+      const int m = idx / cpr;
+      float v[8];
+      load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
+      float mx = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+      atomicMax(&sh_max[m], __float_as_uint(mx));
+    }
+    __syncthreads();
+    if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
+    __syncthreads();
+    for (int idx = tid; idx < nchunk; idx += nthr) {
+      const int m = idx / cpr, kc = idx - m * cpr;
+      float v[8];
+      load_x8(a, m, kbase + kc * 8, v);
+      const float s = exp2i(-sh_exp[m]);
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[chunk_pos<PER>(j)] = __float2half_rn(v[j] * s);
+      *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
     }
   }
   __syncthreads();
@@ -184,15 +250,128 @@ __device__ __forceinline__ void unpack_int8(uint32_t w, uint32_t zlo, uint32_t (
   P[1] = h2_as_u32(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)));
 }
 
+// Register-resident batch of UG consecutive groups of one lane's weights, scales and zeros.
+template <int BITS, int GS>
+struct WBatch {
+  static constexpr int PER = 32 / BITS;
+  static constexpr int SPG = GS / (4 * PER);           // 16-byte loads per lane per group
+  static constexpr int UG = SPG >= 4 ? 1 : 4 / SPG;   // groups per batch (>= 4 loads in flight)
+  uint4 w[UG][SPG];
+  float sc[UG][4];
+  uint32_t z[UG];
+};
+
+template <int BITS, int GS>
+__device__ __forceinline__ void load_batch(WBatch<BITS, GS>& B, const GemvArgs& a, int grp0, int gend, int c0,
+                                           bool col_ok, int t) {
+  using W = WBatch<BITS, GS>;
+  const int N = a.N;
+#pragma unroll
+  for (int u = 0; u < W::UG; ++u) {
+    const int grp = grp0 + u;
+    const bool ok = col_ok && grp < gend;
+    const int srow = grp / a.gs_mult;
+#pragma unroll
+    for (int s = 0; s < W::SPG; ++s) {
+      const long r = (long)grp * (GS / W::PER) + s * 4 + t;
+      B.w[u][s] = ok ? ldg_stream_v4(a.qw + r * N + c0) : make_uint4(0, 0, 0, 0);
+    }
+    if (ok) {
+      if (a.sc_dtype == QL_F16) {
+        const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(a.sc) + (long)srow * N + c0);
+        const float2 f0 = __half22float2(u32_as_h2(h.x));
+        const float2 f1 = __half22float2(u32_as_h2(h.y));
+        B.sc[u][0] = f0.x; B.sc[u][1] = f0.y; B.sc[u][2] = f1.x; B.sc[u][3] = f1.y;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) B.sc[u][i] = load_as_float(a.sc, a.sc_dtype, (long)srow * N + c0 + i);
+      }
+      B.z[u] = a.qz[(long)srow * (N / W::PER) + c0 / W::PER] >> (BITS * (c0 % W::PER));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) B.sc[u][i] = 0.f;
+      B.z[u] = 0;
+    }
+  }
+}
+
+// Multiply-accumulate one batch; kgrp0 = offset of its first group inside the staged slice.
+template <int BITS, int GS, int MT>
+__device__ __forceinline__ void compute_batch(const WBatch<BITS, GS>& B, float (&acc)[2][MT][4], const __half* xs,
+                                              int klen, int kgrp0, int nvalid, int gq, int t, int M, float zoff) {
+  using W = WBatch<BITS, GS>;
+  constexpr uint32_t MASK = (1u << BITS) - 1u;
+#pragma unroll
+  for (int u = 0; u < W::UG; ++u) {
+    if (u >= nvalid) break;  // warp-uniform
+    uint32_t zlo[4], zhi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float z = (float)((B.z[u] >> (BITS * i)) & MASK) + zoff;
+      zlo[i] = h2_as_u32(__float2half2_rn(1024.f + z));
+      zhi[i] = h2_as_u32(__float2half2_rn(-(64.f + z)));
+    }
+    float gacc[2][MT][4];
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) gacc[p][mt][i] = 0.f;
+    const int kgrp = kgrp0 + u * GS;
+#pragma unroll
+    for (int s = 0; s < W::SPG; ++s) {
+      const int koff = kgrp + (s * 4 + t) * W::PER;
+      const uint32_t wcol[4] = {B.w[u][s].x, B.w[u][s].y, B.w[u][s].z, B.w[u][s].w};
+      if constexpr (BITS == 4) {
+        uint32_t P[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) unpack_int4(wcol[i], zlo[i], zhi[i], P[i]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const int tok = gq + 8 * mt;
+          uint4 xv = make_uint4(0, 0, 0, 0);
+          if (tok < M) xv = *reinterpret_cast<const uint4*>(xs + (long)tok * klen + koff);
+#pragma unroll
+          for (int p = 0; p < 2; ++p) {
+            mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
+            mma_16816_f16(gacc[p][mt], P[2 * p][2], P[2 * p + 1][2], P[2 * p][3], P[2 * p + 1][3], xv.z, xv.w);
+          }
+        }
+      } else {
+        uint32_t P[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) unpack_int8(wcol[i], zlo[i], P[i]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const int tok = gq + 8 * mt;
+          uint2 xv = make_uint2(0, 0);
+          if (tok < M) xv = *reinterpret_cast<const uint2*>(xs + (long)tok * klen + koff);
+#pragma unroll
+          for (int p = 0; p < 2; ++p)
+            mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
+        }
+      }
+    }
+    // C fragment: [0],[1] -> column c0+2p, tokens 2t, 2t+1; [2],[3] -> column c0+2p+1
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        acc[p][mt][0] = fmaf(B.sc[u][2 * p], gacc[p][mt][0], acc[p][mt][0]);
+        acc[p][mt][1] = fmaf(B.sc[u][2 * p], gacc[p][mt][1], acc[p][mt][1]);
+        acc[p][mt][2] = fmaf(B.sc[u][2 * p + 1], gacc[p][mt][2], acc[p][mt][2]);
+        acc[p][mt][3] = fmaf(B.sc[u][2 * p + 1], gacc[p][mt][3], acc[p][mt][3]);
+      }
+  }
+}
+
 template <int BITS, int GS, int MT>
 __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a) {
-  constexpr int PER = 32 / BITS;
-  constexpr int KSTEP = 4 * PER;              // K covered by one warp step (4 packed rows)
-  static_assert(GS % KSTEP == 0, "group size must be a multiple of 4 packed rows");
-  constexpr int SPG = GS / KSTEP;             // steps per group
-  constexpr int UG = SPG >= 8 ? 1 : 8 / SPG;  // groups whose loads are in flight together
+  using W = WBatch<BITS, GS>;
+  constexpr int PER = W::PER;
+  constexpr int UG = W::UG;
   constexpr int MAXM = 8 * MT;
-  constexpr uint32_t MASK = (1u << BITS) - 1u;
 
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int sh_exp[16];
@@ -205,9 +384,20 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   const int g0 = (int)((long)a.G * rank / a.cs);
   const int g1 = (int)((long)a.G * (rank + 1) / a.cs);
   const int ng = g1 - g0;
-  const int kbase = g0 * GS;
   const int klen = ng * GS;
   const int M = a.M, N = a.N;
+  const int c0 = blockIdx.y * kCtaCols + warp * 32 + gq * 4;
+  const bool col_ok = c0 < N;
+
+  if (a.cs > 1) cluster_arrive_relaxed();  // every CTA of the cluster is running before DSMEM use
+  if (tid < 16) sh_max[tid] = 0u;
+
+  // The first batch of weights is requested before anything else: it does not depend on
+  // the previous kernel's results, so under PDL it streams while that kernel finishes.
+  W A, B;
+  load_batch<BITS, GS>(A, a, g0, g1, c0, col_ok, t);
+  pdl_trigger();
+  pdl_wait();
 
   __half* xs = reinterpret_cast<__half*>(smem);
   // the partial-sum buffer sits at the same offset in every CTA of the cluster (DSMEM maps
@@ -215,12 +405,8 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
   const int xs_bytes = ((M * klen_max * 2) + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + xs_bytes);
-
-  stage_x<PER>(a, kbase, klen, xs, sh_exp, sh_max);
-
-  const int c0 = blockIdx.y * kCtaCols + warp * 32 + gq * 4;
-  const bool col_ok = c0 < N;
-  const long rows_per_group = GS / PER;
+  __syncthreads();  // sh_max zeroed
+  stage_x<PER>(a, g0 * GS, klen, xs, sh_exp, sh_max);
 
   float acc[2][MT][4];
 #pragma unroll
@@ -230,103 +416,13 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[p][mt][i] = 0.f;
 
-  for (int gb = 0; gb < ng; gb += UG) {
-    uint4 wv[UG][SPG];
-    float scv[UG][4];
-    uint32_t zw[UG];
-    // ---- issue every load of UG groups before touching any of them
-#pragma unroll
-    for (int u = 0; u < UG; ++u) {
-      const int grp = g0 + gb + u;
-      const bool ok = col_ok && (gb + u < ng);
-      const int srow = grp / a.gs_mult;
-#pragma unroll
-      for (int s = 0; s < SPG; ++s) {
-        const long r = (long)grp * rows_per_group + s * 4 + t;
-        wv[u][s] = ok ? ldg_stream_v4(a.qw + r * N + c0) : make_uint4(0, 0, 0, 0);
-      }
-      if (ok) {
-        if (a.sc_dtype == QL_F16) {
-          const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(a.sc) + (long)srow * N + c0);
-          const float2 f0 = __half22float2(u32_as_h2(h.x));
-          const float2 f1 = __half22float2(u32_as_h2(h.y));
-          scv[u][0] = f0.x; scv[u][1] = f0.y; scv[u][2] = f1.x; scv[u][3] = f1.y;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) scv[u][i] = load_as_float(a.sc, a.sc_dtype, (long)srow * N + c0 + i);
-        }
-        zw[u] = a.qz[(long)srow * (N / PER) + c0 / PER] >> (BITS * (c0 % PER));
-      } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) scv[u][i] = 0.f;
-        zw[u] = 0;
-      }
-    }
-    // ---- consume
-#pragma unroll
-    for (int u = 0; u < UG; ++u) {
-      if (gb + u >= ng) break;  // warp-uniform
-      uint32_t zlo[4], zhi[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float z = (float)((zw[u] >> (BITS * i)) & MASK) + a.zoff;
-        zlo[i] = h2_as_u32(__float2half2_rn(1024.f + z));
-        zhi[i] = h2_as_u32(__float2half2_rn(-(64.f + z)));
-      }
-      float gacc[2][MT][4];
-#pragma unroll
-      for (int p = 0; p < 2; ++p)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) gacc[p][mt][i] = 0.f;
-
-      const int kgrp = (gb + u) * GS;  // offset of this group inside the staged slice
-#pragma unroll
-      for (int s = 0; s < SPG; ++s) {
-        const int koff = kgrp + (s * 4 + t) * PER;
-        const uint32_t wcol[4] = {wv[u][s].x, wv[u][s].y, wv[u][s].z, wv[u][s].w};
-        if constexpr (BITS == 4) {
-          uint32_t P[4][4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) unpack_int4(wcol[i], zlo[i], zhi[i], P[i]);
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const int tok = gq + 8 * mt;
-            uint4 xv = make_uint4(0, 0, 0, 0);
-            if (tok < M) xv = *reinterpret_cast<const uint4*>(xs + (long)tok * klen + koff);
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-              mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
-              mma_16816_f16(gacc[p][mt], P[2 * p][2], P[2 * p + 1][2], P[2 * p][3], P[2 * p + 1][3], xv.z, xv.w);
-            }
-          }
-        } else {
-          uint32_t P[4][2];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) unpack_int8(wcol[i], zlo[i], P[i]);
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt) {
-            const int tok = gq + 8 * mt;
-            uint2 xv = make_uint2(0, 0);
-            if (tok < M) xv = *reinterpret_cast<const uint2*>(xs + (long)tok * klen + koff);
-#pragma unroll
-            for (int p = 0; p < 2; ++p)
-              mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
-          }
-        }
-      }
-      // C fragment: [0],[1] -> column c0+2p, tokens 2t, 2t+1; [2],[3] -> column c0+2p+1
-#pragma unroll
-      for (int p = 0; p < 2; ++p)
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          acc[p][mt][0] = fmaf(scv[u][2 * p], gacc[p][mt][0], acc[p][mt][0]);
-          acc[p][mt][1] = fmaf(scv[u][2 * p], gacc[p][mt][1], acc[p][mt][1]);
-          acc[p][mt][2] = fmaf(scv[u][2 * p + 1], gacc[p][mt][2], acc[p][mt][2]);
-          acc[p][mt][3] = fmaf(scv[u][2 * p + 1], gacc[p][mt][3], acc[p][mt][3]);
-        }
-    }
+  // double-buffered batches: the next batch is in flight while the current one is consumed
+  const int nbatch = (ng + UG - 1) / UG;
+  for (int b = 0; b < nbatch; b += 2) {
+    if (b + 1 < nbatch) load_batch<BITS, GS>(B, a, g0 + (b + 1) * UG, g1, c0, col_ok, t);
+    compute_batch<BITS, GS, MT>(A, acc, xs, klen, b * UG * GS, ng - b * UG, gq, t, M, a.zoff);
+    if (b + 2 < nbatch) load_batch<BITS, GS>(A, a, g0 + (b + 2) * UG, g1, c0, col_ok, t);
+    if (b + 1 < nbatch) compute_batch<BITS, GS, MT>(B, acc, xs, klen, (b + 1) * UG * GS, ng - (b + 1) * UG, gq, t, M, a.zoff);
   }
 
   // ---- epilogue: undo the activation scale, then write (single CTA) or reduce (cluster)
@@ -348,6 +444,13 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
     return;
   }
 
+  // Each rank owns a contiguous share of this CTA column's outputs. Every CTA pushes its
+  // partials straight into the owner's shared memory (remote stores do not wait for a round
+  // trip), one cluster barrier publishes them, and each owner sums its share in rank order.
+  cg::cluster_group cluster = cg::this_cluster();
+  const int total = kCtaCols * M;
+  const int chunk = (total + a.cs - 1) / a.cs;
+  cluster_wait_acquire();  // pairs with the relaxed arrive at kernel start
 #pragma unroll
   for (int p = 0; p < 2; ++p)
 #pragma unroll
@@ -355,27 +458,29 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int tok = 8 * mt + 2 * t + (i & 1);
-        const int lcol = warp * 32 + gq * 4 + 2 * p + (i >> 1);
-        if (tok < M) red[lcol * MAXM + tok] = acc[p][mt][i] * exp2i(sh_exp[tok]);
+        if (tok < M) {
+          const int lcol = warp * 32 + gq * 4 + 2 * p + (i >> 1);
+          const int idx = lcol * M + tok;
+          const int owner = idx / chunk;
+          float* dst = cluster.map_shared_rank(red, owner);
+          dst[rank * chunk + (idx - owner * chunk)] = acc[p][mt][i] * exp2i(sh_exp[tok]);
+        }
       }
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster.sync();
-  const int total = kCtaCols * M;
-  const int lo = (int)((long)total * rank / a.cs), hi = (int)((long)total * (rank + 1) / a.cs);
-  for (int idx = lo + tid; idx < hi; idx += blockDim.x) {
-    const int lcol = idx / M, tok = idx % M;
-    const int col = blockIdx.y * kCtaCols + lcol;
+  cluster_arrive_release();
+  cluster_wait_acquire();
+  for (int s = tid; s < chunk; s += blockDim.x) {
+    const int idx = rank * chunk + s;
+    if (idx >= total) break;
     float v = 0.f;
-    for (int q = 0; q < a.cs; ++q) {
-      const float* rr = cluster.map_shared_rank(red, q);
-      v += rr[lcol * MAXM + tok];
-    }
+    for (int q = 0; q < a.cs; ++q) v += red[q * chunk + s];
+    const int lcol = idx / M, tok = idx - (idx / M) * M;
+    const int col = blockIdx.y * kCtaCols + lcol;
     if (col < N) {
       if (a.bias) v += a.bias[col];
       store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
     }
   }
-  cluster.sync();  // keep this CTA's partials alive until every rank has read them
+  (void)MAXM;
 }
 
 template <int BITS, int GS, int MT>
@@ -383,7 +488,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   auto kern = gptq_gemv_kernel<BITS, GS, MT>;
   const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
   const size_t xs_bytes = ((size_t)a.M * klen_max * 2 + 15) & ~(size_t)15;
-  const size_t smem = xs_bytes + (size_t)kCtaCols * 8 * MT * sizeof(float);
+  const size_t smem = xs_bytes + ((size_t)kCtaCols * a.M + a.cs) * sizeof(float);
   if (smem > 200 * 1024) {
     set_error("ql_gptq_matmul: activation slice needs %zu bytes of shared memory (M=%d, K=%d)", smem, a.M, a.K);
     return QL_ERR_UNSUPPORTED;
@@ -405,13 +510,19 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   cfg.blockDim = dim3(kNW * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = a.cs;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  int nattr = 1;
+  if (launch_flags() & QL_LAUNCH_PDL) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    nattr = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, a), "gptq_gemv launch");
 }
 
@@ -442,10 +553,11 @@ int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const
               const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
               int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st) {
   // kernel group: the largest of {128, 64, 32} dividing the checkpoint's group size
-  int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
-  if (bits == 8 && kgs < 16) kgs = 16;
+  const int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
   GemvArgs a;
   a.x = x; a.x_perm = x_perm; a.ldx = ldx; a.x_dtype = x_dtype;
+  const int vec_elems = x_dtype == QL_F32 ? 4 : 8;
+  a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
   a.qw = reinterpret_cast<const uint32_t*>(qweight);
   a.qz = reinterpret_cast<const uint32_t*>(qzeros);
   a.sc = scales; a.sc_dtype = sc_dtype; a.bias = bias;
@@ -454,16 +566,19 @@ int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const
   a.G = K / kgs;
   a.gs_mult = gs / kgs;
   a.zoff = zoff;
-  static int sms = 0;
+  static int sms = 0, cs_cap = 0, warps_per_sm = 0;
   if (sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
+    cs_cap = env_int("QL_GEMV_MAX_CLUSTER", 16);
+    warps_per_sm = env_int("QL_GEMV_WARPS_PER_SM", 16);
   }
   const int cta_cols = (N + kCtaCols - 1) / kCtaCols;
-  const int target = sms * 4;  // 4 CTAs x 4 warps per SM
+  const int target = sms * (warps_per_sm / kNW);
   int cs = pow2_floor(target / cta_cols > 0 ? target / cta_cols : 1);
+  if (cs > cs_cap) cs = cs_cap;
   if (cs > 16) cs = 16;
   while (cs > 1 && cs > a.G) cs /= 2;
   // keep the staged activation slice within shared memory

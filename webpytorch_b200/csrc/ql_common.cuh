@@ -24,6 +24,12 @@ namespace ql {
 void set_error(const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* where);
 
+// Launch flags set through ql_set_launch_flags (QL_LAUNCH_* bits).
+int launch_flags();
+
+// Integer knob from the environment (benchmark tuning only), read once per name by the caller.
+int env_int(const char* name, int dflt);
+
 // ---------------------------------------------------------------------------------------
 // bit twiddling
 // ---------------------------------------------------------------------------------------
@@ -67,6 +73,24 @@ __device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
   uint2 r;
   asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
   return r;
+}
+
+// ---------------------------------------------------------------------------------------
+// programmatic dependent launch (PDL) and cluster barriers
+// ---------------------------------------------------------------------------------------
+// Lets the next kernel in the stream be scheduled once every CTA of this grid has run it.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Waits until the previous kernel in the stream has completed and its writes are visible
+// (a no-op when this grid was not launched as a programmatic dependent).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------------

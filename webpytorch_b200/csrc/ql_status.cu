@@ -1,6 +1,8 @@
 // Status reporting of the C ABI: a per-thread message buffer and the version number.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 
 #include "ql_common.cuh"
 
@@ -21,7 +23,18 @@ int cuda_status(cudaError_t e, const char* where) {
   return QL_ERR_CUDA;
 }
 
+static std::atomic<int> g_launch_flags{0};
+
+int launch_flags() { return g_launch_flags.load(std::memory_order_relaxed); }
+
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
+
 }  // namespace ql
+
+extern "C" int ql_set_launch_flags(int flags) { return ql::g_launch_flags.exchange(flags); }
 
 extern "C" int ql_version(void) { return 100; }  // 0.1.0
 

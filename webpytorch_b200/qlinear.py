@@ -93,7 +93,9 @@ def gptq_quantize(W, group_size=32, bits=4):
     blk = W.reshape(nG, group_size, N)
     wmin = blk.amin(1)
     wmax = blk.amax(1)
-    sc = (wmax - wmin) / qmax
+    # divide by a tensor: torch turns division by a Python scalar into a reciprocal multiply,
+    # which is not the correctly rounded quotient numpy computes
+    sc = (wmax - wmin) / torch.full_like(wmax, float(qmax))
     sc = torch.where(sc == 0, torch.full_like(sc, 1e-8), sc)
     zp = torch.clamp(torch.round(-wmin / sc), 0, qmax).to(torch.int32)
     q = torch.clamp(torch.round(blk / sc[:, None, :]) + zp[:, None, :], 0, qmax).to(torch.int64)
