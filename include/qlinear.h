@@ -13,6 +13,7 @@
 #ifndef WEBPYTORCH_B200_QLINEAR_H
 #define WEBPYTORCH_B200_QLINEAR_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -90,6 +91,32 @@ QL_API int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x
                    const int32_t* qweight, const int32_t* qzeros, const void* scales,
                    int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
                    int M, int K, int N, int gs, int bits, float zero_offset, void* stream);
+
+/*
+ * Bytes of device workspace ql_gptq_matmul_ws needs for an M x K activation on the
+ * tensor-core (large-M) path: the fp16 staging of x plus one int per row.
+ * No counterpart in the reference (its WebGPU buffers are allocated per call, _core.py:4022).
+ */
+QL_API size_t ql_gptq_matmul_workspace(int M, int K);
+
+/*
+ * ql_gptq_matmul with caller-provided device workspace (>= ql_gptq_matmul_workspace(M, K)
+ * bytes, 256-byte aligned). Without it, ql_gptq_matmul takes the workspace from the
+ * stream-ordered allocator (cudaMallocAsync) when the tensor-core path needs one.
+ * Replaces: webtorch/_core.py:4008-4043 (_gptq_matmul), as ql_gptq_matmul.
+ */
+QL_API int ql_gptq_matmul_ws(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                             int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
+                             int M, int K, int N, int gs, int bits, float zero_offset, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/*
+ * Synchronises the device and reports whether a tensor-core kernel gave up on a bounded
+ * wait since the last call (QL_ERR_TIMEOUT), or a CUDA error is pending. Clears the flag.
+ * No counterpart in the reference (its GPU calls have no device-side failure path).
+ */
+QL_API int ql_device_status(void);
 
 /*
  * Load-time row sort for act-order (desc_act) checkpoints: qweight_out row k' takes packed

@@ -166,3 +166,48 @@ def test_empty_batch():
     ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4)
     y = ql(torch.zeros((0, 256), device=DEV))
     assert tuple(y.shape) == (0, 64)
+
+
+# ---------------------------------------------------------------------------------------
+# tensor-core prefill path (M >= 64)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("bits,gs", [(4, 128), (8, 128), (4, 32), (4, 64), (8, 32)])
+@pytest.mark.parametrize("M", [64, 128, 129, 300])
+def test_gemm_path_vs_oracle(bits, gs, M):
+    K, N = 512, 384
+    w = synth.gptq_weights(K, N, bits, gs, seed=M + bits + gs)
+    x = synth.activations(M, K, np.float32, seed=M)
+    ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, gs, bits)
+    y = ql(_t(x)).cpu().numpy()
+    ref = og.gptq_matmul(x, w["qweight"], w["qzeros"], w["scales"], K, N, gs, bits, 1.0)
+    assert max_rel_err(y, ref) < TOL
+    from webpytorch_b200 import _ffi
+    assert _ffi.load().ql_device_status() == 0
+
+
+@pytest.mark.parametrize("M", [64, 200])
+def test_gemm_path_desc_act_bias_ragged_n(M):
+    K, N = 768, 200                    # N not a multiple of the 128-column tile
+    w = synth.gptq_weights(K, N, 4, 128, seed=M, desc_act=True)
+    x = synth.activations(M, K, np.float16, seed=M + 1)
+    bias = np.random.default_rng(M).standard_normal(N).astype(np.float32)
+    ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], bias, 128, 4, g_idx=w["g_idx"])
+    for odt in (torch.float32, torch.bfloat16):
+        y = ql(_t(x), out_dtype=odt).float().cpu().numpy()
+        ref = og.gptq_matmul(x.astype(np.float32), w["qweight"], w["qzeros"], w["scales"], K, N, 128, 4, 1.0,
+                             g_idx=w["g_idx"]) + bias
+        assert max_rel_err(y, ref) < OUT_TOL[odt]
+
+
+@pytest.mark.parametrize("K,N", [(4096, 11008), (3584, 18944)])
+@pytest.mark.parametrize("M", [128, 512, 2048])
+def test_config3_full_size(K, N, M):
+    """Config 3 (desc_act, bf16 x) at full size against the exact dequant in fp64."""
+    w = synth.gptq_weights(K, N, 4, 128, seed=K + M, desc_act=True)
+    ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4, g_idx=w["g_idx"])
+    x = torch.randn((M, K), device=DEV, generator=torch.Generator(device=DEV).manual_seed(M)).to(torch.bfloat16)
+    y = ql(x)
+    W = gptq_dequant(_t(w["qweight"]), _t(w["qzeros"]), _t(w["scales"]), K, N, 128, 4, 1.0,
+                     g_idx=_t(w["g_idx"])).double()
+    ref = x.double() @ W
+    assert max_rel_err(y.cpu().numpy(), ref.cpu().numpy()) < TOL

@@ -26,6 +26,11 @@ SIGNATURES = {
                                 _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
     "ql_gptq_sort_rows": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "ql_set_launch_flags": (_c_int, [_c_int]),
+    "ql_gptq_matmul_workspace": (ctypes.c_size_t, [_c_int, _c_int]),
+    "ql_gptq_matmul_ws": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_int,
+                                   _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp,
+                                   ctypes.c_size_t, _vp]),
+    "ql_device_status": (_c_int, []),
     "ql_q4k_dequant": (_c_int, [_vp, _vp, _c_int, _c_int, _vp]),
     "ql_q4k_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp]),
 }

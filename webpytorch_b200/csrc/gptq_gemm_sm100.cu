@@ -1,13 +1,476 @@
-// Prefill dequant-GEMM (large M) on the sm_100a tensor cores.
+// GPTQ int4/int8 prefill dequant-GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
+//
+// y[M, N] = x[M, K] @ W[K, N], W = scales[g, n] * (q[k, n] - (z[g, n] + zero_offset)).
+//
+// The product is computed transposed, D^T[n, m] = W^T[n, :] . x^T[:, m], so that
+//  * the dequantised weights are the MMA's A operand held in tensor memory: each of 128
+//    dequant threads owns one TMEM lane (one output column n), unpacks its packed words in
+//    registers and writes the fp16 values straight into TMEM with tcgen05.st. Weights never
+//    pass through shared memory, which keeps shared-memory traffic to the activation tile.
+//  * the activations are the B operand: a 256-token x 64-k fp16 tile per stage, loaded by TMA
+//    into 128-byte-swizzled shared memory.
+//  * the fp32 accumulator D (128 columns n x 256 tokens) lives in TMEM; the epilogue warps read
+//    it with tcgen05.ld, undo the activation row scale, add the bias and store y.
+//
+// Numerics: the MMA runs in fp16 with fp32 accumulation. x is staged once (prep_x_kernel) as
+// fp16 scaled per row by an exact power of two (largest |x| in [2^14, 2^15)), which keeps
+// fp16's 11-bit significand for bf16/fp32 inputs without overflow; the weights are
+// fp16(scale * (q - z - off)), one rounding of 2^-12 relative. The staging also applies the
+// act-order permutation x[:, perm[k]] and stores each 8-value block in the (j, j+4) pair order
+// that the register unpack produces, so weights and activations agree on K order.
+//
+// Warp roles (384 threads, one CTA per SM, persistent over output tiles):
+//   warp 0       TMA producer for activation tiles
+//   warp 1       TMEM allocator and MMA issuer (one elected lane)
+//   warps 4-7    dequant producers (TMEM lanes 0-127)
+//   warps 8-11   epilogue (TMEM lanes 0-127)
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "ql_common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace ql {
 
-int gptq_gemm_sm100(const void*, int, long, const int32_t*, const int32_t*, const int32_t*, const void*, int,
-                    const float*, void*, int, long, int, int, int, int, int, float, cudaStream_t,
-                    bool* handled) {
+// device-side status of the tensor-core kernels (a bounded wait that gave up)
+__device__ int g_tc_status = 0;
+
+namespace {
+
+constexpr int kSlabK = 64;          // K per pipeline stage
+constexpr int kTileN = 128;         // output columns per tile (MMA M, TMEM lanes)
+constexpr int kThreads = 384;
+constexpr int kDequantWarp0 = 4;
+constexpr int kEpilogueWarp0 = 8;
+
+// ---------------------------------------------------------------------------------------
+// activation staging: fp16, power-of-two row scale, act-order gather, (j, j+4) pair order
+// ---------------------------------------------------------------------------------------
+template <int BITS>
+__global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x, int x_dtype, long ldx,
+                                                     const int32_t* __restrict__ perm, int M, int K,
+                                                     __half* __restrict__ x16, int* __restrict__ row_exp) {
+  __shared__ float wmax[8];
+  __shared__ int sh_e;
+  const int m = blockIdx.x;
+  const int tid = threadIdx.x;
+  const long base = (long)m * ldx;
+  float mx = 0.f;
+  for (int k = tid; k < K; k += blockDim.x) {
+    const int src = perm ? perm[k] : k;
+    mx = fmaxf(mx, fabsf(load_as_float(x, x_dtype, base + src)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) wmax[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float v = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v = fmaxf(v, wmax[i]);
+    sh_e = stage_exponent(v);
+    row_exp[m] = sh_e;
+  }
+  __syncthreads();
+  const float s = exp2i(-sh_e);
+  for (int b = tid; b < K / 8; b += blockDim.x) {
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = b * 8 + j;
+      const int src = perm ? perm[k] : k;
+      // int4 words pair (j, j+4) of each 8-block; int8 words pair (j, j+2) of each 4-block
+      const int pos = BITS == 4 ? (j & 3) * 2 + (j >> 2) : (j & 4) + (j & 1) * 2 + ((j >> 1) & 1);
+      h[pos] = __float2half_rn(load_as_float(x, x_dtype, base + src) * s);
+    }
+    *reinterpret_cast<uint4*>(x16 + (long)m * K + b * 8) = *reinterpret_cast<uint4*>(h);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// GEMM
+// ---------------------------------------------------------------------------------------
+struct GemmArgs {
+  const uint32_t* qw;
+  const uint32_t* qz;
+  const void* sc;
+  int sc_dtype;
+  const float* bias;
+  const int* row_exp;
+  void* out;
+  long ldo;
+  int out_dtype;
+  int M, K, N, gs;
+  float zoff;
+  int n_wtiles, n_ttiles;
+};
+
+template <int BT, int NS>
+struct SmemLayout {
+  static constexpr int kStageBytes = BT * kSlabK * 2;  // BT rows of 128 bytes
+  static constexpr int kXOff = 0;
+  static constexpr int kBarOff = NS * kStageBytes;
+  // barriers: x_full[NS], a_full[NS], slab_free[NS], d_full, d_empty, final
+  static constexpr int kNumBars = 3 * NS + 3;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kMiscOff + 16 + 1024;  // + tmem slot, abort flag, alignment slack
+};
+
+// Unpack one packed int4 word (8 values along K) for one column into 4 fp16 pairs
+// (q_j, q_{j+4}) * scale; q - z - off is exact in fp16 before the single scale rounding.
+__device__ __forceinline__ void dq_int4(uint32_t w, uint32_t zlo, uint32_t zhi, __half2 s2, uint32_t* out4) {
+  const __half2 one16 = __floats2half2_rn(0.0625f, 0.0625f);
+  const uint32_t w8 = w >> 8;
+  const uint32_t v0 = lop3_andor(w, 0x000F000Fu, kMagicF16x2);
+  const uint32_t v1 = lop3_andor(w, 0x00F000F0u, kMagicF16x2);
+  const uint32_t v2 = lop3_andor(w8, 0x000F000Fu, kMagicF16x2);
+  const uint32_t v3 = lop3_andor(w8, 0x00F000F0u, kMagicF16x2);
+  out4[0] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v0), u32_as_h2(zlo)), s2));
+  out4[1] = h2_as_u32(__hmul2(__hfma2(u32_as_h2(v1), one16, u32_as_h2(zhi)), s2));
+  out4[2] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v2), u32_as_h2(zlo)), s2));
+  out4[3] = h2_as_u32(__hmul2(__hfma2(u32_as_h2(v3), one16, u32_as_h2(zhi)), s2));
+}
+// int8: one word = 4 values along K -> pairs (q0, q2), (q1, q3)
+__device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, uint32_t* out2) {
+  const uint32_t v0 = lop3_andor(w, 0x00FF00FFu, kMagicF16x2);
+  const uint32_t v1 = lop3_andor(w >> 8, 0x00FF00FFu, kMagicF16x2);
+  out2[0] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v0), u32_as_h2(zlo)), s2));
+  out2[1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)), s2));
+}
+
+template <int BITS, int BT, int NS>
+__global__ void __launch_bounds__(kThreads, 1)
+    gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs a) {
+  using L = SmemLayout<BT, NS>;
+  constexpr int PER = 32 / BITS;
+  constexpr int ROWS = kSlabK / PER;            // packed rows per slab (8 for int4, 16 for int8)
+  constexpr int TCOLS_A = kSlabK / 2;           // TMEM columns per A stage (fp16 pairs)
+  constexpr int D_COL = 0;
+  constexpr int A_COL = BT;                     // A stages start after the accumulator
+  constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, BT);
+  static_assert(A_COL + NS * TCOLS_A <= 512, "TMEM budget");
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // the 128-byte swizzle pattern is anchored to 1024-byte boundaries
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = ptx::smem_addr(smem);
+  const uint32_t bar0 = sbase + L::kBarOff;
+  auto x_full = [&](int s) { return bar0 + 8u * s; };
+  auto a_full = [&](int s) { return bar0 + 8u * (NS + s); };
+  auto slab_free = [&](int s) { return bar0 + 8u * (2 * NS + s); };
+  const uint32_t d_full = bar0 + 8u * (3 * NS);
+  const uint32_t d_empty = bar0 + 8u * (3 * NS + 1);
+  const uint32_t fin_bar = bar0 + 8u * (3 * NS + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 8);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      ptx::mbar_init(x_full(s), 1);
+      ptx::mbar_init(a_full(s), 128);
+      ptx::mbar_init(slab_free(s), 1);
+    }
+    ptx::mbar_init(d_full, 1);
+    ptx::mbar_init(d_empty, 128);
+    ptx::mbar_init(fin_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 512);
+    ptx::tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) ptx::tma_prefetch(&tmap_x);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int nslab = a.K / kSlabK;
+  const int ntiles = a.n_wtiles * a.n_ttiles;
+
+  if (warp == 0) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
+        const int tt = tile / a.n_wtiles;
+        for (int kb = 0; kb < nslab; ++kb, ++it) {
+          const int s = it % NS;
+          if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(x_full(s), L::kStageBytes);
+          ptx::tma_load_2d(sbase + L::kXOff + s * L::kStageBytes, &tmap_x, x_full(s), kb * kSlabK, tt * BT);
+        }
+      }
+      if (!ok) {  // let the copies already in flight land before the CTA releases its smem
+        for (int j = it > NS ? it - NS : 0; j < it; ++j) ptx::mbar_wait_drain(x_full(j % NS), (j / NS) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      int it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tcount) {
+        if (!ptx::mbar_wait(d_empty, (tcount & 1) ^ 1, abort_flag)) break;
+        ptx::tc_fence_after();
+        for (int kb = 0; kb < nslab; ++kb, ++it) {
+          const int s = it % NS;
+          const uint32_t par = (it / NS) & 1;
+          if (!ptx::mbar_wait(x_full(s), par, abort_flag) || !ptx::mbar_wait(a_full(s), par, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t xs = sbase + L::kXOff + s * L::kStageBytes;
+#pragma unroll
+          for (int j = 0; j < kSlabK / 16; ++j) {
+            ptx::mma_f16_ts(tmem + D_COL, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
+                            IDESC, (kb | j) != 0);
+          }
+          ptx::mma_commit(slab_free(s));  // frees the activation stage and the TMEM A stage
+        }
+        if (ok) ptx::mma_commit(d_full);
+      }
+      // every MMA this thread issued has completed before TMEM is released (also on abort)
+      ptx::mma_commit(fin_bar);
+      ptx::mbar_wait_drain(fin_bar, 0);
+    }
+  } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + 4) {
+    // ---------------- dequant producers: thread = TMEM lane = output column of the tile
+    const int q = warp & 3;
+    const int lrow = q * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int wt = tile % a.n_wtiles;
+      const int n = wt * kTileN + lrow;
+      const bool ok = n < a.N;
+      const int nn = ok ? n : 0;
+      uint32_t w[ROWS];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(a.qw + (long)r * a.N + nn) : 0u;
+      for (int kb = 0; kb < nslab; ++kb, ++it) {
+        const int s = it % NS;
+        // scale and zero of this slab's group(s): a slab of 64 never straddles a group of >= 64,
+        // and a group of 32 is half a slab
+        uint32_t zlo[2], zhi[2];
+        __half2 s2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int g = (kb * kSlabK + h * (kSlabK / 2)) / a.gs;
+          float scv = 0.f;
+          uint32_t z = 0;
+          if (ok) {
+            scv = load_as_float(a.sc, a.sc_dtype, (long)g * a.N + nn);
+            z = (a.qz[(long)g * (a.N / PER) + nn / PER] >> (BITS * (nn % PER))) & MASK;
+          }
+          const float zf = (float)z + a.zoff;
+          zlo[h] = h2_as_u32(__float2half2_rn(1024.f + zf));
+          zhi[h] = h2_as_u32(__float2half2_rn(-(64.f + zf)));
+          s2[h] = __float2half2_rn(scv);
+        }
+        uint32_t v[32];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+          const int h = (r * PER) / (kSlabK / 2);
+          if constexpr (BITS == 4) {
+            dq_int4(w[r], zlo[h], zhi[h], s2[h], &v[r * 4]);
+          } else {
+            dq_int8(w[r], zlo[h], s2[h], &v[r * 2]);
+          }
+        }
+        // prefetch the next slab's packed words (next tile's first slab after the last)
+        if (kb + 1 < nslab) {
+#pragma unroll
+          for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(a.qw + (long)((kb + 1) * ROWS + r) * a.N + nn) : 0u;
+        }
+        if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) goto done;
+        ptx::tmem_st32(lane_addr + A_COL + s * TCOLS_A, v);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(a_full(s));
+      }
+    }
+  } else if (warp >= kEpilogueWarp0) {
+    // ---------------- epilogue: thread = TMEM lane = output column, TMEM columns = tokens
+    const int q = warp & 3;
+    const int lrow = q * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
+      const int wt = tile % a.n_wtiles, tt = tile / a.n_wtiles;
+      const int n = wt * kTileN + lrow;
+      const float b = (a.bias && n < a.N) ? a.bias[n] : 0.f;
+      if (!ptx::mbar_wait(d_full, tcount & 1, abort_flag)) goto done;
+      ptx::tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BT / 32; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld32(lane_addr + D_COL + c * 32, v);
+        ptx::tmem_wait_ld();
+        if (c == BT / 32 - 1) {
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(d_empty);  // accumulator drained into registers
+        }
+        if (n < a.N) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int tok = tt * BT + c * 32 + j;
+            if (tok < a.M) {
+              const float val = __uint_as_float(v[j]) * exp2i(a.row_exp[tok]) + b;
+              store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + n, val);
+            }
+          }
+        }
+      }
+    }
+  }
+done:
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_tc_status, 1);
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, 512);
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+template <int BITS, int BT, int NS>
+int launch_gemm(const GemmArgs& a, const __half* x16, cudaStream_t st) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) {
+    set_error("ql_gptq_matmul: cuTensorMapEncodeTiled is unavailable");
+    return QL_ERR_CUDA;
+  }
+  CUtensorMap tmap;
+  const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+  const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kSlabK, (cuuint32_t)BT};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return QL_ERR_CUDA;
+  }
+  auto kern = gptq_gemm_tc_kernel<BITS, BT, NS>;
+  const int smem = SmemLayout<BT, NS>::kBytes;
+  static int configured_dev = -1;
+  static int sms = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                         "cudaFuncSetAttribute(gemm smem)");
+    if (rc) return rc;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    configured_dev = dev;
+  }
+  const int ntiles = a.n_wtiles * a.n_ttiles;
+  const int grid = ntiles < sms ? ntiles : sms;
+  kern<<<grid, kThreads, smem, st>>>(tmap, a);
+  return cuda_status(cudaGetLastError(), "gptq_gemm_tc launch");
+}
+
+}  // namespace
+
+size_t gptq_gemm_workspace(int M, int K) {
+  return (((size_t)M * K * 2 + 255) & ~(size_t)255) + (size_t)M * 4 + 256;
+}
+
+// Large-M path. *handled = false leaves the call to the GEMV path.
+int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
+                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
+                    void* workspace, size_t ws_bytes, bool* handled) {
   *handled = false;
-  return QL_OK;
+  static int min_m = -1;
+  if (min_m < 0) min_m = env_int("QL_GEMM_MIN_M", 64);
+  if (M < min_m || K % kSlabK != 0 || (gs % 64 != 0 && gs != 32)) return QL_OK;
+  *handled = true;
+  const size_t need = gptq_gemm_workspace(M, K);
+  void* ws = workspace;
+  bool owned = false;
+  if (ws == nullptr || ws_bytes < need) {
+    if (ws != nullptr) {
+      set_error("ql_gptq_matmul: workspace of %zu bytes is smaller than the %zu needed", ws_bytes, need);
+      return QL_ERR_ARG;
+    }
+    int rc = cuda_status(cudaMallocAsync(&ws, need, st), "cudaMallocAsync(workspace)");
+    if (rc) return rc;
+    owned = true;
+  }
+  __half* x16 = reinterpret_cast<__half*>(ws);
+  int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * K * 2 + 255) & ~(size_t)255));
+  if (bits == 4)
+    prep_x_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, M, K, x16, row_exp);
+  else
+    prep_x_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, M, K, x16, row_exp);
+  int rc = cuda_status(cudaGetLastError(), "prep_x launch");
+  if (!rc) {
+    GemmArgs a;
+    a.qw = reinterpret_cast<const uint32_t*>(qweight);
+    a.qz = reinterpret_cast<const uint32_t*>(qzeros);
+    a.sc = scales; a.sc_dtype = sc_dtype; a.bias = bias; a.row_exp = row_exp;
+    a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
+    a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
+    a.n_wtiles = (N + kTileN - 1) / kTileN;
+    if (M <= 128) {
+      a.n_ttiles = (M + 127) / 128;
+      rc = bits == 4 ? launch_gemm<4, 128, 8>(a, x16, st) : launch_gemm<8, 128, 8>(a, x16, st);
+    } else {
+      a.n_ttiles = (M + 255) / 256;
+      rc = bits == 4 ? launch_gemm<4, 256, 4>(a, x16, st) : launch_gemm<8, 256, 4>(a, x16, st);
+    }
+  }
+  if (owned) {
+    const int rc2 = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(workspace)");
+    if (!rc) rc = rc2;
+  }
+  return rc;
+}
+
+int take_tc_status() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(int));
+  const int zero = 0;
+  cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int));
+  return v;
 }
 
 }  // namespace ql
+
+extern "C" size_t ql_gptq_matmul_workspace(int M, int K) { return ql::gptq_gemm_workspace(M, K); }
+
+extern "C" int ql_device_status(void) {
+  const cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return ql::cuda_status(e, "ql_device_status");
+  if (ql::take_tc_status()) {
+    ql::set_error("a tensor-core kernel gave up on a bounded wait");
+    return QL_ERR_TIMEOUT;
+  }
+  return QL_OK;
+}

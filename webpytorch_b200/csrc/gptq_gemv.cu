@@ -175,13 +175,23 @@ __device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int*
         load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
       }
     }
+    // per-token maxima: reduce across the warp first (a warp's chunks span at most two
+    // tokens when a row holds >= 32 chunks; otherwise fall back to per-lane atomics)
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int idx = tid + c * nthr;
+      float mx = 0.f;
       if (idx < nchunk) {
-        float mx = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+      }
+      const int base_idx = tid - (tid & 31) + c * nthr;   // chunk of lane 0 of this warp
+      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;  // whole warp on one token
+      if (uniform) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((tid & 31) == 0) atomicMax(&sh_max[base_idx / cpr], __float_as_uint(mx));
+      } else if (idx < nchunk) {
         atomicMax(&sh_max[idx / cpr], __float_as_uint(mx));
       }
     }
@@ -201,14 +211,17 @@ __device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int*
       }
     }
   } else {
-    for (int idx = tid; idx < nchunk; idx += nthr) {
-      const int m = idx / cpr;
-      float v[8];
-      load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
+    for (int m = 0; m < M; ++m) {
       float mx = 0.f;
+      for (int kc = tid; kc < cpr; kc += nthr) {
+        float v[8];
+        load_x8(a, m, kbase + kc * 8, v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
-      atomicMax(&sh_max[m], __float_as_uint(mx));
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if ((tid & 31) == 0) atomicMax(&sh_max[m], __float_as_uint(mx));
     }
     __syncthreads();
     if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
@@ -447,10 +460,18 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   // Each rank owns a contiguous share of this CTA column's outputs. Every CTA pushes its
   // partials straight into the owner's shared memory (remote stores do not wait for a round
   // trip), one cluster barrier publishes them, and each owner sums its share in rank order.
+  // rank q owns CTA columns [q * cpo, (q + 1) * cpo), cpo = 128 / cs (cs is a power of two)
   cg::cluster_group cluster = cg::this_cluster();
-  const int total = kCtaCols * M;
-  const int chunk = (total + a.cs - 1) / a.cs;
+  const int lg_cpo = 7 - (31 - __clz(a.cs));
+  const int chunk = (kCtaCols >> (31 - __clz(a.cs))) * MAXM;   // floats per source rank
+  float* mine[2];
   cluster_wait_acquire();  // pairs with the relaxed arrive at kernel start
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int lcol = warp * 32 + gq * 4 + 2 * p;    // columns lcol and lcol + 1 (same owner)
+    const int owner = lcol >> lg_cpo;
+    mine[p] = cluster.map_shared_rank(red, owner) + rank * chunk + (lcol - (owner << lg_cpo)) * MAXM;
+  }
 #pragma unroll
   for (int p = 0; p < 2; ++p)
 #pragma unroll
@@ -458,23 +479,16 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int tok = 8 * mt + 2 * t + (i & 1);
-        if (tok < M) {
-          const int lcol = warp * 32 + gq * 4 + 2 * p + (i >> 1);
-          const int idx = lcol * M + tok;
-          const int owner = idx / chunk;
-          float* dst = cluster.map_shared_rank(red, owner);
-          dst[rank * chunk + (idx - owner * chunk)] = acc[p][mt][i] * exp2i(sh_exp[tok]);
-        }
+        if (tok < M) mine[p][(i >> 1) * MAXM + tok] = acc[p][mt][i] * exp2i(sh_exp[tok]);
       }
   cluster_arrive_release();
   cluster_wait_acquire();
-  for (int s = tid; s < chunk; s += blockDim.x) {
-    const int idx = rank * chunk + s;
-    if (idx >= total) break;
+  const int cpo = kCtaCols >> (31 - __clz(a.cs));
+  for (int s = tid; s < cpo * M; s += blockDim.x) {
+    const int c = s / M, tok = s - c * M;
     float v = 0.f;
-    for (int q = 0; q < a.cs; ++q) v += red[q * chunk + s];
-    const int lcol = idx / M, tok = idx - (idx / M) * M;
-    const int col = blockIdx.y * kCtaCols + lcol;
+    for (int q = 0; q < a.cs; ++q) v += red[q * chunk + c * MAXM + tok];
+    const int col = blockIdx.y * kCtaCols + rank * cpo + c;
     if (col < N) {
       if (a.bias) v += a.bias[col];
       store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
@@ -488,7 +502,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   auto kern = gptq_gemv_kernel<BITS, GS, MT>;
   const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
   const size_t xs_bytes = ((size_t)a.M * klen_max * 2 + 15) & ~(size_t)15;
-  const size_t smem = xs_bytes + ((size_t)kCtaCols * a.M + a.cs) * sizeof(float);
+  const size_t smem = xs_bytes + (size_t)kCtaCols * 8 * MT * sizeof(float);
   if (smem > 200 * 1024) {
     set_error("ql_gptq_matmul: activation slice needs %zu bytes of shared memory (M=%d, K=%d)", smem, a.M, a.K);
     return QL_ERR_UNSUPPORTED;
@@ -661,14 +675,36 @@ extern "C" int ql_gptq_sort_rows(const int32_t* qweight_in, const int32_t* perm,
 namespace ql {
 int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
                     const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
-                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff,
-                    cudaStream_t st, bool* handled);
+                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
+                    void* workspace, size_t ws_bytes, bool* handled);
 }
+
+static int gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                            const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias,
+                            void* out, int out_dtype, long ldo, int M, int K, int N, int gs, int bits,
+                            float zero_offset, void* stream, void* workspace, size_t ws_bytes);
 
 extern "C" int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
                               const int32_t* qweight, const int32_t* qzeros, const void* scales,
                               int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
                               int M, int K, int N, int gs, int bits, float zero_offset, void* stream) {
+  return gptq_matmul_impl(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype,
+                          ldo, M, K, N, gs, bits, zero_offset, stream, nullptr, 0);
+}
+
+extern "C" int ql_gptq_matmul_ws(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                                 const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                 int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
+                                 int M, int K, int N, int gs, int bits, float zero_offset, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  return gptq_matmul_impl(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype,
+                          ldo, M, K, N, gs, bits, zero_offset, stream, workspace, workspace_bytes);
+}
+
+static int gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                            const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias,
+                            void* out, int out_dtype, long ldo, int M, int K, int N, int gs, int bits,
+                            float zero_offset, void* stream, void* workspace, size_t ws_bytes) {
   int rc = check_gptq_dims("ql_gptq_matmul", K, N, gs, bits);
   if (rc) return rc;
   if ((rc = check_dtype(x_dtype, "ql_gptq_matmul(x)"))) return rc;
@@ -707,7 +743,7 @@ extern "C" int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_
   cudaStream_t st = (cudaStream_t)stream;
   bool handled = false;
   rc = gptq_gemm_sm100(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype,
-                       ldo, M, K, N, gs, bits, zero_offset, st, &handled);
+                       ldo, M, K, N, gs, bits, zero_offset, st, workspace, ws_bytes, &handled);
   if (handled || rc) return rc;
   // decode path: chunks of up to 16 tokens per launch
   for (int m0 = 0; m0 < M; m0 += 16) {

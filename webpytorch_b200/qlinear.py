@@ -36,6 +36,15 @@ def _to_dev(a, dtype, device):
     return torch.from_numpy(np.ascontiguousarray(np.asarray(a))).to(device=device, dtype=dtype).contiguous()
 
 
+def _param_array(p):
+    """The array behind a parameter: a torch tensor, a numpy array, or an object with `.data`
+    holding one (the reference's Parameter). numpy's own `.data` is a raw buffer, not this."""
+    if isinstance(p, (torch.Tensor, np.ndarray)):
+        return p.detach() if isinstance(p, torch.Tensor) else p
+    d = getattr(p, "data", p)
+    return d.detach() if isinstance(d, torch.Tensor) else np.asarray(d)
+
+
 def _scale_tensor(scales, device):
     """Scales keep their on-disk precision (fp16 for AutoGPTQ, fp32 for the reference quantizer)."""
     if isinstance(scales, torch.Tensor):
@@ -69,10 +78,13 @@ def _gptq_matmul(xf, qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, *, x_per
     M = xf.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=xf.device)
-    _ffi.call("ql_gptq_matmul", _ffi.ptr(xf), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(x_perm),
+    # the tensor-core (large-M) path stages x in a workspace; take it from torch's allocator
+    ws_bytes = _ffi.load().ql_gptq_matmul_workspace(M, K) if M >= 16 else 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xf.device) if ws_bytes else None
+    _ffi.call("ql_gptq_matmul_ws", _ffi.ptr(xf), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(x_perm),
               _ffi.ptr(qweight), _ffi.ptr(qzeros), _ffi.ptr(scales), _ffi.dtype_code(scales.dtype),
               _ffi.ptr(bias), _ffi.ptr(out), _ffi.dtype_code(out.dtype), out.stride(0), M, K, N, gs, bits,
-              float(zoff), _ffi.stream_ptr(stream))
+              float(zoff), _ffi.ptr(ws), ws_bytes, _ffi.stream_ptr(stream))
     return out
 
 
@@ -173,12 +185,12 @@ class QuantizedLinear(torch.nn.Module):
         """Quantise a linear layer whose `weight` is (K, N) = (in, out), as the reference's
         `Linear` stores it (webtorch/_core.py:472-477, 4432-4444)."""
         dev = _device(device)
-        W = lin.weight.data if isinstance(lin.weight, torch.Tensor) else getattr(lin.weight, "data", lin.weight)
-        wdt = torch.float64 if str(getattr(W, "dtype", "")) in ("float64", "torch.float64") else torch.float32
+        W = _param_array(lin.weight)
+        wdt = torch.float64 if W.dtype in (torch.float64, np.float64) else torch.float32
         W = _to_dev(W, wdt, dev)
         b = getattr(lin, "bias", None)
         if b is not None:
-            b = b.data if isinstance(b, torch.Tensor) else getattr(b, "data", b)
+            b = _param_array(b)
         K, N = W.shape
         per = 32 // bits
         kmul = group_size if group_size % per == 0 else group_size * per
