@@ -32,6 +32,8 @@ SHAPES = [(4096, 4096), (4096, 11008), (11008, 4096), (4096, 14336), (14336, 409
 GS = 128
 COPIES = 4
 METRIC = "int4 GEMV HBM GB/s at M=1 (config 1 sweep)"
+GEMM_SHAPES = [(4096, 11008), (3584, 18944)]
+GEMM_M = 2048
 L2_BYTES = 126 * 2 ** 20
 
 
@@ -186,6 +188,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--skip-gemm", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -323,6 +326,37 @@ def main():
     e2e_steps = max(1, min(args.steps, 500))
     ems, _, _ = timed(e2e_step, e2e_steps)
 
+    # ---- config 3: prefill dequant-GEMM (tcgen05), desc_act, bf16 x, M = 2048
+    gemm = {}
+    if not args.skip_gemm:
+        from webpytorch_b200.qlinear import QuantizedLinear
+        _, bf16_peak, _ = peaks()
+        for (K, N) in GEMM_SHAPES:
+            M = GEMM_M
+            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=g)
+            qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // GS, N // 8), dtype=torch.int32, device=dev, generator=g)
+            sc = (torch.rand((K // GS, N), device=dev, generator=g) * 0.018 + 0.002).half()
+            gidx = (torch.arange(K, device=dev) // GS)[torch.randperm(K, device=dev, generator=g)]
+            ql = QuantizedLinear.from_autogptq(qw, qz, sc, None, GS, 4, g_idx=gidx, device=dev)
+            x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+            yb = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                ql(x, out=yb, out_dtype=torch.bfloat16)
+            torch.cuda.synchronize()
+            reps = 20
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                ql(x, out=yb, out_dtype=torch.bfloat16)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            tflops = 2.0 * M * N * K / (us * 1e-6) / 1e12
+            gemm["%dx%d_M%d" % (K, N, M)] = {"us": round(us, 2), "TFLOP/s": round(tflops, 1),
+                                              "frac_of_bf16_peak": round(tflops / bf16_peak, 4)}
+            del ql, qw, qz, sc, x, yb
+        torch.cuda.empty_cache()
+
     tot_bytes = step_bytes() * args.steps * world
     value = tot_bytes / (ms / 1e3) / 1e9
     value_plain = tot_bytes / (ms_plain / 1e3) / 1e9
@@ -347,6 +381,9 @@ def main():
                      "avg_launch_us": round(avg_launch_us, 3)},
         "value_without_pdl": round(value_plain, 2),
         "per_shape": per_shape,
+        "gemm": {"workload": "config3: int4 g128 desc_act dequant-GEMM, bf16 x/out, M=%d (act-order gather "
+                             "+ fp16 staging + tcgen05 GEMM per call)" % GEMM_M,
+                 "bound": "tensor", "peak_TFLOP/s": peaks()[1], "shapes": gemm},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "QuantizedLinear boundary (_gptq_matmul via ctypes) with pinned host x/y copies"},

@@ -44,3 +44,12 @@ def max_rel_err(got, ref):
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.abs(got - ref).max() / (np.abs(ref).max() + 1e-30))
+
+
+def same_bits_or_both_nan(a, b):
+    """Bit-identical float32 arrays, except that NaN matches NaN whatever its payload (numpy keeps
+    an input NaN's payload through arithmetic, CUDA returns the canonical NaN)."""
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return bool(np.array_equal(na, nb) and np.array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32)))

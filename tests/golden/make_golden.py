@@ -98,16 +98,25 @@ def gptq_fromlinear_case(wt):
 
 
 def q4k_cases(G):
-    # (a) the reference self-check's recipe (_core.py:3697-3705): random bytes, redrawn until finite
-    for seed in range(32):
+    # (a) the reference self-check's recipe (_core.py:3697-3705): two random-byte blocks, redrawn
+    # until the dequantised values are finite and below 1e4
+    for seed in range(1000):
         rng = np.random.default_rng(seed)
-        raw = rng.integers(0, 256, (8, 2 * 144), dtype=np.uint8)
-        W = np.asarray(G.dequant(12, raw.tobytes(), 8 * 512), np.float32).reshape(8, 512)
+        raw = rng.integers(0, 256, (2, 144), dtype=np.uint8)
+        W = np.asarray(G.dequant(12, raw.tobytes(), 2 * 256), np.float32).reshape(2, 256)
         if np.all(np.isfinite(W)) and float(np.abs(W).max()) < 1e4:
             break
-    x = rng.standard_normal((3, 512)).astype(np.float32)
-    np.savez_compressed(os.path.join(HERE, "q4k_randombytes.npz"), N=8, K=512, raw=raw, W=W, x=x,
-                        y=(x @ W.T).astype(np.float32))
+    else:
+        raise RuntimeError("no finite random Q4_K block found")
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "q4k_randombytes.npz"), N=2, K=256, raw=raw, W=W, x=x,
+                        y=(x @ W.T).astype(np.float32), seed=seed)
+    # (a') unrestricted random bytes (inf / nan scales included): the decode must agree bit for bit
+    # on every non-NaN value and put NaNs in the same places
+    rng = np.random.default_rng(12345)
+    raw = rng.integers(0, 256, (8, 2 * 144), dtype=np.uint8)
+    W = np.asarray(G.dequant(12, raw.tobytes(), 8 * 512), np.float32).reshape(8, 512)
+    np.savez_compressed(os.path.join(HERE, "q4k_rawbytes_nonfinite.npz"), N=8, K=512, raw=raw, W=W)
     # (b) the benchmark distribution (config 2) at a small size
     rng = np.random.default_rng(11)
     N, K = 64, 1024

@@ -94,8 +94,9 @@ def test_from_linear_padding_and_bias_vs_reference():
 
 @pytest.mark.parametrize("bits,gs", [(4, 128), (8, 128), (4, 32), (8, 64)])
 @pytest.mark.parametrize("M", [1, 7, 16, 17, 40])
-def test_desc_act_vs_oracle(bits, gs, M):
-    K, N = 1024, 384
+@pytest.mark.parametrize("N", [384, 200])    # 384: TMA-fed GEMV; 200 (not a multiple of 32): register-fed
+def test_desc_act_vs_oracle(bits, gs, M, N):
+    K = 1024
     w = synth.gptq_weights(K, N, bits, gs, seed=M + bits, desc_act=True)
     x = synth.activations(M, K, np.float16, seed=M)
     ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, gs, bits, g_idx=w["g_idx"])

@@ -2,7 +2,7 @@
 import numpy as np
 import pytest
 
-from conftest import golden, golden_files, max_rel_err
+from conftest import golden, golden_files, max_rel_err, same_bits_or_both_nan
 from oracle import gptq as og
 from oracle import moe as om
 from oracle import q4k as oq
@@ -80,11 +80,11 @@ def test_autogptq_packer_roundtrip():
 
 
 def test_q4k_dequant_bitexact_vs_reference():
-    for name in ("q4k_randombytes.npz", "q4k_synth.npz"):
+    for name in ("q4k_randombytes.npz", "q4k_synth.npz", "q4k_rawbytes_nonfinite.npz"):
         d = golden(name)
         N, K = int(d["N"]), int(d["K"])
         W = oq.dequant(d["raw"].tobytes(), N * K).reshape(N, K)
-        assert np.array_equal(W.view(np.uint32), d["W"].view(np.uint32))
+        assert same_bits_or_both_nan(W, d["W"])
 
 
 def test_q4k_matmul_vs_reference():

@@ -465,10 +465,16 @@ int take_tc_status() {
 
 extern "C" size_t ql_gptq_matmul_workspace(int M, int K) { return ql::gptq_gemm_workspace(M, K); }
 
+namespace ql {
+int take_tma_gemv_status();
+}
+
 extern "C" int ql_device_status(void) {
   const cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return ql::cuda_status(e, "ql_device_status");
-  if (ql::take_tc_status()) {
+  const int gemm = ql::take_tc_status();
+  const int gemv = ql::take_tma_gemv_status();
+  if (gemm || gemv) {
     ql::set_error("a tensor-core kernel gave up on a bounded wait");
     return QL_ERR_TIMEOUT;
   }

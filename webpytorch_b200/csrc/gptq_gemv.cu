@@ -562,10 +562,19 @@ inline int pow2_floor(int v) {
 
 }  // namespace
 
+bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                   const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
+                   int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
+                   int* rc);
+
 // Picks the K split (cluster size) so the grid holds ~16 warps per SM, then launches.
 int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
               const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
               int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st) {
+  int trc = 0;
+  if (gptq_gemv_tma(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, sc_dtype, bias, out, out_dtype, ldo, M, K, N,
+                    gs, bits, zoff, st, &trc))
+    return trc;
   // kernel group: the largest of {128, 64, 32} dividing the checkpoint's group size
   const int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
   GemvArgs a;

@@ -91,8 +91,8 @@ struct Q4kArgs {
 
 // Stage x[:, kb0*256 : kb1*256] as power-of-two-scaled fp16, each 4-value chunk stored in the
 // order (0, 2, 1, 3) the nibble-pair unpack produces, plus fp32 sums per 32-value sub-block.
-__device__ void q4k_stage_x(const Q4kArgs& a, int k0, int klen, __half* xs, float* xsum, int* sh_exp,
-                            unsigned* sh_max) {
+__device__ void q4k_stage_x(const Q4kArgs& a, int k0, int klen, int xsum_stride, __half* xs, float* xsum,
+                            int* sh_exp, unsigned* sh_max) {
   const int tid = threadIdx.x, nthr = blockDim.x, M = a.M;
   if (tid < 16) sh_max[tid] = 0u;
   __syncthreads();
@@ -124,7 +124,7 @@ __device__ void q4k_stage_x(const Q4kArgs& a, int k0, int klen, __half* xs, floa
       }
       *reinterpret_cast<uint2*>(xs + (long)m * klen + sb * 32 + c * 4) = *reinterpret_cast<uint2*>(v);
     }
-    xsum[m * nsub + sb] = sum;
+    xsum[m * xsum_stride + sb] = sum;
   }
   __syncthreads();
 }
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kNW * 32, 4) q4k_gemv_kernel(const Q4kArgs a) 
   const int xsum_bytes = (M * nb_max * 8 * 4 + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + xs_bytes + xsum_bytes);  // [kCtaRows][MAXM]
 
-  q4k_stage_x(a, k0, klen, xs, xsum, sh_exp, sh_max);
+  q4k_stage_x(a, k0, klen, nb_max * 8, xs, xsum, sh_exp, sh_max);
 
   const int rbase = blockIdx.y * kCtaRows + warp * 16;
   const int rA = rbase + gq, rB = rbase + gq + 8;   // MMA-layout rows
