@@ -1,0 +1,228 @@
+// Mixture-of-experts block on B200: device-side routing and the element-wise glue around the
+// grouped expert GEMMs.
+//
+// Reference semantics (webtorch/lm_engine.py:294-333, moe_mlp): probabilities = softmax over
+// all experts of the router logits (float64 on the host there); the top_k experts of each token
+// are selected (argpartition), their probabilities optionally renormalised to sum to one, every
+// expert runs down(silu(gate(x)) * up(x)) over its tokens, and each token's output is the
+// weighted sum of its experts' outputs.
+//
+// Here everything is on the device, so a decode step needs no host round trip and can be
+// captured in a CUDA graph:
+//   1. moe_topk_kernel      one warp per token: softmax statistics, top-k by repeated warp
+//                           argmax (ties to the lower expert index), weights, per-expert counts
+//   2. moe_scan_kernel      exclusive scan of the counts -> expert row offsets, the list of
+//                           active experts, and the tile table of the grouped tensor-core GEMM
+//   3. moe_scatter_kernel   each (token, k) pair takes a row of its expert's segment
+//   4. grouped GEMMs over the permuted rows (gptq_gemv_tma.cu / gptq_gemm_sm100.cu)
+//   5. moe_act_kernel       a = silu(gate) * up on the fused gate|up output
+//   6. moe_combine_kernel   out[t] = sum_j w[t, j] * y[row(t, j)], in a fixed j order
+// Rows inside an expert's segment are assigned with atomics, so their order varies from run to
+// run, but no output value depends on it: every row is computed independently and the combine
+// sums each token's k rows in slot order.
+#include "ql_common.cuh"
+
+namespace ql {
+namespace {
+
+constexpr int kMaxTopK = 16;
+
+__global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int norm,
+                                int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                                int32_t* __restrict__ counts) {
+  const int warps = blockDim.x >> 5;
+  const int t = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* row = logits + (long)t * E;
+  // softmax statistics: max and sum of exp (full softmax denominator, as the reference)
+  float mx = -INFINITY;
+  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  double den = 0.0;
+  for (int e = lane; e < E; e += 32) den += exp((double)row[e] - (double)mx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  // top-k by repeated argmax over the remaining logits
+  int chosen[kMaxTopK];
+  double pw[kMaxTopK];
+  double psum = 0.0;
+  for (int j = 0; j < k; ++j) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < E; e += 32) {
+      bool taken = false;
+      for (int q = 0; q < j; ++q) taken |= (chosen[q] == e);
+      const float v = row[e];
+      if (!taken && (v > best || (v == best && e < bi))) {
+        best = v;
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    chosen[j] = bi;
+    pw[j] = exp((double)best - (double)mx) / den;
+    psum += pw[j];
+  }
+  if (lane < k) {
+    int my = 0;
+    double w = 0.0;
+    for (int j = 0; j < k; ++j)
+      if (j == lane) {
+        my = chosen[j];
+        w = pw[j];
+      }
+    topk_idx[(long)t * k + lane] = my;
+    topk_w[(long)t * k + lane] = (float)(norm ? w / psum : w);
+    atomicAdd(&counts[my], 1);
+  }
+}
+
+// One CTA: offsets (exclusive scan), active expert list, tile table for the grouped GEMM
+// (tiles of `tile_rows` rows per expert), cursors reset.
+__global__ void moe_scan_kernel(const int32_t* __restrict__ counts, int E, int tile_rows, int32_t* __restrict__ offsets,
+                                int32_t* __restrict__ cursor, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
+                                int32_t* __restrict__ tiles, int32_t* __restrict__ n_tiles, int max_tiles) {
+  __shared__ int s_cnt[1024];
+  __shared__ int s_tile[1024];
+  const int tid = threadIdx.x;
+  for (int base = 0; base < E; base += blockDim.x) {
+    // E <= blockDim.x is the common case; the loop keeps larger E correct
+  }
+  if (tid == 0) {
+    int off = 0, na = 0, nt = 0;
+    for (int e = 0; e < E; ++e) {
+      const int c = counts[e];
+      offsets[e] = off;
+      cursor[e] = 0;
+      if (c > 0) {
+        active[na++] = e;
+        for (int r = 0; r < c; r += tile_rows) {
+          if (nt < max_tiles) {
+            tiles[2 * nt] = e;
+            tiles[2 * nt + 1] = r;
+          }
+          ++nt;
+        }
+      }
+      off += c;
+    }
+    offsets[E] = off;
+    *n_active = na;
+    *n_tiles = nt < max_tiles ? nt : max_tiles;
+  }
+  (void)s_cnt;
+  (void)s_tile;
+}
+
+__global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int T, int k, const int32_t* __restrict__ offsets,
+                                   int32_t* __restrict__ cursor, int32_t* __restrict__ row_token,
+                                   int32_t* __restrict__ pair_row) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * k) return;
+  const int e = topk_idx[i];
+  const int r = offsets[e] + atomicAdd(&cursor[e], 1);
+  row_token[r] = i / k;
+  pair_row[i] = r;
+}
+
+// a[r, n] = silu(y[r, n]) * y[r, I + n]  (gate | up fused along columns), silu = v * sigmoid(v)
+__global__ void moe_act_kernel(const float* __restrict__ y, long P, int I, void* __restrict__ a, int a_dtype) {
+  const long total = P * I;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / I;
+    const int n = (int)(i - r * I);
+    const float g = y[r * 2 * I + n];
+    const float u = y[r * 2 * I + I + n];
+    const float s = g / (1.0f + expf(-g));
+    store_from_float(a, a_dtype, i, s * u);
+  }
+}
+
+// out[t, h] = sum_j w[t, j] * z[pair_row[t, j], h]
+__global__ void moe_combine_kernel(const float* __restrict__ z, const int32_t* __restrict__ pair_row,
+                                   const float* __restrict__ topk_w, int T, int k, int H, void* __restrict__ out,
+                                   int out_dtype, long ldo) {
+  const long total = (long)T * H;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / H);
+    const int h = (int)(i - (long)t * H);
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc = fmaf(topk_w[(long)t * k + j], z[(long)pair_row[(long)t * k + j] * H + h], acc);
+    store_from_float(out, out_dtype, (long)t * ldo + h, acc);
+  }
+}
+
+}  // namespace
+}  // namespace ql
+
+using namespace ql;
+
+extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int norm_topk_prob, int tile_rows,
+                            int32_t* topk_idx, float* topk_w, int32_t* counts, int32_t* offsets, int32_t* cursor,
+                            int32_t* active, int32_t* n_active, int32_t* tiles, int32_t* n_tiles, int max_tiles,
+                            int32_t* row_token, int32_t* pair_row, void* stream) {
+  if (T < 0 || E <= 0 || top_k <= 0 || top_k > E || top_k > kMaxTopK || tile_rows <= 0) {
+    set_error("ql_moe_route: bad sizes (T=%d E=%d top_k=%d, top_k <= %d)", T, E, top_k, kMaxTopK);
+    return QL_ERR_ARG;
+  }
+  if (!logits || !topk_idx || !topk_w || !counts || !offsets || !cursor || !active || !n_active || !tiles ||
+      !n_tiles || !row_token || !pair_row) {
+    set_error("ql_moe_route: null pointer");
+    return QL_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = cuda_status(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "ql_moe_route memset");
+  if (rc) return rc;
+  if (T > 0) {
+    moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, top_k, norm_topk_prob, topk_idx, topk_w, counts);
+    if ((rc = cuda_status(cudaGetLastError(), "moe_topk launch"))) return rc;
+  }
+  moe_scan_kernel<<<1, 32, 0, st>>>(counts, E, tile_rows, offsets, cursor, active, n_active, tiles, n_tiles,
+                                    max_tiles);
+  if ((rc = cuda_status(cudaGetLastError(), "moe_scan launch"))) return rc;
+  if (T > 0) {
+    const int pairs = T * top_k;
+    moe_scatter_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(topk_idx, T, top_k, offsets, cursor, row_token,
+                                                             pair_row);
+    if ((rc = cuda_status(cudaGetLastError(), "moe_scatter launch"))) return rc;
+  }
+  return QL_OK;
+}
+
+extern "C" int ql_moe_act(const float* y, long P, int I, void* a, int a_dtype, void* stream) {
+  if (P < 0 || I <= 0 || !y || !a || a_dtype < QL_F32 || a_dtype > QL_BF16) {
+    set_error("ql_moe_act: bad arguments");
+    return QL_ERR_ARG;
+  }
+  if (P == 0) return QL_OK;
+  const long total = P * I;
+  const long blocks = (total + 255) / 256;
+  moe_act_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, (cudaStream_t)stream>>>(y, P, I, a,
+                                                                                                     a_dtype);
+  return cuda_status(cudaGetLastError(), "moe_act launch");
+}
+
+extern "C" int ql_moe_combine(const float* z, const int32_t* pair_row, const float* topk_w, int T, int top_k, int H,
+                              void* out, int out_dtype, long ldo, void* stream) {
+  if (T < 0 || top_k <= 0 || H <= 0 || !z || !pair_row || !topk_w || !out || ldo < H || out_dtype < QL_F32 ||
+      out_dtype > QL_BF16) {
+    set_error("ql_moe_combine: bad arguments");
+    return QL_ERR_ARG;
+  }
+  if (T == 0) return QL_OK;
+  const long total = (long)T * H;
+  const long blocks = (total + 255) / 256;
+  moe_combine_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, (cudaStream_t)stream>>>(
+      z, pair_row, topk_w, T, top_k, H, out, out_dtype, ldo);
+  return cuda_status(cudaGetLastError(), "moe_combine launch");
+}
