@@ -157,14 +157,47 @@ __device__ __forceinline__ void load_x8(const GemvArgs& a, int m, int k, float (
 }
 
 // Stage x[:, kbase : kbase + klen] for M tokens into shared memory as power-of-two-scaled
-// fp16 in unpack order; sh_exp[m] = e with x_staged = x * 2^-e. sh_max must be zero and
-// visible (a __syncthreads after zeroing) before the call.
-template <int PER>
-__device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int* sh_exp, unsigned* sh_max) {
-  constexpr int CH = 4;  // 8-value chunks a thread keeps in registers on the one-pass path
+// fp16 in unpack order, and the per-(token, group) sums the folded zero point needs.
+//
+// The unpack feeds the MMA "magic" values 1024 + q (even K offsets of an int4 word, all of an
+// int8 word) and 1024 + 16 q (odd K offsets of an int4 word) without subtracting anything, so
+// the activations at odd int4 offsets are stored divided by 16 (exact). Then, per group,
+//   MMA sum C = sum_k xs_k * magic_k = 1024 * A + sum_k x_k q_k,  A = sum_k xs_k (stored values)
+//   sum_k x_k (q_k - z - off) = C - 1024 * A - (z + off) * S,    S = sum_k x_k (effective values)
+// and gsum[m][g] = (A, S). sh_exp[m] = e with x_staged = x * 2^-e. sh_max must be zero and
+// visible before the call.
+template <int BITS, int GS>
+__device__ void stage_x(const GemvArgs& a, int kbase, int klen, int gstride, __half* xs, float2* gsum, int* sh_exp,
+                        unsigned* sh_max) {
+  constexpr int PER = 32 / BITS;
+  constexpr int CH = 4;          // 8-value chunks a thread keeps in registers on the one-pass path
+  constexpr int SEG = GS / 8;    // chunks per group (lanes reduced together)
   const int tid = threadIdx.x, nthr = blockDim.x, M = a.M;
   const int cpr = klen / 8;
   const int nchunk = M * cpr;
+  auto store_chunk = [&](int idx, const float (&v)[8]) {
+    const int m = idx / cpr, kc = idx - m * cpr;
+    const float s = exp2i(-sh_exp[m]);
+    __align__(16) __half h[8];
+    float sa = 0.f, ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool hi = (BITS == 4) && (j & 1);
+      const __half q = __float2half_rn(v[j] * s * (hi ? 0.0625f : 1.f));
+      const float f = __half2float(q);
+      sa += f;
+      ss += hi ? 16.f * f : f;
+      h[chunk_pos<PER>(j)] = q;
+    }
+    *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
+    // the SEG chunks of one group sit in SEG consecutive lanes
+#pragma unroll
+    for (int o = SEG / 2; o > 0; o >>= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, o);
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    if ((kc % SEG) == 0) gsum[m * gstride + kc / SEG] = make_float2(sa, ss);
+  };
   if (nchunk <= nthr * CH) {
     float v[CH][8];
 #pragma unroll
@@ -175,8 +208,7 @@ __device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int*
         load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
       }
     }
-    // per-token maxima: reduce across the warp first (a warp's chunks span at most two
-    // tokens when a row holds >= 32 chunks; otherwise fall back to per-lane atomics)
+    // per-token maxima: reduce across the warp first when the whole warp is on one token
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int idx = tid + c * nthr;
@@ -185,8 +217,8 @@ __device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int*
 #pragma unroll
         for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
       }
-      const int base_idx = tid - (tid & 31) + c * nthr;   // chunk of lane 0 of this warp
-      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;  // whole warp on one token
+      const int base_idx = tid - (tid & 31) + c * nthr;
+      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;
       if (uniform) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -201,13 +233,8 @@ __device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int*
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int idx = tid + c * nthr;
-      if (idx < nchunk) {
-        const int m = idx / cpr, kc = idx - m * cpr;
-        const float s = exp2i(-sh_exp[m]);
-        __align__(16) __half h[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) h[chunk_pos<PER>(j)] = __float2half_rn(v[c][j] * s);
-        *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
+      if (tid - (tid & 31) + c * nthr < nchunk) {   // warp-uniform: whole groups per warp
+        store_chunk(idx, v[c]);
       }
     }
   } else {
@@ -226,41 +253,17 @@ __device__ void stage_x(const GemvArgs& a, int kbase, int klen, __half* xs, int*
     __syncthreads();
     if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
     __syncthreads();
-    for (int idx = tid; idx < nchunk; idx += nthr) {
-      const int m = idx / cpr, kc = idx - m * cpr;
-      float v[8];
-      load_x8(a, m, kbase + kc * 8, v);
-      const float s = exp2i(-sh_exp[m]);
-      __align__(16) __half h[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) h[chunk_pos<PER>(j)] = __float2half_rn(v[j] * s);
-      *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
+    for (int base = 0; base < nchunk; base += nthr) {
+      const int idx = base + tid;
+      if (base + (tid - (tid & 31)) < nchunk) {      // warp-uniform
+        float v[8];
+        const int m = idx / cpr;
+        load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
+        store_chunk(idx, v);
+      }
     }
   }
   __syncthreads();
-}
-
-// Unpack one int4 word (8 values along K) into 4 half2 registers P[j] = (q_j, q_{j+4}) - zz.
-__device__ __forceinline__ void unpack_int4(uint32_t w, uint32_t zlo, uint32_t zhi, uint32_t (&P)[4]) {
-  const __half2 one16 = __floats2half2_rn(0.0625f, 0.0625f);
-  const uint32_t w8 = w >> 8;
-  const uint32_t v0 = lop3_andor(w, 0x000F000Fu, kMagicF16x2);   // 1024 + q0 | 1024 + q4
-  const uint32_t v1 = lop3_andor(w, 0x00F000F0u, kMagicF16x2);   // 1024 + 16 q1 | ... q5
-  const uint32_t v2 = lop3_andor(w8, 0x000F000Fu, kMagicF16x2);  // q2 | q6
-  const uint32_t v3 = lop3_andor(w8, 0x00F000F0u, kMagicF16x2);  // 16 q3 | 16 q7
-  // zlo = 1024 + z + off (both halves); zhi = -(64 + z + off)
-  P[0] = h2_as_u32(__hsub2(u32_as_h2(v0), u32_as_h2(zlo)));
-  P[1] = h2_as_u32(__hfma2(u32_as_h2(v1), one16, u32_as_h2(zhi)));
-  P[2] = h2_as_u32(__hsub2(u32_as_h2(v2), u32_as_h2(zlo)));
-  P[3] = h2_as_u32(__hfma2(u32_as_h2(v3), one16, u32_as_h2(zhi)));
-}
-
-// Unpack one int8 word (4 values along K) into P[0] = (q0, q2) - zz, P[1] = (q1, q3) - zz.
-__device__ __forceinline__ void unpack_int8(uint32_t w, uint32_t zlo, uint32_t (&P)[2]) {
-  const uint32_t v0 = lop3_andor(w, 0x00FF00FFu, kMagicF16x2);
-  const uint32_t v1 = lop3_andor(w >> 8, 0x00FF00FFu, kMagicF16x2);
-  P[0] = h2_as_u32(__hsub2(u32_as_h2(v0), u32_as_h2(zlo)));
-  P[1] = h2_as_u32(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)));
 }
 
 // Register-resident batch of UG consecutive groups of one lane's weights, scales and zeros.
@@ -308,22 +311,17 @@ __device__ __forceinline__ void load_batch(WBatch<BITS, GS>& B, const GemvArgs& 
   }
 }
 
-// Multiply-accumulate one batch; kgrp0 = offset of its first group inside the staged slice.
+// Multiply-accumulate one batch; g_local0 = index of its first group inside the staged slice.
 template <int BITS, int GS, int MT>
 __device__ __forceinline__ void compute_batch(const WBatch<BITS, GS>& B, float (&acc)[2][MT][4], const __half* xs,
-                                              int klen, int kgrp0, int nvalid, int gq, int t, int M, float zoff) {
+                                              const float2* gsum, int gstride, int klen, int g_local0, int nvalid,
+                                              int gq, int t, int M, float zoff) {
   using W = WBatch<BITS, GS>;
   constexpr uint32_t MASK = (1u << BITS) - 1u;
 #pragma unroll
   for (int u = 0; u < W::UG; ++u) {
     if (u >= nvalid) break;  // warp-uniform
-    uint32_t zlo[4], zhi[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float z = (float)((B.z[u] >> (BITS * i)) & MASK) + zoff;
-      zlo[i] = h2_as_u32(__float2half2_rn(1024.f + z));
-      zhi[i] = h2_as_u32(__float2half2_rn(-(64.f + z)));
-    }
+    const int gl = g_local0 + u;
     float gacc[2][MT][4];
 #pragma unroll
     for (int p = 0; p < 2; ++p)
@@ -331,15 +329,20 @@ __device__ __forceinline__ void compute_batch(const WBatch<BITS, GS>& B, float (
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) gacc[p][mt][i] = 0.f;
-    const int kgrp = kgrp0 + u * GS;
 #pragma unroll
     for (int s = 0; s < W::SPG; ++s) {
-      const int koff = kgrp + (s * 4 + t) * W::PER;
+      const int koff = gl * GS + (s * 4 + t) * W::PER;
       const uint32_t wcol[4] = {B.w[u][s].x, B.w[u][s].y, B.w[u][s].z, B.w[u][s].w};
       if constexpr (BITS == 4) {
         uint32_t P[4][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) unpack_int4(wcol[i], zlo[i], zhi[i], P[i]);
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t w8 = wcol[i] >> 8;
+          P[i][0] = lop3_andor(wcol[i], 0x000F000Fu, kMagicF16x2);   // 1024 + q0 | 1024 + q4
+          P[i][1] = lop3_andor(wcol[i], 0x00F000F0u, kMagicF16x2);   // 1024 + 16 q1 | 1024 + 16 q5
+          P[i][2] = lop3_andor(w8, 0x000F000Fu, kMagicF16x2);        // q2 | q6
+          P[i][3] = lop3_andor(w8, 0x00F000F0u, kMagicF16x2);        // 16 q3 | 16 q7
+        }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           const int tok = gq + 8 * mt;
@@ -354,7 +357,10 @@ __device__ __forceinline__ void compute_batch(const WBatch<BITS, GS>& B, float (
       } else {
         uint32_t P[4][2];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) unpack_int8(wcol[i], zlo[i], P[i]);
+        for (int i = 0; i < 4; ++i) {
+          P[i][0] = lop3_andor(wcol[i], 0x00FF00FFu, kMagicF16x2);      // 1024 + b0 | 1024 + b2
+          P[i][1] = lop3_andor(wcol[i] >> 8, 0x00FF00FFu, kMagicF16x2); // 1024 + b1 | 1024 + b3
+        }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           const int tok = gq + 8 * mt;
@@ -366,23 +372,36 @@ __device__ __forceinline__ void compute_batch(const WBatch<BITS, GS>& B, float (
         }
       }
     }
-    // C fragment: [0],[1] -> column c0+2p, tokens 2t, 2t+1; [2],[3] -> column c0+2p+1
+    // fold the magic offset and the zero point, then scale:
+    //   acc += sc * (C - (1024 * A + (z + off) * S))
+    float zc[4];
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+    for (int i = 0; i < 4; ++i) zc[i] = (float)((B.z[u] >> (BITS * i)) & MASK) + zoff;
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        acc[p][mt][0] = fmaf(B.sc[u][2 * p], gacc[p][mt][0], acc[p][mt][0]);
-        acc[p][mt][1] = fmaf(B.sc[u][2 * p], gacc[p][mt][1], acc[p][mt][1]);
-        acc[p][mt][2] = fmaf(B.sc[u][2 * p + 1], gacc[p][mt][2], acc[p][mt][2]);
-        acc[p][mt][3] = fmaf(B.sc[u][2 * p + 1], gacc[p][mt][3], acc[p][mt][3]);
+    for (int mt = 0; mt < MT; ++mt) {
+      float A[2], S[2];
+#pragma unroll
+      for (int tk = 0; tk < 2; ++tk) {
+        const int tok = 8 * mt + 2 * t + tk;
+        const float2 as = tok < M ? gsum[tok * gstride + gl] : make_float2(0.f, 0.f);
+        A[tk] = 1024.f * as.x;
+        S[tk] = as.y;
       }
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int col = 2 * p + (i >> 1), tk = i & 1;
+          const float v = gacc[p][mt][i] - fmaf(zc[col], S[tk], A[tk]);
+          acc[p][mt][i] = fmaf(B.sc[u][col], v, acc[p][mt][i]);
+        }
+    }
   }
 }
 
 template <int BITS, int GS, int MT>
 __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a) {
   using W = WBatch<BITS, GS>;
-  constexpr int PER = W::PER;
   constexpr int UG = W::UG;
   constexpr int MAXM = 8 * MT;
 
@@ -412,14 +431,18 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   pdl_trigger();
   pdl_wait();
 
+  // shared memory: staged x [M][klen_max] | group sums [M][ng_max] | partial sums
+  // (offsets are the same in every CTA of the cluster: DSMEM maps a local address to the
+  // same offset in the peer)
+  const int ng_max = (a.G + a.cs - 1) / a.cs;
+  const int klen_max = ng_max * GS;
   __half* xs = reinterpret_cast<__half*>(smem);
-  // the partial-sum buffer sits at the same offset in every CTA of the cluster (DSMEM maps
-  // a local address to the same offset in the peer), so size the x slice for the largest rank
-  const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
   const int xs_bytes = ((M * klen_max * 2) + 15) & ~15;
-  float* red = reinterpret_cast<float*>(smem + xs_bytes);
+  float2* gsum = reinterpret_cast<float2*>(smem + xs_bytes);
+  const int gs_bytes = ((M * ng_max * 8) + 15) & ~15;
+  float* red = reinterpret_cast<float*>(smem + xs_bytes + gs_bytes);
   __syncthreads();  // sh_max zeroed
-  stage_x<PER>(a, g0 * GS, klen, xs, sh_exp, sh_max);
+  stage_x<BITS, GS>(a, g0 * GS, klen, ng_max, xs, gsum, sh_exp, sh_max);
 
   float acc[2][MT][4];
 #pragma unroll
@@ -433,9 +456,10 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   const int nbatch = (ng + UG - 1) / UG;
   for (int b = 0; b < nbatch; b += 2) {
     if (b + 1 < nbatch) load_batch<BITS, GS>(B, a, g0 + (b + 1) * UG, g1, c0, col_ok, t);
-    compute_batch<BITS, GS, MT>(A, acc, xs, klen, b * UG * GS, ng - b * UG, gq, t, M, a.zoff);
+    compute_batch<BITS, GS, MT>(A, acc, xs, gsum, ng_max, klen, b * UG, ng - b * UG, gq, t, M, a.zoff);
     if (b + 2 < nbatch) load_batch<BITS, GS>(A, a, g0 + (b + 2) * UG, g1, c0, col_ok, t);
-    if (b + 1 < nbatch) compute_batch<BITS, GS, MT>(B, acc, xs, klen, (b + 1) * UG * GS, ng - (b + 1) * UG, gq, t, M, a.zoff);
+    if (b + 1 < nbatch)
+      compute_batch<BITS, GS, MT>(B, acc, xs, gsum, ng_max, klen, (b + 1) * UG, ng - (b + 1) * UG, gq, t, M, a.zoff);
   }
 
   // ---- epilogue: undo the activation scale, then write (single CTA) or reduce (cluster)
@@ -457,10 +481,9 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
     return;
   }
 
-  // Each rank owns a contiguous share of this CTA column's outputs. Every CTA pushes its
-  // partials straight into the owner's shared memory (remote stores do not wait for a round
-  // trip), one cluster barrier publishes them, and each owner sums its share in rank order.
-  // rank q owns CTA columns [q * cpo, (q + 1) * cpo), cpo = 128 / cs (cs is a power of two)
+  // rank q owns CTA columns [q * cpo, (q + 1) * cpo), cpo = 128 / cs (cs is a power of two);
+  // every CTA pushes its partials into the owner's shared memory, one cluster barrier
+  // publishes them, and each owner sums its share in rank order
   cg::cluster_group cluster = cg::this_cluster();
   const int lg_cpo = 7 - (31 - __clz(a.cs));
   const int chunk = (kCtaCols >> (31 - __clz(a.cs))) * MAXM;   // floats per source rank
@@ -494,15 +517,15 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
       store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
     }
   }
-  (void)MAXM;
 }
 
 template <int BITS, int GS, int MT>
 int launch_gemv(const GemvArgs& a, cudaStream_t st) {
   auto kern = gptq_gemv_kernel<BITS, GS, MT>;
-  const int klen_max = ((a.G + a.cs - 1) / a.cs) * GS;
-  const size_t xs_bytes = ((size_t)a.M * klen_max * 2 + 15) & ~(size_t)15;
-  const size_t smem = xs_bytes + (size_t)kCtaCols * 8 * MT * sizeof(float);
+  const int ng_max = (a.G + a.cs - 1) / a.cs;
+  const size_t xs_bytes = ((size_t)a.M * ng_max * GS * 2 + 15) & ~(size_t)15;
+  const size_t gs_bytes = ((size_t)a.M * ng_max * 8 + 15) & ~(size_t)15;
+  const size_t smem = xs_bytes + gs_bytes + (size_t)kCtaCols * 8 * MT * sizeof(float);
   if (smem > 200 * 1024) {
     set_error("ql_gptq_matmul: activation slice needs %zu bytes of shared memory (M=%d, K=%d)", smem, a.M, a.K);
     return QL_ERR_UNSUPPORTED;

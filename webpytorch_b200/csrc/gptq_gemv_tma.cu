@@ -523,7 +523,7 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
                    int* rc) {
   static int enabled = -1, sms = 0, ctas_per_sm = 0;
   if (enabled < 0) {
-    enabled = env_int("QL_GEMV_TMA", 1);
+    enabled = env_int("QL_GEMV_TMA", 0);
     ctas_per_sm = env_int("QL_GEMV_TMA_CTAS_PER_SM", 2);
     int dev = 0;
     cudaGetDevice(&dev);
