@@ -1,0 +1,182 @@
+// Device helpers shared by the two decode-GEMV kernels (register-fed and TMA-fed): loading
+// activations, and staging them as power-of-two-scaled fp16 in the order the nibble unpack
+// produces, together with the per-group sums that fold the zero point into the partial sums.
+#pragma once
+
+#include "ql_common.cuh"
+
+namespace ql {
+namespace gemv {
+
+// Position of value j of a packed word inside the fp16 staging of x. The register unpack
+// pairs value j with value j + per/2 in one half2, so x is stored in the same pair order.
+template <int PER>
+__device__ __forceinline__ int stage_pos(int j) {
+  return (j % (PER / 2)) * 2 + j / (PER / 2);
+}
+// the same inside an 8-value chunk (one int4 word, or two int8 words)
+template <int PER>
+__device__ __forceinline__ int chunk_pos(int j) {
+  return (j / PER) * PER + stage_pos<PER>(j % PER);
+}
+
+// 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats.
+template <class Args>
+__device__ __forceinline__ void load_x8(const Args& a, int m, int k, float (&v)[8]) {
+  const long base = (long)m * a.ldx;
+  if (a.x_perm == nullptr && a.x_vec) {
+    if (a.x_dtype == QL_F16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(a.x) + base + k);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(u32_as_h2(w[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    } else if (a.x_dtype == QL_BF16) {
+      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) + base + k);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __uint_as_float(w[i] << 16);
+        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else {
+      const float4 f0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + base + k);
+      const float4 f1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + base + k + 4);
+      v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+      v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int src = a.x_perm ? a.x_perm[k + j] : k + j;
+      v[j] = load_as_float(a.x, a.x_dtype, base + src);
+    }
+  }
+}
+
+// Stage x[:, kbase : kbase + klen] for M tokens into shared memory as power-of-two-scaled
+// fp16 in unpack order, and the per-(token, group) sums the folded zero point needs.
+//
+// The unpack feeds the MMA "magic" values 1024 + q (even K offsets of an int4 word, all of an
+// int8 word) and 1024 + 16 q (odd K offsets of an int4 word) without subtracting anything, so
+// the activations at odd int4 offsets are stored divided by 16 (exact). Then, per group,
+//   MMA sum C = sum_k xs_k * magic_k = 1024 * A + sum_k x_k q_k,  A = sum_k xs_k (stored values)
+//   sum_k x_k (q_k - z - off) = C - 1024 * A - (z + off) * S,    S = sum_k x_k (effective values)
+// and gsum[m][g] = (A, S). sh_exp[m] = e with x_staged = x * 2^-e. sh_max must be zero and
+// visible before the call.
+//
+// NAMED: synchronise only the nthr participating threads with named barrier 1 (the TMA-fed
+// kernel keeps its producer warp out of the staging); otherwise __syncthreads.
+template <int BITS, int GS, bool NAMED, class Args>
+__device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half* xs, float2* gsum, int* sh_exp,
+                        unsigned* sh_max, int tid, int nthr) {
+  constexpr int PER = 32 / BITS;
+  constexpr int CH = 4;          // 8-value chunks a thread keeps in registers on the one-pass path
+  constexpr int SEG = GS / 8;    // chunks per group (lanes reduced together)
+  const int M = a.M;
+  auto sync = [&]() {
+    if constexpr (NAMED) {
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    } else {
+      __syncthreads();
+    }
+  };
+  const int cpr = klen / 8;
+  const int nchunk = M * cpr;
+  auto store_chunk = [&](int idx, const float (&v)[8]) {
+    const int m = idx / cpr, kc = idx - m * cpr;
+    const float s = exp2i(-sh_exp[m]);
+    __align__(16) __half h[8];
+    float sa = 0.f, ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const bool hi = (BITS == 4) && (j & 1);
+      const __half q = __float2half_rn(v[j] * s * (hi ? 0.0625f : 1.f));
+      const float f = __half2float(q);
+      sa += f;
+      ss += hi ? 16.f * f : f;
+      h[chunk_pos<PER>(j)] = q;
+    }
+    *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
+    // the SEG chunks of one group sit in SEG consecutive lanes
+#pragma unroll
+    for (int o = SEG / 2; o > 0; o >>= 1) {
+      sa += __shfl_xor_sync(0xffffffffu, sa, o);
+      ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    }
+    if ((kc % SEG) == 0) gsum[m * gstride + kc / SEG] = make_float2(sa, ss);
+  };
+  if (nchunk <= nthr * CH) {
+    float v[CH][8];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (idx < nchunk) {
+        const int m = idx / cpr;
+        load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
+      }
+    }
+    // per-token maxima: reduce across the warp first when the whole warp is on one token
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      float mx = 0.f;
+      if (idx < nchunk) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+      }
+      const int base_idx = tid - (tid & 31) + c * nthr;
+      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;
+      if (uniform) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((tid & 31) == 0) atomicMax(&sh_max[base_idx / cpr], __float_as_uint(mx));
+      } else if (idx < nchunk) {
+        atomicMax(&sh_max[idx / cpr], __float_as_uint(mx));
+      }
+    }
+    sync();
+    if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
+    sync();
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (tid - (tid & 31) + c * nthr < nchunk) {   // warp-uniform: whole groups per warp
+        store_chunk(idx, v[c]);
+      }
+    }
+  } else {
+    for (int m = 0; m < M; ++m) {
+      float mx = 0.f;
+      for (int kc = tid; kc < cpr; kc += nthr) {
+        float v[8];
+        load_x8(a, m, kbase + kc * 8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if ((tid & 31) == 0) atomicMax(&sh_max[m], __float_as_uint(mx));
+    }
+    sync();
+    if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
+    sync();
+    for (int base = 0; base < nchunk; base += nthr) {
+      const int idx = base + tid;
+      if (base + (tid - (tid & 31)) < nchunk) {      // warp-uniform
+        float v[8];
+        const int m = idx / cpr;
+        load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
+        store_chunk(idx, v);
+      }
+    }
+  }
+  sync();
+}
+
+
+}  // namespace gemv
+}  // namespace ql

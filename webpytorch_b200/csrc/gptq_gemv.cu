@@ -29,8 +29,10 @@
 #include <cooperative_groups.h>
 
 #include "ql_common.cuh"
+#include "gemv_common.cuh"
 
 namespace cg = cooperative_groups;
+using ql::gemv::chunk_pos;
 
 namespace ql {
 namespace {
@@ -104,167 +106,11 @@ struct GemvArgs {
   int M, K, N;
   int G;        // number of GS-row kernel groups (K / GS)
   int gs_mult;  // scale/zero row = kernel group / gs_mult (checkpoint group size = GS * gs_mult)
-  int cs;       // cluster size along K (== gridDim.x)
+  int lg_gs_mult;  // log2(gs_mult) when it is a power of two, else -1
+  int cs;       // cluster size along K (== gridDim.x), a power of two
+  int lg_cs;
   float zoff;
 };
-
-// Position of value j of a packed word inside the fp16 staging of x. The register unpack
-// pairs value j with value j + per/2 in one half2, so x is stored in the same pair order.
-template <int PER>
-__device__ __forceinline__ int stage_pos(int j) {
-  return (j % (PER / 2)) * 2 + j / (PER / 2);
-}
-// the same inside an 8-value chunk (one int4 word, or two int8 words)
-template <int PER>
-__device__ __forceinline__ int chunk_pos(int j) {
-  return (j / PER) * PER + stage_pos<PER>(j % PER);
-}
-
-// 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats.
-__device__ __forceinline__ void load_x8(const GemvArgs& a, int m, int k, float (&v)[8]) {
-  const long base = (long)m * a.ldx;
-  if (a.x_perm == nullptr && a.x_vec) {
-    if (a.x_dtype == QL_F16) {
-      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(a.x) + base + k);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(u32_as_h2(w[i]));
-        v[2 * i] = f.x;
-        v[2 * i + 1] = f.y;
-      }
-    } else if (a.x_dtype == QL_BF16) {
-      const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) + base + k);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        v[2 * i] = __uint_as_float(w[i] << 16);
-        v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-      }
-    } else {
-      const float4 f0 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + base + k);
-      const float4 f1 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.x) + base + k + 4);
-      v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-      v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int src = a.x_perm ? a.x_perm[k + j] : k + j;
-      v[j] = load_as_float(a.x, a.x_dtype, base + src);
-    }
-  }
-}
-
-// Stage x[:, kbase : kbase + klen] for M tokens into shared memory as power-of-two-scaled
-// fp16 in unpack order, and the per-(token, group) sums the folded zero point needs.
-//
-// The unpack feeds the MMA "magic" values 1024 + q (even K offsets of an int4 word, all of an
-// int8 word) and 1024 + 16 q (odd K offsets of an int4 word) without subtracting anything, so
-// the activations at odd int4 offsets are stored divided by 16 (exact). Then, per group,
-//   MMA sum C = sum_k xs_k * magic_k = 1024 * A + sum_k x_k q_k,  A = sum_k xs_k (stored values)
-//   sum_k x_k (q_k - z - off) = C - 1024 * A - (z + off) * S,    S = sum_k x_k (effective values)
-// and gsum[m][g] = (A, S). sh_exp[m] = e with x_staged = x * 2^-e. sh_max must be zero and
-// visible before the call.
-template <int BITS, int GS>
-__device__ void stage_x(const GemvArgs& a, int kbase, int klen, int gstride, __half* xs, float2* gsum, int* sh_exp,
-                        unsigned* sh_max) {
-  constexpr int PER = 32 / BITS;
-  constexpr int CH = 4;          // 8-value chunks a thread keeps in registers on the one-pass path
-  constexpr int SEG = GS / 8;    // chunks per group (lanes reduced together)
-  const int tid = threadIdx.x, nthr = blockDim.x, M = a.M;
-  const int cpr = klen / 8;
-  const int nchunk = M * cpr;
-  auto store_chunk = [&](int idx, const float (&v)[8]) {
-    const int m = idx / cpr, kc = idx - m * cpr;
-    const float s = exp2i(-sh_exp[m]);
-    __align__(16) __half h[8];
-    float sa = 0.f, ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const bool hi = (BITS == 4) && (j & 1);
-      const __half q = __float2half_rn(v[j] * s * (hi ? 0.0625f : 1.f));
-      const float f = __half2float(q);
-      sa += f;
-      ss += hi ? 16.f * f : f;
-      h[chunk_pos<PER>(j)] = q;
-    }
-    *reinterpret_cast<uint4*>(xs + (long)m * klen + kc * 8) = *reinterpret_cast<uint4*>(h);
-    // the SEG chunks of one group sit in SEG consecutive lanes
-#pragma unroll
-    for (int o = SEG / 2; o > 0; o >>= 1) {
-      sa += __shfl_xor_sync(0xffffffffu, sa, o);
-      ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    }
-    if ((kc % SEG) == 0) gsum[m * gstride + kc / SEG] = make_float2(sa, ss);
-  };
-  if (nchunk <= nthr * CH) {
-    float v[CH][8];
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int idx = tid + c * nthr;
-      if (idx < nchunk) {
-        const int m = idx / cpr;
-        load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
-      }
-    }
-    // per-token maxima: reduce across the warp first when the whole warp is on one token
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int idx = tid + c * nthr;
-      float mx = 0.f;
-      if (idx < nchunk) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
-      }
-      const int base_idx = tid - (tid & 31) + c * nthr;
-      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;
-      if (uniform) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if ((tid & 31) == 0) atomicMax(&sh_max[base_idx / cpr], __float_as_uint(mx));
-      } else if (idx < nchunk) {
-        atomicMax(&sh_max[idx / cpr], __float_as_uint(mx));
-      }
-    }
-    __syncthreads();
-    if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
-    __syncthreads();
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int idx = tid + c * nthr;
-      if (tid - (tid & 31) + c * nthr < nchunk) {   // warp-uniform: whole groups per warp
-        store_chunk(idx, v[c]);
-      }
-    }
-  } else {
-    for (int m = 0; m < M; ++m) {
-      float mx = 0.f;
-      for (int kc = tid; kc < cpr; kc += nthr) {
-        float v[8];
-        load_x8(a, m, kbase + kc * 8, v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if ((tid & 31) == 0) atomicMax(&sh_max[m], __float_as_uint(mx));
-    }
-    __syncthreads();
-    if (tid < M) sh_exp[tid] = stage_exponent(__uint_as_float(sh_max[tid]));
-    __syncthreads();
-    for (int base = 0; base < nchunk; base += nthr) {
-      const int idx = base + tid;
-      if (base + (tid - (tid & 31)) < nchunk) {      // warp-uniform
-        float v[8];
-        const int m = idx / cpr;
-        load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
-        store_chunk(idx, v);
-      }
-    }
-  }
-  __syncthreads();
-}
 
 // Register-resident batch of UG consecutive groups of one lane's weights, scales and zeros.
 template <int BITS, int GS>
@@ -286,11 +132,11 @@ __device__ __forceinline__ void load_batch(WBatch<BITS, GS>& B, const GemvArgs& 
   for (int u = 0; u < W::UG; ++u) {
     const int grp = grp0 + u;
     const bool ok = col_ok && grp < gend;
-    const int srow = grp / a.gs_mult;
+    const int srow = a.lg_gs_mult >= 0 ? (grp >> a.lg_gs_mult) : grp / a.gs_mult;
+    const uint32_t* wp = a.qw + (size_t)(grp * (GS / W::PER) + t) * N + c0;
 #pragma unroll
     for (int s = 0; s < W::SPG; ++s) {
-      const long r = (long)grp * (GS / W::PER) + s * 4 + t;
-      B.w[u][s] = ok ? ldg_stream_v4(a.qw + r * N + c0) : make_uint4(0, 0, 0, 0);
+      B.w[u][s] = ok ? ldg_stream_v4(wp + (size_t)(s * 4) * N) : make_uint4(0, 0, 0, 0);
     }
     if (ok) {
       if (a.sc_dtype == QL_F16) {
@@ -413,8 +259,10 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   const int warp = tid >> 5, lane = tid & 31;
   const int gq = lane >> 2, t = lane & 3;
   const int rank = blockIdx.x;  // position along K inside the cluster
-  const int g0 = (int)((long)a.G * rank / a.cs);
-  const int g1 = (int)((long)a.G * (rank + 1) / a.cs);
+  // balanced split of G groups over cs ranks: the first G % cs ranks take one extra group
+  const int gq_base = a.G >> a.lg_cs, grem = a.G & (a.cs - 1);
+  const int g0 = rank * gq_base + min(rank, grem);
+  const int g1 = g0 + gq_base + (rank < grem ? 1 : 0);
   const int ng = g1 - g0;
   const int klen = ng * GS;
   const int M = a.M, N = a.N;
@@ -442,7 +290,7 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   const int gs_bytes = ((M * ng_max * 8) + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + xs_bytes + gs_bytes);
   __syncthreads();  // sh_max zeroed
-  stage_x<BITS, GS>(a, g0 * GS, klen, ng_max, xs, gsum, sh_exp, sh_max);
+  gemv::stage_x<BITS, GS, false>(a, g0 * GS, klen, ng_max, xs, gsum, sh_exp, sh_max, tid, (int)blockDim.x);
 
   float acc[2][MT][4];
 #pragma unroll
@@ -611,6 +459,7 @@ int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const
   a.M = M; a.K = K; a.N = N;
   a.G = K / kgs;
   a.gs_mult = gs / kgs;
+  a.lg_gs_mult = (a.gs_mult & (a.gs_mult - 1)) == 0 ? 31 - __builtin_clz(a.gs_mult) : -1;
   a.zoff = zoff;
   static int sms = 0, cs_cap = 0, warps_per_sm = 0;
   if (sms == 0) {
@@ -630,6 +479,7 @@ int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const
   // keep the staged activation slice within shared memory
   while (cs < 16 && cs < a.G && (size_t)M * ((a.G + cs - 1) / cs) * kgs * 2 > 96 * 1024) cs *= 2;
   a.cs = cs;
+  a.lg_cs = 31 - __builtin_clz(cs);
   return bits == 4 ? dispatch_gs<4>(a, kgs, st) : dispatch_gs<8>(a, kgs, st);
 }
 
