@@ -57,7 +57,7 @@ struct TmaGemvArgs {
   int out_dtype;
   int M, K, N, gs;
   int nstage;   // K / kStageK
-  int cs;       // cluster size along K (power of two)
+  int cs;       // cluster size along K
   float zoff;
 };
 
@@ -200,15 +200,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t zw = *reinterpret_cast<const uint32_t*>(stp + L::kWBytes + L::kScBytes +
                                                                (u * (kTileCols / PER) + lcol / PER) * 4) >>
                             (BITS * (lcol % PER));
-        float gacc[2][MT][4];
+        // two accumulator sets, alternating by step, halve the dependent MMA chain
+        float gacc2[2][2][MT][4];
 #pragma unroll
-        for (int p = 0; p < 2; ++p)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
+          for (int p = 0; p < 2; ++p)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) gacc[p][mt][q] = 0.f;
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+              for (int q = 0; q < 4; ++q) gacc2[h][p][mt][q] = 0.f;
 #pragma unroll
         for (int sp = 0; sp < SPG; ++sp) {
+          float (&gacc)[2][MT][4] = gacc2[sp & 1];
           const int row = (u * SPG + sp) * 4 + t;                  // packed row inside the stage
           const uint32_t addr = st + strip_off + row * 128 + ((gq ^ (row & 7)) << 4);
           uint4 wv;
@@ -256,6 +260,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+        float gacc[2][MT][4];
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) gacc[p][mt][q] = gacc2[0][p][mt][q] + gacc2[1][p][mt][q];
         // acc += scale * (C - (1024 A + (z + off) S))
         const int gl = i * GPS + u;
         float zc[4];
@@ -304,24 +315,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       // partials pushed into the owning rank's shared memory (rank q owns columns
       // [q * cpo, (q + 1) * cpo) of the CTA tile, cpo = 256 / cs)
       cg::cluster_group cluster = cg::this_cluster();
-      const int lg_cs = 31 - __clz(a.cs);
-      const int lg_cpo = 8 - lg_cs;
-      const int chunk = (kTileCols >> lg_cs) * MAXM;
+      const int cpo_max = (kTileCols + a.cs - 1) / a.cs;
+      const int chunk = cpo_max * MAXM;
       __syncwarp();
       cluster_wait_acquire();
 #pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const int lc = lcol + 2 * p;
-        const int owner = lc >> lg_cpo;
-        float* dst = cluster.map_shared_rank(red, owner) + rank * chunk + (lc - (owner << lg_cpo)) * MAXM;
+      for (int p = 0; p < 2; ++p)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
+        for (int h = 0; h < 2; ++h) {
+          const int lc = lcol + 2 * p + h;
+          const int owner = (lc * a.cs) >> 8;
+          const int ostart = (owner * kTileCols + a.cs - 1) / a.cs;
+          float* dst = cluster.map_shared_rank(red, owner) + rank * chunk + (lc - ostart) * MAXM;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int tok = 8 * mt + 2 * t + (q & 1);
-            if (tok < M) dst[(q >> 1) * MAXM + tok] = acc[p][mt][q] * exp2i(sh_exp[tok]);
-          }
-      }
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int tk = 0; tk < 2; ++tk) {
+              const int tok = 8 * mt + 2 * t + tk;
+              if (tok < M) dst[tok] = acc[p][mt][2 * h + tk] * exp2i(sh_exp[tok]);
+            }
+        }
     }
   }
 
@@ -330,14 +343,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kCW) cluster_wait_acquire();   // the producer joins the cluster barrier phases
     cluster_arrive_release();
     cluster_wait_acquire();
-    const int lg_cs = 31 - __clz(a.cs);
-    const int cpo = kTileCols >> lg_cs;
-    const int chunk = cpo * MAXM;
+    const int cpo_max = (kTileCols + a.cs - 1) / a.cs;
+    const int chunk = cpo_max * MAXM;
+    const int ostart = (rank * kTileCols + a.cs - 1) / a.cs;
+    const int oend = ((rank + 1) * kTileCols + a.cs - 1) / a.cs;
+    const int cpo = oend - ostart;
     for (int s = tid; s < cpo * M; s += blockDim.x) {
       const int c = s / M, tok = s - c * M;
       float v = 0.f;
       for (int q = 0; q < a.cs; ++q) v += red[q * chunk + c * MAXM + tok];
-      const int col = blockIdx.y * kTileCols + rank * cpo + c;
+      const int col = blockIdx.y * kTileCols + ostart + c;
       if (col < N) {
         if (a.bias) v += a.bias[col];
         store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
@@ -403,7 +418,7 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   const int sq = a.nstage / a.cs;
   const int nst_max = sq + (a.nstage % a.cs ? 1 : 0);
   const size_t smem = 1024 + L::kXsOff + (((size_t)a.M * nst_max * kStageK * 2 + 15) & ~(size_t)15) +
-                      (((size_t)a.M * nst_max * L::GPS * 8 + 15) & ~(size_t)15) + (size_t)kTileCols * 8 * MT * 4;
+                      (((size_t)a.M * nst_max * L::GPS * 8 + 15) & ~(size_t)15) + (size_t)(kTileCols + 16) * 8 * MT * 4;
   if (smem > 200 * 1024) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -455,12 +470,6 @@ int tma_gs(const TmaGemvArgs& a, int kgs, const uint32_t* qw, const uint32_t* qz
   }
 }
 
-inline int pow2_floor(int v) {
-  int p = 1;
-  while (p * 2 <= v) p *= 2;
-  return p;
-}
-
 }  // namespace
 
 // Returns true (and the launch status in *rc) when the TMA-fed GEMV handles this shape.
@@ -490,11 +499,23 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
+  // cluster size (K split): the CTA count tiles * cs should fill one resident wave of
+  // ctas_per_sm CTAs per SM as evenly as possible (the busiest SM sets the time)
   const int tiles = (N + kTileCols - 1) / kTileCols;
-  int cs = pow2_floor(sms * ctas_per_sm / tiles > 0 ? sms * ctas_per_sm / tiles : 1);
-  if (cs > 16) cs = 16;
-  while (cs > 1 && cs > a.nstage) cs /= 2;
-  while (cs < 16 && cs < a.nstage && (size_t)M * ((a.nstage + cs - 1) / cs) * kStageK * 2 > 64 * 1024) cs *= 2;
+  int cs = 1;
+  double best = -1.0;
+  for (int c = 1; c <= 16 && c <= a.nstage; ++c) {
+    const int ctas = tiles * c;
+    if (ctas > sms * ctas_per_sm && c > 1) break;
+    if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;
+    const double per_sm = (double)ctas / sms;
+    const double busiest = (double)((ctas + sms - 1) / sms);
+    const double score = per_sm / busiest * (per_sm < ctas_per_sm ? per_sm / ctas_per_sm : 1.0);
+    if (score > best + 1e-9) {
+      best = score;
+      cs = c;
+    }
+  }
   a.cs = cs;
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
