@@ -477,10 +477,12 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
                    int* rc) {
-  static int enabled = -1, sms = 0, ctas_per_sm = 0;
+  static int enabled = -1, sms = 0, ctas_per_sm = 0, max_cluster = 8;
   if (enabled < 0) {
     enabled = env_int("QL_GEMV_TMA", 1);
     ctas_per_sm = env_int("QL_GEMV_TMA_CTAS_PER_SM", 2);
+    // clusters of 16 CTAs with this kernel's shared memory do not all fit in one wave
+    max_cluster = env_int("QL_GEMV_MAX_CLUSTER", 8);
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -504,7 +506,7 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   const int tiles = (N + kTileCols - 1) / kTileCols;
   int cs = 1;
   double best = -1.0;
-  for (int c = 1; c <= 16 && c <= a.nstage; ++c) {
+  for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
     const int ctas = tiles * c;
     if (ctas > sms * ctas_per_sm && c > 1) break;
     if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;

@@ -50,9 +50,11 @@ constexpr uint32_t kMagicF16x2 = 0x64006400u;
 // ---------------------------------------------------------------------------------------
 // legacy warp MMA: D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
 // ---------------------------------------------------------------------------------------
+// Not volatile: a pure register computation the compiler may schedule freely, so independent
+// loads and unpacking interleave with the MMAs.
 __device__ __forceinline__ void mma_16816_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                               uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -62,16 +64,18 @@ __device__ __forceinline__ void mma_16816_f16(float (&d)[4], uint32_t a0, uint32
 // ---------------------------------------------------------------------------------------
 // global loads that bypass L1 allocation for streamed, read-once weights
 // ---------------------------------------------------------------------------------------
+// Weights are read-only for the kernel's lifetime, so these loads are not volatile: the
+// compiler may hoist them and overlap them with unrelated work.
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
   return r;
 }
 __device__ __forceinline__ uint2 ldg_stream_v2(const void* p) {
   uint2 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
   return r;
 }
 
