@@ -112,6 +112,27 @@ QL_API int ql_gptq_matmul_ws(const void* x, int x_dtype, long ldx, const int32_t
                              size_t workspace_bytes, void* stream);
 
 /*
+ * ql_gptq_matmul for callers that cannot allocate device memory at call time: hosts that hand
+ * out all device memory through their own allocator or budget (inference servers, plugin
+ * sandboxes, language bindings with no handle on a CUDA allocator) and code that must not
+ * allocate under a latency budget. It allocates nothing. The large-M (tensor-core) path keeps
+ * its scratch in a fixed 24 MiB device array inside the library, held by every GPU that loads
+ * it until the process exits (ql_gptq_matmul_noalloc_max_scratch() returns the size); calls
+ * whose M x K needs more than that fail with QL_ERR_UNSUPPORTED. The first call on a device
+ * resolves the array's device address, so make one call per device before any stream capture.
+ * All calls share the array: calls that can overlap on the GPU (different streams) race and
+ * must be serialised by the caller. Small-M calls use no scratch at all.
+ * No counterpart in the reference.
+ */
+QL_API int ql_gptq_matmul_noalloc(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                                  const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                  int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
+                                  int M, int K, int N, int gs, int bits, float zero_offset, void* stream);
+
+/* Bytes of the fixed scratch array ql_gptq_matmul_noalloc works in. No counterpart in the reference. */
+QL_API size_t ql_gptq_matmul_noalloc_max_scratch(void);
+
+/*
  * Synchronises the device and reports whether a tensor-core kernel gave up on a bounded
  * wait since the last call (QL_ERR_TIMEOUT), or a CUDA error is pending. Clears the flag.
  * No counterpart in the reference (its GPU calls have no device-side failure path).

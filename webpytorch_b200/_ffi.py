@@ -31,6 +31,9 @@ SIGNATURES = {
                                    _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp,
                                    ctypes.c_size_t, _vp]),
     "ql_device_status": (_c_int, []),
+    "ql_gptq_matmul_noalloc": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_int,
+                                        _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
+    "ql_gptq_matmul_noalloc_max_scratch": (ctypes.c_size_t, []),
     "ql_q4k_dequant": (_c_int, [_vp, _vp, _c_int, _c_int, _vp]),
     "ql_q4k_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp]),
 }

@@ -27,6 +27,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "ql_common.cuh"
 #include "sm100_ptx.cuh"
 
@@ -401,15 +403,20 @@ size_t gptq_gemm_workspace(int M, int K) {
   return (((size_t)M * K * 2 + 255) & ~(size_t)255) + (size_t)M * 4 + 256;
 }
 
+// True when a call of this shape takes the tensor-core (large-M) path below.
+bool gemm_path_taken(int M, int K, int gs) {
+  static int min_m = -1;
+  if (min_m < 0) min_m = env_int("QL_GEMM_MIN_M", 64);
+  return M >= min_m && K % kSlabK == 0 && (gs % 64 == 0 || gs == 32);
+}
+
 // Large-M path. *handled = false leaves the call to the GEMV path.
 int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
                     const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
                     int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
                     void* workspace, size_t ws_bytes, bool* handled) {
   *handled = false;
-  static int min_m = -1;
-  if (min_m < 0) min_m = env_int("QL_GEMM_MIN_M", 64);
-  if (M < min_m || K % kSlabK != 0 || (gs % 64 != 0 && gs != 32)) return QL_OK;
+  if (!gemm_path_taken(M, K, gs)) return QL_OK;
   *handled = true;
   const size_t need = gptq_gemm_workspace(M, K);
   void* ws = workspace;
@@ -479,4 +486,75 @@ extern "C" int ql_device_status(void) {
     return QL_ERR_TIMEOUT;
   }
   return QL_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// allocation-free entry point
+// ---------------------------------------------------------------------------------------
+namespace ql {
+// Some callers cannot allocate device memory at call time: hosts that hand out every byte of
+// device memory through their own allocator or a fixed budget (inference servers, plugin
+// sandboxes, language bindings with no handle on a CUDA allocator) and code that must not
+// allocate while it runs under a latency budget. For them the only scratch this library needs
+// -- the large-M path's fp16 activation staging plus one int per row -- lives in the fixed
+// array below, which every GPU that loads the library holds until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 24ull << 20;  // 24 MiB: M * K up to ~12.5 M activations
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64];
+
+// Device address of the scratch array on the current device, resolved once per device (the
+// host-side symbol is only a stand-in; a kernel must be given this address).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  int rc = cuda_status(cudaGetDevice(&dev), "ql_gptq_matmul_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= 64) {
+    set_error("ql_gptq_matmul_noalloc: device ordinal %d out of range", dev);
+    return QL_ERR_UNSUPPORTED;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "ql_gptq_matmul_noalloc: cudaGetSymbolAddress");
+    if (rc) return rc;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return QL_OK;
+}
+
+}  // namespace
+
+int gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                     const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias, void* out,
+                     int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zero_offset,
+                     void* stream, void* workspace, size_t ws_bytes);
+}  // namespace ql
+
+extern "C" size_t ql_gptq_matmul_noalloc_max_scratch(void) { return ql::kNoAllocScratchBytes; }
+
+extern "C" int ql_gptq_matmul_noalloc(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                                      const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                      int scales_dtype, const float* bias, void* out, int out_dtype, long ldo,
+                                      int M, int K, int N, int gs, int bits, float zero_offset, void* stream) {
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  if (M > 0 && K > 0 && gs > 0 && ql::gemm_path_taken(M, K, gs)) {
+    const size_t need = ql::gptq_gemm_workspace(M, K);
+    if (need > ql::kNoAllocScratchBytes) {
+      ql::set_error("ql_gptq_matmul_noalloc: M=%d x K=%d needs %zu bytes of scratch; this entry point has %zu "
+                    "(use ql_gptq_matmul_ws with a workspace, or split M)",
+                    M, K, need, ql::kNoAllocScratchBytes);
+      return QL_ERR_UNSUPPORTED;
+    }
+    const int rc = ql::noalloc_scratch(&ws);
+    if (rc) return rc;
+    ws_bytes = ql::kNoAllocScratchBytes;
+  }
+  return ql::gptq_matmul_impl(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype,
+                              ldo, M, K, N, gs, bits, zero_offset, stream, ws, ws_bytes);
 }

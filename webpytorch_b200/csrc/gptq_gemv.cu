@@ -561,10 +561,12 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
                     void* workspace, size_t ws_bytes, bool* handled);
 }
 
-static int gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
-                            const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias,
-                            void* out, int out_dtype, long ldo, int M, int K, int N, int gs, int bits,
-                            float zero_offset, void* stream, void* workspace, size_t ws_bytes);
+namespace ql {
+int gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                     const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias, void* out,
+                     int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zero_offset,
+                     void* stream, void* workspace, size_t ws_bytes);
+}
 
 extern "C" int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
                               const int32_t* qweight, const int32_t* qzeros, const void* scales,
@@ -583,10 +585,10 @@ extern "C" int ql_gptq_matmul_ws(const void* x, int x_dtype, long ldx, const int
                           ldo, M, K, N, gs, bits, zero_offset, stream, workspace, workspace_bytes);
 }
 
-static int gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
-                            const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias,
-                            void* out, int out_dtype, long ldo, int M, int K, int N, int gs, int bits,
-                            float zero_offset, void* stream, void* workspace, size_t ws_bytes) {
+int ql::gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
+                         const int32_t* qzeros, const void* scales, int scales_dtype, const float* bias, void* out,
+                         int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zero_offset,
+                         void* stream, void* workspace, size_t ws_bytes) {
   int rc = check_gptq_dims("ql_gptq_matmul", K, N, gs, bits);
   if (rc) return rc;
   if ((rc = check_dtype(x_dtype, "ql_gptq_matmul(x)"))) return rc;
