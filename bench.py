@@ -4,7 +4,7 @@ Headline (config 1): int4 GPTQ decode GEMV at M=1 over the five (
 shapes {(4096,4096), (4096,11008), (11008,4096), (4096,14336), (14336,4096)}, group 128,
 fp16 x, fp32 out. One step = one pass over the five shapes on each of R=4 distinct weight
 copies (20 GEMVs, 466 MB of packed weights > 2 x L2), so no launch finds its weights in L2.
-`value` = algorithmic bytes (weights + x + out, SURVEY 8d basis) / device time, inputs
+`value` = algorithmic bytes (packed weights + scales + zeros + x + out) / device time, inputs
 resident in HBM. `e2e` = the same bytes through the public Python operator with pinned host
 x copied in and y copied out every step.
 

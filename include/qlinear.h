@@ -168,6 +168,50 @@ QL_API int ql_q4k_dequant(const uint8_t* raw, float* W, int N, int K, void* stre
 QL_API int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias,
                          void* out, int out_dtype, long ldo, int M, int K, int N, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Mixture-of-experts block. Replaces the body of `moe_mlp` (webtorch/lm_engine.py:294-329):
+ * the host-side softmax / argpartition / per-expert loop becomes device routing plus two
+ * grouped GEMMs over expert-sorted rows, so a step needs no host round trip.
+ *
+ *   ql_moe_route           logits [T, E] fp32 -> topk_idx/topk_w [T, top_k] (softmax over all
+ *                          experts, top_k by value, ties to the lower index; renormalised when
+ *                          norm_topk_prob, as lm_engine.py:301-307), counts [E], offsets [E+1]
+ *                          (expert e owns rows offsets[e] .. offsets[e+1]-1 of the P = T*top_k
+ *                          sorted rows), the active-expert list, the tile table (tiles of
+ *                          tile_rows rows, 2 ints each; max_tiles >= P/tile_rows + min(E, P)),
+ *                          row_token [P] (token of each sorted row) and pair_row [T*top_k].
+ *                          cursor [E] is scratch. E <= 1024, top_k <= 16.
+ *   ql_moe_grouped_matmul  y[r] = x[row_token[r]] @ W_e (row_token NULL: x[r]) for every sorted
+ *                          row r of expert e; W stacked [E] GPTQ packs (qweight [E][K/per][N],
+ *                          qzeros [E][K/gs][N/per], scales [E][K/gs][N]). Rows per expert are
+ *                          read on the device; max_rows_per_expert is a host bound (<= T) that
+ *                          sizes the decode kernel. Workspace: ql_moe_grouped_workspace bytes.
+ *   ql_moe_act             a [P, I] = silu(y[:, :I]) * y[:, I:] (gate|up fused, _core.py:502)
+ *   ql_moe_combine         out[t] = sum_j topk_w[t, j] * z[pair_row[t, j]]
+ *                          (+ g[t] * shared[t], g = sigmoid(shared_gate[t * ldg]) or 1;
+ *                          lm_engine.py:318-328)
+ * --------------------------------------------------------------------------------------- */
+QL_API int ql_moe_route(const float* logits, int T, int E, int top_k, int norm_topk_prob, int tile_rows,
+                        int32_t* topk_idx, float* topk_w, int32_t* counts, int32_t* offsets, int32_t* cursor,
+                        int32_t* active, int32_t* n_active, int32_t* tiles, int32_t* n_tiles, int max_tiles,
+                        int32_t* row_token, int32_t* pair_row, void* stream);
+
+QL_API size_t ql_moe_grouped_workspace(long P, int E, int K, int gs);
+
+QL_API int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int32_t* row_token, long P,
+                                 const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                 int scales_dtype, int E, const int32_t* offsets, const int32_t* active,
+                                 const int32_t* n_active, const int32_t* tiles, const int32_t* n_tiles,
+                                 int max_tiles, int tile_rows, int max_rows_per_expert, void* out, int out_dtype,
+                                 long ldo, int K, int N, int gs, int bits, float zero_offset, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+QL_API int ql_moe_act(const float* y, long P, int I, void* a, int a_dtype, void* stream);
+
+QL_API int ql_moe_combine(const float* z, const int32_t* pair_row, const float* topk_w, int T, int top_k, int H,
+                          const float* shared, long lds, const float* shared_gate, long ldg, void* out,
+                          int out_dtype, long ldo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,9 +31,10 @@ def silu(x):
     return (x * (1.0 / (1.0 + np.exp(-x)))).astype(np.float32)
 
 
-def moe_mlp(x, logits, experts, top_k, norm_topk_prob=True):
-    """x [T, H] float32; experts[e] = (gate, up, down) callables mapping float32 arrays.
-    Returns float32 [T, H] (lm_engine.py:309-321)."""
+def moe_mlp(x, logits, experts, top_k, norm_topk_prob=True, shared=None, shared_gate=None):
+    """x [T, H] float32; experts[e] = (gate, up, down) callables mapping float32 arrays;
+    shared = (gate, up, down) or None; shared_gate = callable x -> [T, 1] logits or None.
+    Returns float32 [T, H] (lm_engine.py:309-328)."""
     x = np.asarray(x, np.float32)
     T, H = x.shape
     topk_idx, topk_w = route(logits, top_k, norm_topk_prob)
@@ -48,4 +49,12 @@ def moe_mlp(x, logits, experts, top_k, norm_topk_prob=True):
         w = topk_w[rows, slot].astype(np.float32)
         ye = ye * w.reshape(-1, 1)
         out[rows] = out[rows] + ye
-    return out
+    if shared is not None:
+        # lm_engine.py:322-328: shared expert over every token, optionally sigmoid-gated
+        sg, su, sd = shared
+        ys = sd(silu(sg(x)) * su(x)).astype(np.float32)
+        if shared_gate is not None:
+            g = 1.0 / (1.0 + np.exp(-np.asarray(shared_gate(x))))
+            ys = ys * g
+        out = out + ys
+    return out.astype(np.float32)

@@ -156,14 +156,52 @@ def moe_cases(wt, LE):
         np.savez_compressed(os.path.join(HERE, "moe_E%d_k%d_T%d.npz" % (E, top_k, T)), **d)
 
 
+def moe_shared_case(wt, LE):
+    """Qwen-style block: routed experts plus a shared expert gated by sigmoid(x @ g)."""
+    E, top_k, H, I, T, SI = 4, 2, 128, 64, 6, 128
+    rng = np.random.default_rng(300)
+    exps = synth.moe_experts(E, H, I, bits=4, gs=64, rng=rng)
+    sh = synth.moe_experts(1, H, SI, bits=4, gs=64, rng=rng)[0]
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    gate_w = (rng.standard_normal((H, 1)) * 0.05).astype(np.float32)
+
+    class _LM:
+        pass
+    lm = _LM()
+    lm.H = H
+
+    def q(w):
+        return wt.QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 64, 4)
+    experts = [{k: q(e[k]) for k in ("gate", "up", "down")} for e in exps]
+    shared = {k: q(sh[k]) for k in ("gate", "up", "down")}
+    lay = {"moe": {"gate": (lambda t, _l=logits: wt.Tensor(_l)), "top_k": top_k, "norm_topk_prob": False,
+                   "experts": experts, "shared": shared,
+                   "shared_gate": (lambda t: wt.Tensor(np.asarray(t.numpy(), np.float32) @ gate_w))}}
+    y = LE.moe_mlp(lm, lay, wt.Tensor(x)).numpy()
+    d = {"E": E, "top_k": top_k, "H": H, "I": I, "SI": SI, "T": T, "gs": 64, "bits": 4, "logits": logits,
+         "x": x, "y": y, "shared_gate_w": gate_w, "norm_topk_prob": 0}
+    for i, e in enumerate(exps):
+        for k in ("gate", "up", "down"):
+            for f in ("qweight", "qzeros", "scales"):
+                d["e%d_%s_%s" % (i, k, f)] = e[k][f]
+    for k in ("gate", "up", "down"):
+        for f in ("qweight", "qzeros", "scales"):
+            d["shared_%s_%s" % (k, f)] = sh[k][f]
+    np.savez_compressed(os.path.join(HERE, "moe_shared_E%d_k%d_T%d.npz" % (E, top_k, T)), **d)
+
+
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WEBTORCH_REFERENCE", "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WEBTORCH_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py <reference checkout> (or set WEBTORCH_REFERENCE)")
     wt, G, LE = _import_reference(ref)
     gptq_ref_cases(wt)
     gptq_autogptq_cases(wt)
     gptq_fromlinear_case(wt)
     q4k_cases(G)
     moe_cases(wt, LE)
+    moe_shared_case(wt, LE)
     print("golden fixtures written to", HERE)
 
 

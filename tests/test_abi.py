@@ -88,3 +88,32 @@ def test_q4k_entry_points_reject_bad_arguments(lib):
 def test_launch_flags_roundtrip(lib):
     old = lib.ql_set_launch_flags(1)
     assert lib.ql_set_launch_flags(old) == 1
+
+
+def test_moe_entry_points_reject_bad_arguments(lib):
+    v = ctypes.c_void_p
+    p = [v(16)] * 12
+    # ql_moe_route: E above the device scan's limit, top_k above E, top_k above 16
+    for T, E, k in [(4, 1025, 2), (4, 8, 9), (4, 64, 17), (-1, 8, 2)]:
+        assert lib.ql_moe_route(p[0], T, E, k, 1, 128, *p[:9], 4, *p[:2], None) == 1
+    assert lib.ql_moe_route(p[0], 4, 8, 2, 1, 128, *p[:9], 4, None, p[0], None) == 1   # null buffer
+
+    def gm(**kw):
+        a = dict(x=16, x_dtype=0, ldx=256, P=8, qw=16, sc=16, sc_dtype=1, E=4, K=256, N=64, gs=128, bits=4,
+                 zoff=1.0, ldo=64)
+        a.update(kw)
+        return lib.ql_moe_grouped_matmul(v(a["x"]), a["x_dtype"], a["ldx"], None, a["P"], v(a["qw"]), v(16),
+                                         v(a["sc"]), a["sc_dtype"], a["E"], v(16), v(16), v(16), None, None, 0,
+                                         128, 4, v(16), 0, a["ldo"], a["K"], a["N"], a["gs"], a["bits"],
+                                         a["zoff"], None, 0, None)
+    for kw, code in [(dict(bits=3), 3), (dict(N=60, ldo=60), 1), (dict(K=200), 1), (dict(E=0), 1),
+                     (dict(x_dtype=5), 1), (dict(zoff=0.5), 3), (dict(qw=8), 2), (dict(ldx=100), 1),
+                     (dict(P=-1), 1)]:
+        assert gm(**kw) == code, kw
+    assert gm(P=0) == 0
+    assert lib.ql_moe_grouped_workspace(0, 8, 256, 128) == 0
+    assert lib.ql_moe_grouped_workspace(4096, 8, 256, 128) >= 4096 * 256 * 2   # tensor-core path stages x
+    assert lib.ql_moe_act(v(16), 4, 0, v(16), 0, None) == 1
+    assert lib.ql_moe_act(v(16), 0, 8, v(16), 0, None) == 0
+    assert lib.ql_moe_combine(v(16), v(16), v(16), 2, 2, 64, None, 0, None, 0, v(16), 0, 32, None) == 1
+    assert lib.ql_moe_combine(v(16), v(16), v(16), 2, 2, 64, None, 0, v(16), 1, v(16), 0, 64, None) == 1

@@ -1,0 +1,197 @@
+"""MoE block on the GPU against the oracle (a restatement of lm_engine.moe_mlp) and the reference's
+own outputs (tests/golden/moe_*.npz, made by importing the reference)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden, golden_files, max_rel_err
+from oracle import gptq as og
+from oracle import moe as om
+from webpytorch_b200 import moe, synth
+from webpytorch_b200.qlinear import QuantizedLinear
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+DEV = "cuda"
+
+
+def _ql(w, gs, bits):
+    return QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, gs, bits, device=DEV)
+
+
+def _oracle_lin(w, K, N, gs, bits):
+    return lambda x: og.quantized_linear(x, w["qweight"], w["qzeros"], w["scales"], None, K, N, K, N, gs, bits, 1.0)
+
+
+def _check_routing(r, logits, top_k, norm):
+    T, E = logits.shape
+    idx = r.topk_idx.cpu().numpy()
+    w = r.topk_w.cpu().numpy()
+    ref_idx, ref_w = om.route(logits, top_k, norm)
+    for t in range(T):
+        o, ro = np.argsort(idx[t]), np.argsort(ref_idx[t])
+        assert np.array_equal(idx[t][o], ref_idx[t][ro]), t
+        np.testing.assert_allclose(w[t][o], ref_w[t][ro], rtol=1e-6, atol=1e-7)
+    counts = np.bincount(idx.ravel(), minlength=E)
+    assert np.array_equal(r.counts.cpu().numpy(), counts)
+    offs = np.concatenate([[0], np.cumsum(counts)])
+    assert np.array_equal(r.offsets.cpu().numpy(), offs)
+    act = np.nonzero(counts)[0]
+    assert int(r.n_active.item()) == len(act)
+    assert np.array_equal(r.active.cpu().numpy()[:len(act)], act)
+    row_token = r.row_token.cpu().numpy()[:T * top_k]
+    pair_row = r.pair_row.cpu().numpy()
+    assert sorted(pair_row.ravel().tolist()) == list(range(T * top_k))
+    for t in range(T):
+        for j in range(top_k):
+            p = pair_row[t, j]
+            e = idx[t, j]
+            assert row_token[p] == t and offs[e] <= p < offs[e + 1]
+    tiles = [(e, s) for e in act for s in range(0, counts[e], moe.TILE_ROWS)]
+    assert int(r.n_tiles.item()) == len(tiles)
+    assert np.array_equal(r.tiles.cpu().numpy()[:2 * len(tiles)].reshape(-1, 2), np.array(tiles).reshape(-1, 2))
+
+
+@pytest.mark.parametrize("T,E,k,norm", [(1, 8, 2, True), (37, 64, 8, True), (300, 128, 8, False),
+                                        (5, 1000, 16, True), (64, 16, 1, True)])
+def test_route_matches_oracle(T, E, k, norm):
+    rng = np.random.default_rng(T * 7 + E)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    r = moe.route(torch.from_numpy(logits).to(DEV), k, norm)
+    torch.cuda.synchronize()
+    _check_routing(r, logits, k, norm)
+
+
+def test_route_ties_pick_lower_expert():
+    logits = np.zeros((3, 8), np.float32)
+    logits[1, 5] = 1.0
+    r = moe.route(torch.from_numpy(logits).to(DEV), 2)
+    idx = np.sort(r.topk_idx.cpu().numpy(), 1)
+    assert idx[0].tolist() == [0, 1] and idx[1].tolist() == [0, 5] and idx[2].tolist() == [0, 1]
+
+
+def _block_from_fixture(d):
+    E, top_k, gs, bits = (int(d[k]) for k in ("E", "top_k", "gs", "bits"))
+
+    def q(pre, k):
+        return _ql({f: d["%s_%s_%s" % (pre, k, f)] for f in ("qweight", "qzeros", "scales")}, gs, bits)
+    experts = [{k: q("e%d" % e, k) for k in ("gate", "up", "down")} for e in range(E)]
+    logits = torch.from_numpy(d["logits"]).to(DEV)
+    shared = shared_gate = None
+    if "SI" in d:
+        shared = {k: q("shared", k) for k in ("gate", "up", "down")}
+        gw = torch.from_numpy(d["shared_gate_w"]).to(DEV)
+        shared_gate = (lambda x: x @ gw)
+    norm = bool(int(d["norm_topk_prob"])) if "norm_topk_prob" in d else True
+    return moe.MoEBlock(lambda x: logits, experts, top_k, norm, shared, shared_gate)
+
+
+@pytest.mark.parametrize("name", golden_files("moe_"))
+def test_moe_block_vs_reference_fixture(name):
+    d = golden(name)
+    blk = _block_from_fixture(d)
+    y = blk(torch.from_numpy(d["x"]).to(DEV))
+    torch.cuda.synchronize()
+    assert max_rel_err(y.cpu().numpy(), d["y"]) < TOL
+
+
+def test_moe_function_level_dropin():
+    """moe_mlp(lm, lay, x) takes the reference's own layer dict (QuantizedLinear experts)."""
+    d = golden("moe_E8_k2_T5.npz")
+    E, top_k, gs, bits = (int(d[k]) for k in ("E", "top_k", "gs", "bits"))
+    logits = torch.from_numpy(d["logits"]).to(DEV)
+    experts = [{k: _ql({f: d["e%d_%s_%s" % (e, k, f)] for f in ("qweight", "qzeros", "scales")}, gs, bits)
+                for k in ("gate", "up", "down")} for e in range(E)]
+    lay = {"moe": {"gate": (lambda x: logits), "experts": experts, "top_k": top_k, "norm_topk_prob": True,
+                   "shared": None}}
+    x = torch.from_numpy(d["x"]).to(DEV)
+    y = moe.moe_mlp(None, lay, x)
+    assert max_rel_err(y.cpu().numpy(), d["y"]) < TOL
+    assert torch.equal(moe.moe_mlp(None, lay, x), y)     # the cached block is reused
+
+
+def _synthetic_case(E, H, I, T, k, bits, seed, skew=0.0, shared=False):
+    rng = np.random.default_rng(seed)
+    exps = synth.moe_experts(E, H, I, bits=bits, gs=128, rng=rng)
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    if skew:
+        logits[:, 3] += skew                        # one expert takes (nearly) every token
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    sh = synth.moe_experts(1, H, I, bits=bits, gs=128, rng=rng)[0] if shared else None
+    return exps, logits, x, sh
+
+
+@pytest.mark.parametrize("E,H,I,T,k,bits,skew", [
+    (8, 512, 256, 300, 2, 4, 0.0),     # ~75 rows per expert: tensor-core grouped GEMM
+    (8, 512, 256, 260, 2, 8, 0.0),
+    (16, 256, 128, 200, 1, 4, 30.0),   # every token on expert 3: GEMV walks 13 chunks of one expert
+    (64, 1024, 512, 4, 8, 4, 0.0),     # decode: grouped GEMV over the active experts
+    (64, 1024, 512, 16, 8, 8, 0.0),
+])
+def test_moe_block_vs_oracle(E, H, I, T, k, bits, skew):
+    exps, logits, x, _ = _synthetic_case(E, H, I, T, k, bits, seed=E + T, skew=skew)
+    experts = [{p: _ql(e[p], 128, bits) for p in ("gate", "up", "down")} for e in exps]
+    lg = torch.from_numpy(logits).to(DEV)
+    blk = moe.MoEBlock(lambda t: lg, experts, k)
+    y = blk(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    ref_experts = [(_oracle_lin(e["gate"], H, I, 128, bits), _oracle_lin(e["up"], H, I, 128, bits),
+                    _oracle_lin(e["down"], I, H, 128, bits)) for e in exps]
+    ref = om.moe_mlp(x, logits, ref_experts, k)
+    assert max_rel_err(y, ref) < TOL
+
+
+def test_moe_shared_expert_prefill_vs_oracle():
+    E, H, I, T, k = 8, 256, 256, 192, 2
+    exps, logits, x, sh = _synthetic_case(E, H, I, T, k, 4, seed=5, shared=True)
+    gw = (np.random.default_rng(6).standard_normal((H, 1)) * 0.05).astype(np.float32)
+    experts = [{p: _ql(e[p], 128, 4) for p in ("gate", "up", "down")} for e in exps]
+    lg = torch.from_numpy(logits).to(DEV)
+    gwd = torch.from_numpy(gw).to(DEV)
+    blk = moe.MoEBlock(lambda t: lg, experts, k, True, {p: _ql(sh[p], 128, 4) for p in ("gate", "up", "down")},
+                       lambda t: t @ gwd)
+    y = blk(torch.from_numpy(x).to(DEV)).cpu().numpy()
+    lin = _oracle_lin
+    ref = om.moe_mlp(x, logits, [(lin(e["gate"], H, I, 128, 4), lin(e["up"], H, I, 128, 4),
+                                  lin(e["down"], I, H, 128, 4)) for e in exps], k, True,
+                     (lin(sh["gate"], H, I, 128, 4), lin(sh["up"], H, I, 128, 4), lin(sh["down"], I, H, 128, 4)),
+                     lambda t: t @ gw)
+    assert max_rel_err(y, ref) < TOL
+
+
+@pytest.mark.parametrize("T", [3, 333])
+def test_moe_block_is_deterministic(T):
+    exps, logits, x, _ = _synthetic_case(16, 512, 256, T, 4, 4, seed=T)
+    experts = [{p: _ql(e[p], 128, 4) for p in ("gate", "up", "down")} for e in exps]
+    lg = torch.from_numpy(logits).to(DEV)
+    blk = moe.MoEBlock(lambda t: lg, experts, 4)
+    xd = torch.from_numpy(x).to(DEV)
+    a = blk(xd)
+    b = blk(xd)
+    assert torch.equal(a, b)
+
+
+def test_moe_block_empty_batch():
+    exps, logits, x, _ = _synthetic_case(4, 256, 128, 1, 2, 4, seed=1)
+    experts = [{p: _ql(e[p], 128, 4) for p in ("gate", "up", "down")} for e in exps]
+    blk = moe.MoEBlock(lambda t: torch.zeros((0, 4), device=DEV), experts, 2)
+    y = blk(torch.zeros((0, 256), device=DEV))
+    assert y.shape == (0, 256)
+
+
+def test_moe_step_replays_in_a_cuda_graph():
+    exps, logits, x, _ = _synthetic_case(32, 512, 256, 4, 4, 4, seed=9)
+    experts = [{p: _ql(e[p], 128, 4) for p in ("gate", "up", "down")} for e in exps]
+    lg = torch.from_numpy(logits).to(DEV)
+    blk = moe.MoEBlock(lambda t: lg, experts, 4)
+    xd = torch.from_numpy(x).to(DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ref = blk(xd)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = blk(xd)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)

@@ -109,10 +109,17 @@ def test_moe_vs_reference(name):
     d = golden(name)
     E, top_k, H, I, gs, bits = (int(d[k]) for k in ("E", "top_k", "H", "I", "gs", "bits"))
 
-    def lin(e, k, Kin, Nout):
-        qw, qz, sc = (d["e%d_%s_%s" % (e, k, f)] for f in ("qweight", "qzeros", "scales"))
+    def lin(pre, k, Kin, Nout):
+        qw, qz, sc = (d["%s_%s_%s" % (pre, k, f)] for f in ("qweight", "qzeros", "scales"))
         return lambda x: og.quantized_linear(x, qw, qz, sc, None, Kin, Nout, Kin, Nout, gs, bits, 1.0)
 
-    experts = [(lin(e, "gate", H, I), lin(e, "up", H, I), lin(e, "down", I, H)) for e in range(E)]
-    y = om.moe_mlp(d["x"], d["logits"], experts, top_k)
+    experts = [(lin("e%d" % e, "gate", H, I), lin("e%d" % e, "up", H, I), lin("e%d" % e, "down", I, H))
+               for e in range(E)]
+    shared = shared_gate = None
+    if "SI" in d:
+        SI = int(d["SI"])
+        shared = (lin("shared", "gate", H, SI), lin("shared", "up", H, SI), lin("shared", "down", SI, H))
+        shared_gate = (lambda x: x @ d["shared_gate_w"])
+    norm = bool(int(d["norm_topk_prob"])) if "norm_topk_prob" in d else True
+    y = om.moe_mlp(d["x"], d["logits"], experts, top_k, norm, shared, shared_gate)
     assert max_rel_err(y, d["y"]) < 1e-6

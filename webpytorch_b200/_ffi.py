@@ -36,6 +36,15 @@ SIGNATURES = {
     "ql_gptq_matmul_noalloc_max_scratch": (ctypes.c_size_t, []),
     "ql_q4k_dequant": (_c_int, [_vp, _vp, _c_int, _c_int, _vp]),
     "ql_q4k_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp]),
+    "ql_moe_route": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                              _vp, _vp, _c_int, _vp, _vp, _vp]),
+    "ql_moe_grouped_workspace": (ctypes.c_size_t, [_c_long, _c_int, _c_int, _c_int]),
+    "ql_moe_grouped_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _c_long, _vp, _vp, _vp, _c_int, _c_int, _vp,
+                                       _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_long, _c_int,
+                                       _c_int, _c_int, _c_int, _c_float, _vp, ctypes.c_size_t, _vp]),
+    "ql_moe_act": (_c_int, [_vp, _c_long, _c_int, _vp, _c_int, _vp]),
+    "ql_moe_combine": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_long, _vp, _c_long, _vp, _c_int,
+                                _c_long, _vp]),
 }
 
 LAUNCH_PDL = 1

@@ -23,7 +23,7 @@ __device__ __forceinline__ int chunk_pos(int j) {
 // 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats.
 template <class Args>
 __device__ __forceinline__ void load_x8(const Args& a, int m, int k, float (&v)[8]) {
-  const long base = (long)m * a.ldx;
+  const long base = (long)(a.x_rows ? a.x_rows[m] : m) * a.ldx;   // x_rows: gather of token rows
   if (a.x_perm == nullptr && a.x_vec) {
     if (a.x_dtype == QL_F16) {
       const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(a.x) + base + k);

@@ -50,13 +50,14 @@ constexpr int kEpilogueWarp0 = 8;
 // ---------------------------------------------------------------------------------------
 template <int BITS>
 __global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x, int x_dtype, long ldx,
-                                                     const int32_t* __restrict__ perm, int M, int K,
+                                                     const int32_t* __restrict__ perm,
+                                                     const int32_t* __restrict__ row_map, int M, int K,
                                                      __half* __restrict__ x16, int* __restrict__ row_exp) {
   __shared__ float wmax[8];
   __shared__ int sh_e;
   const int m = blockIdx.x;
   const int tid = threadIdx.x;
-  const long base = (long)m * ldx;
+  const long base = (long)(row_map ? row_map[m] : m) * ldx;   // row_map: MoE token gather
   float mx = 0.f;
   for (int k = tid; k < K; k += blockDim.x) {
     const int src = perm ? perm[k] : k;
@@ -104,7 +105,31 @@ struct GemmArgs {
   int M, K, N, gs;
   float zoff;
   int n_wtiles, n_ttiles;
+  // grouped (MoE) mode when tiles != NULL: token tile i is rows [offsets[e] + r, offsets[e + 1])
+  // capped at BT rows, with (e, r) = tiles[2i], tiles[2i + 1]; *n_tiles tiles are valid
+  const int32_t* tiles;
+  const int32_t* n_tiles;
+  const int32_t* offsets;
+  long qw_estride, qz_estride, sc_estride;
 };
+
+// Rows of token tile `tt` and the expert whose weights it uses.
+struct TileRows {
+  int row0, row_end, e;
+};
+__device__ __forceinline__ TileRows tile_rows(const GemmArgs& a, int tt, int BT) {
+  TileRows r;
+  if (a.tiles) {
+    r.e = a.tiles[2 * tt];
+    r.row0 = a.offsets[r.e] + a.tiles[2 * tt + 1];
+    r.row_end = a.offsets[r.e + 1];
+  } else {
+    r.e = 0;
+    r.row0 = tt * BT;
+    r.row_end = a.M;
+  }
+  return r;
+}
 
 template <int BT, int NS>
 struct SmemLayout {
@@ -189,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int nslab = a.K / kSlabK;
-  const int ntiles = a.n_wtiles * a.n_ttiles;
+  const int ntiles = a.n_wtiles * (a.tiles ? *a.n_tiles : a.n_ttiles);
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -197,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        const int tt = tile / a.n_wtiles;
+        const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
           if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) {
@@ -205,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::mbar_arrive_expect_tx(x_full(s), L::kStageBytes);
-          ptx::tma_load_2d(sbase + L::kXOff + s * L::kStageBytes, &tmap_x, x_full(s), kb * kSlabK, tt * BT);
+          ptx::tma_load_2d(sbase + L::kXOff + s * L::kStageBytes, &tmap_x, x_full(s), kb * kSlabK, tr.row0);
         }
       }
       if (!ok) {  // let the copies already in flight land before the CTA releases its smem
@@ -254,9 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = wt * kTileN + lrow;
       const bool ok = n < a.N;
       const int nn = ok ? n : 0;
+      const int e = a.tiles ? a.tiles[2 * (tile / a.n_wtiles)] : 0;
+      const uint32_t* qw = a.qw + (size_t)e * a.qw_estride;
+      const uint32_t* qz = a.qz + (size_t)e * a.qz_estride;
+      const char* scb = reinterpret_cast<const char*>(a.sc) + (size_t)e * a.sc_estride * (a.sc_dtype == QL_F32 ? 4 : 2);
       uint32_t w[ROWS];
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(a.qw + (long)r * a.N + nn) : 0u;
+      for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(qw + (long)r * a.N + nn) : 0u;
       for (int kb = 0; kb < nslab; ++kb, ++it) {
         const int s = it % NS;
         // scale and zero of this slab's group(s): a slab of 64 never straddles a group of >= 64,
@@ -269,8 +298,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           float scv = 0.f;
           uint32_t z = 0;
           if (ok) {
-            scv = load_as_float(a.sc, a.sc_dtype, (long)g * a.N + nn);
-            z = (a.qz[(long)g * (a.N / PER) + nn / PER] >> (BITS * (nn % PER))) & MASK;
+            scv = load_as_float(scb, a.sc_dtype, (long)g * a.N + nn);
+            z = (qz[(long)g * (a.N / PER) + nn / PER] >> (BITS * (nn % PER))) & MASK;
           }
           const float zf = (float)z + a.zoff;
           zlo[h] = h2_as_u32(__float2half2_rn(1024.f + zf));
@@ -290,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // prefetch the next slab's packed words (next tile's first slab after the last)
         if (kb + 1 < nslab) {
 #pragma unroll
-          for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(a.qw + (long)((kb + 1) * ROWS + r) * a.N + nn) : 0u;
+          for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(qw + (long)((kb + 1) * ROWS + r) * a.N + nn) : 0u;
         }
         if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) goto done;
         ptx::tmem_st32(lane_addr + A_COL + s * TCOLS_A, v);
@@ -306,7 +335,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     int tcount = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
-      const int wt = tile % a.n_wtiles, tt = tile / a.n_wtiles;
+      const int wt = tile % a.n_wtiles;
+      const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
       const int n = wt * kTileN + lrow;
       const float b = (a.bias && n < a.N) ? a.bias[n] : 0.f;
       if (!ptx::mbar_wait(d_full, tcount & 1, abort_flag)) goto done;
@@ -323,8 +353,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n < a.N) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int tok = tt * BT + c * 32 + j;
-            if (tok < a.M) {
+            const int tok = tr.row0 + c * 32 + j;
+            if (tok < tr.row_end) {
               const float val = __uint_as_float(v[j]) * exp2i(a.row_exp[tok]) + b;
               store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + n, val);
             }
@@ -391,7 +421,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, cudaStream_t st) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     configured_dev = dev;
   }
-  const int ntiles = a.n_wtiles * a.n_ttiles;
+  const int ntiles = a.n_wtiles * a.n_ttiles;   // grouped mode: n_ttiles is the table's capacity
   const int grid = ntiles < sms ? ntiles : sms;
   kern<<<grid, kThreads, smem, st>>>(tmap, a);
   return cuda_status(cudaGetLastError(), "gptq_gemm_tc launch");
@@ -433,12 +463,12 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
   __half* x16 = reinterpret_cast<__half*>(ws);
   int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * K * 2 + 255) & ~(size_t)255));
   if (bits == 4)
-    prep_x_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, M, K, x16, row_exp);
+    prep_x_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, nullptr, M, K, x16, row_exp);
   else
-    prep_x_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, M, K, x16, row_exp);
+    prep_x_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, nullptr, M, K, x16, row_exp);
   int rc = cuda_status(cudaGetLastError(), "prep_x launch");
   if (!rc) {
-    GemmArgs a;
+    GemmArgs a = {};
     a.qw = reinterpret_cast<const uint32_t*>(qweight);
     a.qz = reinterpret_cast<const uint32_t*>(qzeros);
     a.sc = scales; a.sc_dtype = sc_dtype; a.bias = bias; a.row_exp = row_exp;
@@ -458,6 +488,50 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
     if (!rc) rc = rc2;
   }
   return rc;
+}
+
+// Grouped (MoE) GEMM over P permuted rows: x rows gathered through row_map, experts' weights
+// strided by *_estride elements, tiles from the device-built table (capacity max_tiles).
+int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_map, int P, const int32_t* qweight,
+                      const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
+                      long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
+                      int max_tiles, int tile_rows_n, void* out, int out_dtype, long ldo, int K, int N, int gs,
+                      int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  if (K % kSlabK != 0 || (gs % 64 != 0 && gs != 32)) {
+    set_error("grouped GEMM: K=%d must be a multiple of 64 and gs=%d a multiple of 64 or 32", K, gs);
+    return QL_ERR_UNSUPPORTED;
+  }
+  if (tile_rows_n != 128 && tile_rows_n != 256) {
+    set_error("grouped GEMM: tile rows must be 128 or 256 (got %d)", tile_rows_n);
+    return QL_ERR_ARG;
+  }
+  const size_t need = gptq_gemm_workspace(P, K);
+  if (!workspace || ws_bytes < need) {
+    set_error("grouped GEMM: workspace of %zu bytes needed", need);
+    return QL_ERR_ARG;
+  }
+  __half* x16 = reinterpret_cast<__half*>(workspace);
+  int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + (((size_t)P * K * 2 + 255) & ~(size_t)255));
+  if (P == 0) return QL_OK;
+  if (bits == 4)
+    prep_x_kernel<4><<<P, 256, 0, st>>>(x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp);
+  else
+    prep_x_kernel<8><<<P, 256, 0, st>>>(x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp);
+  int rc = cuda_status(cudaGetLastError(), "prep_x launch");
+  if (rc) return rc;
+  GemmArgs a = {};
+  a.qw = reinterpret_cast<const uint32_t*>(qweight);
+  a.qz = reinterpret_cast<const uint32_t*>(qzeros);
+  a.sc = scales; a.sc_dtype = sc_dtype; a.bias = nullptr; a.row_exp = row_exp;
+  a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
+  a.M = P; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
+  a.n_wtiles = (N + kTileN - 1) / kTileN;
+  a.n_ttiles = max_tiles;
+  a.tiles = tiles; a.n_tiles = n_tiles; a.offsets = offsets;
+  a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
+  if (tile_rows_n == 128)
+    return bits == 4 ? launch_gemm<4, 128, 8>(a, x16, st) : launch_gemm<8, 128, 8>(a, x16, st);
+  return bits == 4 ? launch_gemm<4, 256, 4>(a, x16, st) : launch_gemm<8, 256, 4>(a, x16, st);
 }
 
 int take_tc_status() {

@@ -91,6 +91,7 @@ constexpr int kCtaCols = kNW * 32;
 
 struct GemvArgs {
   const void* x;
+  const int32_t* x_rows;   // NULL, or token row of x for each staged row (MoE gather)
   const int32_t* x_perm;
   long ldx;
   int x_dtype;
@@ -110,6 +111,12 @@ struct GemvArgs {
   int cs;       // cluster size along K (== gridDim.x), a power of two
   int lg_cs;
   float zoff;
+  // grouped (MoE) mode, when moe_offsets != NULL: blockIdx.z picks an active expert, whose
+  // rows [offsets[e], offsets[e + 1]) of x/out are processed in chunks of 8 * MT
+  const int32_t* moe_offsets;
+  const int32_t* moe_active;
+  const int32_t* moe_n_active;
+  long qw_estride, qz_estride, sc_estride;   // elements between consecutive experts
 };
 
 // Register-resident batch of UG consecutive groups of one lane's weights, scales and zeros.
@@ -246,7 +253,40 @@ __device__ __forceinline__ void compute_batch(const WBatch<BITS, GS>& B, float (
 }
 
 template <int BITS, int GS, int MT>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a);
+
+template <int BITS, int GS, int MT, bool GROUPED>
 __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a) {
+  if constexpr (!GROUPED) {
+    gemv_body<BITS, GS, MT>(a);
+    return;
+  }
+  // grouped experts: every CTA of a cluster shares blockIdx.z, so these exits are cluster-uniform
+  const int slot = blockIdx.z;
+  if (slot >= *a.moe_n_active) return;
+  const int e = a.moe_active[slot];
+  const int r0 = a.moe_offsets[e];
+  const int ne = a.moe_offsets[e + 1] - r0;
+  const int xsz = a.x_dtype == QL_F32 ? 4 : 2, osz = a.out_dtype == QL_F32 ? 4 : 2;
+  const int ssz = a.sc_dtype == QL_F32 ? 4 : 2;
+  GemvArgs c = a;
+  c.qw = a.qw + (size_t)e * a.qw_estride;
+  c.qz = a.qz + (size_t)e * a.qz_estride;
+  c.sc = reinterpret_cast<const char*>(a.sc) + (size_t)e * a.sc_estride * ssz;
+  for (int m0 = 0; m0 < ne; m0 += 8 * MT) {
+    c.M = min(8 * MT, ne - m0);
+    if (a.x_rows) {
+      c.x_rows = a.x_rows + r0 + m0;
+    } else {
+      c.x = reinterpret_cast<const char*>(a.x) + (size_t)(r0 + m0) * a.ldx * xsz;
+    }
+    c.out = reinterpret_cast<char*>(a.out) + (size_t)(r0 + m0) * a.ldo * osz;
+    gemv_body<BITS, GS, MT>(c);
+  }
+}
+
+template <int BITS, int GS, int MT>
+__device__ __forceinline__ void gemv_body(const GemvArgs& a) {
   using W = WBatch<BITS, GS>;
   constexpr int UG = W::UG;
   constexpr int MAXM = 8 * MT;
@@ -367,9 +407,9 @@ __global__ void __launch_bounds__(kNW * 32, 4) gptq_gemv_kernel(const GemvArgs a
   }
 }
 
-template <int BITS, int GS, int MT>
-int launch_gemv(const GemvArgs& a, cudaStream_t st) {
-  auto kern = gptq_gemv_kernel<BITS, GS, MT>;
+template <int BITS, int GS, int MT, bool GROUPED>
+int launch_gemv(const GemvArgs& a, cudaStream_t st, int zdim) {
+  auto kern = gptq_gemv_kernel<BITS, GS, MT, GROUPED>;
   const int ng_max = (a.G + a.cs - 1) / a.cs;
   const size_t xs_bytes = ((size_t)a.M * ng_max * GS * 2 + 15) & ~(size_t)15;
   const size_t gs_bytes = ((size_t)a.M * ng_max * 8 + 15) & ~(size_t)15;
@@ -391,7 +431,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
     configured_dev = dev;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.cs, (a.N + kCtaCols - 1) / kCtaCols, 1);
+  cfg.gridDim = dim3(a.cs, (a.N + kCtaCols - 1) / kCtaCols, zdim);
   cfg.blockDim = dim3(kNW * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -412,16 +452,18 @@ int launch_gemv(const GemvArgs& a, cudaStream_t st) {
 }
 
 template <int BITS, int GS>
-int dispatch_mt(const GemvArgs& a, cudaStream_t st) {
-  return a.M <= 8 ? launch_gemv<BITS, GS, 1>(a, st) : launch_gemv<BITS, GS, 2>(a, st);
+int dispatch_mt(const GemvArgs& a, cudaStream_t st, int zdim) {
+  if (a.moe_offsets)
+    return a.M <= 8 ? launch_gemv<BITS, GS, 1, true>(a, st, zdim) : launch_gemv<BITS, GS, 2, true>(a, st, zdim);
+  return a.M <= 8 ? launch_gemv<BITS, GS, 1, false>(a, st, zdim) : launch_gemv<BITS, GS, 2, false>(a, st, zdim);
 }
 
 template <int BITS>
-int dispatch_gs(const GemvArgs& a, int kgs, cudaStream_t st) {
+int dispatch_gs(const GemvArgs& a, int kgs, cudaStream_t st, int zdim) {
   switch (kgs) {
-    case 32: return dispatch_mt<BITS, 32>(a, st);
-    case 64: return dispatch_mt<BITS, 64>(a, st);
-    default: return dispatch_mt<BITS, 128>(a, st);
+    case 32: return dispatch_mt<BITS, 32>(a, st, zdim);
+    case 64: return dispatch_mt<BITS, 64>(a, st, zdim);
+    default: return dispatch_mt<BITS, 128>(a, st, zdim);
   }
 }
 
@@ -448,7 +490,7 @@ int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const
     return trc;
   // kernel group: the largest of {128, 64, 32} dividing the checkpoint's group size
   const int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
-  GemvArgs a;
+  GemvArgs a = {};
   a.x = x; a.x_perm = x_perm; a.ldx = ldx; a.x_dtype = x_dtype;
   const int vec_elems = x_dtype == QL_F32 ? 4 : 8;
   a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
@@ -480,7 +522,46 @@ int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const
   while (cs < 16 && cs < a.G && (size_t)M * ((a.G + cs - 1) / cs) * kgs * 2 > 96 * 1024) cs *= 2;
   a.cs = cs;
   a.lg_cs = 31 - __builtin_clz(cs);
-  return bits == 4 ? dispatch_gs<4>(a, kgs, st) : dispatch_gs<8>(a, kgs, st);
+  return bits == 4 ? dispatch_gs<4>(a, kgs, st, 1) : dispatch_gs<8>(a, kgs, st, 1);
+}
+
+// Grouped (MoE) decode GEMV: one launch over every active expert. rows_per_expert_max bounds the
+// rows any single expert holds (chooses 8- or 16-row chunks); max_active bounds the z extent.
+int gptq_gemv_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_rows, const int32_t* qweight,
+                      const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
+                      long sc_estride, const int32_t* offsets, const int32_t* active, const int32_t* n_active,
+                      int max_active, int rows_hint, void* out, int out_dtype, long ldo, int K, int N, int gs,
+                      int bits, float zoff, cudaStream_t st) {
+  const int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
+  GemvArgs a = {};
+  a.x = x; a.x_rows = x_rows; a.x_perm = nullptr; a.ldx = ldx; a.x_dtype = x_dtype;
+  const int vec_elems = x_dtype == QL_F32 ? 4 : 8;
+  a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
+  a.qw = reinterpret_cast<const uint32_t*>(qweight);
+  a.qz = reinterpret_cast<const uint32_t*>(qzeros);
+  a.sc = scales; a.sc_dtype = sc_dtype; a.bias = nullptr;
+  a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
+  a.M = rows_hint <= 8 ? 8 : 16;   // chunk size: selects MT and sizes shared memory
+  a.K = K; a.N = N;
+  a.G = K / kgs;
+  a.gs_mult = gs / kgs;
+  a.lg_gs_mult = (a.gs_mult & (a.gs_mult - 1)) == 0 ? 31 - __builtin_clz(a.gs_mult) : -1;
+  a.zoff = zoff;
+  a.moe_offsets = offsets; a.moe_active = active; a.moe_n_active = n_active;
+  a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int cta_cols = (N + kCtaCols - 1) / kCtaCols;
+  const int target = sms * 4;
+  const int per = cta_cols * (max_active > 0 ? max_active : 1);
+  int cs = pow2_floor(target / per > 0 ? target / per : 1);
+  if (cs > 8) cs = 8;
+  while (cs > 1 && cs > a.G) cs /= 2;
+  while (cs < 16 && cs < a.G && (size_t)a.M * ((a.G + cs - 1) / cs) * kgs * 2 > 96 * 1024) cs *= 2;
+  a.cs = cs;
+  a.lg_cs = 31 - __builtin_clz(cs);
+  return bits == 4 ? dispatch_gs<4>(a, kgs, st, max_active) : dispatch_gs<8>(a, kgs, st, max_active);
 }
 
 }  // namespace ql

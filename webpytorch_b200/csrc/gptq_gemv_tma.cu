@@ -46,6 +46,7 @@ constexpr int kStageK = 128;           // K per ring stage
 
 struct TmaGemvArgs {
   const void* x;
+  const int32_t* x_rows;   // unused here (always null): row gathers take the register-fed kernel
   const int32_t* x_perm;
   long ldx;
   int x_dtype;
@@ -494,7 +495,7 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
     return false;
   const int kgs = gs % 128 == 0 ? 128 : gs;
   TmaGemvArgs a;
-  a.x = x; a.x_perm = x_perm; a.ldx = ldx; a.x_dtype = x_dtype;
+  a.x = x; a.x_rows = nullptr; a.x_perm = x_perm; a.ldx = ldx; a.x_dtype = x_dtype;
   const int vec_elems = x_dtype == QL_F32 ? 4 : 8;
   a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
   a.sc_dtype = sc_dtype; a.bias = bias;

@@ -26,6 +26,7 @@ namespace ql {
 namespace {
 
 constexpr int kMaxTopK = 16;
+constexpr int kMaxExperts = 1024;
 
 __global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int norm,
                                 int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
@@ -87,41 +88,65 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, 
   }
 }
 
-// One CTA: offsets (exclusive scan), active expert list, tile table for the grouped GEMM
-// (tiles of `tile_rows` rows per expert), cursors reset.
-__global__ void moe_scan_kernel(const int32_t* __restrict__ counts, int E, int tile_rows, int32_t* __restrict__ offsets,
-                                int32_t* __restrict__ cursor, int32_t* __restrict__ active, int32_t* __restrict__ n_active,
-                                int32_t* __restrict__ tiles, int32_t* __restrict__ n_tiles, int max_tiles) {
-  __shared__ int s_cnt[1024];
-  __shared__ int s_tile[1024];
-  const int tid = threadIdx.x;
-  for (int base = 0; base < E; base += blockDim.x) {
-    // E <= blockDim.x is the common case; the loop keeps larger E correct
-  }
-  if (tid == 0) {
-    int off = 0, na = 0, nt = 0;
-    for (int e = 0; e < E; ++e) {
-      const int c = counts[e];
-      offsets[e] = off;
-      cursor[e] = 0;
-      if (c > 0) {
-        active[na++] = e;
-        for (int r = 0; r < c; r += tile_rows) {
-          if (nt < max_tiles) {
-            tiles[2 * nt] = e;
-            tiles[2 * nt + 1] = r;
-          }
-          ++nt;
-        }
-      }
-      off += c;
+// One CTA, one thread per expert (E <= 1024): block-wide exclusive scans of the row counts
+// (-> segment offsets), of the active flags (-> compact active-expert list) and of the tile
+// counts (-> the grouped GEMM's tile table of `tile_rows`-row tiles); scatter cursors reset.
+__global__ void __launch_bounds__(1024) moe_scan_kernel(const int32_t* __restrict__ counts, int E, int tile_rows,
+                                                        int32_t* __restrict__ offsets, int32_t* __restrict__ cursor,
+                                                        int32_t* __restrict__ active, int32_t* __restrict__ n_active,
+                                                        int32_t* __restrict__ tiles, int32_t* __restrict__ n_tiles,
+                                                        int max_tiles) {
+  __shared__ int s_tot[3][32];
+  const int e = threadIdx.x, lane = e & 31, w = e >> 5, nw = (blockDim.x + 31) >> 5;
+  const int c = e < E ? counts[e] : 0;
+  const int v[3] = {c, c > 0 ? 1 : 0, (c + tile_rows - 1) / tile_rows};
+  int inc[3] = {v[0], v[1], v[2]};
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int t = __shfl_up_sync(0xffffffffu, inc[q], o);
+      if (lane >= o) inc[q] += t;
     }
-    offsets[E] = off;
-    *n_active = na;
-    *n_tiles = nt < max_tiles ? nt : max_tiles;
   }
-  (void)s_cnt;
-  (void)s_tile;
+  if (lane == 31)
+    for (int q = 0; q < 3; ++q) s_tot[q][w] = inc[q];
+  __syncthreads();
+  if (w == 0) {
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      const int own = lane < nw ? s_tot[q][lane] : 0;
+      int x = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += t;
+      }
+      if (lane < nw) s_tot[q][lane] = x - own;   // exclusive warp base
+    }
+  }
+  __syncthreads();
+  int ex[3];
+#pragma unroll
+  for (int q = 0; q < 3; ++q) ex[q] = s_tot[q][w] + inc[q] - v[q];
+  if (e < E) {
+    offsets[e] = ex[0];
+    cursor[e] = 0;
+    if (c > 0) active[ex[1]] = e;
+    for (int i = 0; i < v[2]; ++i) {
+      const int ti = ex[2] + i;
+      if (ti < max_tiles) {
+        tiles[2 * ti] = e;
+        tiles[2 * ti + 1] = i * tile_rows;
+      }
+    }
+    if (e == E - 1) {
+      offsets[E] = ex[0] + c;
+      *n_active = ex[1] + v[1];
+      const int nt = ex[2] + v[2];
+      *n_tiles = nt < max_tiles ? nt : max_tiles;
+    }
+  }
 }
 
 __global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int T, int k, const int32_t* __restrict__ offsets,
@@ -148,16 +173,23 @@ __global__ void moe_act_kernel(const float* __restrict__ y, long P, int I, void*
   }
 }
 
-// out[t, h] = sum_j w[t, j] * z[pair_row[t, j], h]
+// out[t, h] = sum_j w[t, j] * z[pair_row[t, j], h]  (+ g[t] * shared[t, h], g = sigmoid of the
+// shared-expert gate logit when given, else 1)
 __global__ void moe_combine_kernel(const float* __restrict__ z, const int32_t* __restrict__ pair_row,
-                                   const float* __restrict__ topk_w, int T, int k, int H, void* __restrict__ out,
-                                   int out_dtype, long ldo) {
+                                   const float* __restrict__ topk_w, int T, int k, int H,
+                                   const float* __restrict__ shared, long lds, const float* __restrict__ shared_gate,
+                                   long ldg, void* __restrict__ out, int out_dtype, long ldo) {
   const long total = (long)T * H;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int t = (int)(i / H);
     const int h = (int)(i - (long)t * H);
     float acc = 0.f;
     for (int j = 0; j < k; ++j) acc = fmaf(topk_w[(long)t * k + j], z[(long)pair_row[(long)t * k + j] * H + h], acc);
+    if (shared) {
+      float g = 1.f;
+      if (shared_gate) g = 1.0f / (1.0f + expf(-shared_gate[(long)t * ldg]));
+      acc += g * shared[(long)t * lds + h];
+    }
     store_from_float(out, out_dtype, (long)t * ldo + h, acc);
   }
 }
@@ -171,8 +203,10 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
                             int32_t* topk_idx, float* topk_w, int32_t* counts, int32_t* offsets, int32_t* cursor,
                             int32_t* active, int32_t* n_active, int32_t* tiles, int32_t* n_tiles, int max_tiles,
                             int32_t* row_token, int32_t* pair_row, void* stream) {
-  if (T < 0 || E <= 0 || top_k <= 0 || top_k > E || top_k > kMaxTopK || tile_rows <= 0) {
-    set_error("ql_moe_route: bad sizes (T=%d E=%d top_k=%d, top_k <= %d)", T, E, top_k, kMaxTopK);
+  if (T < 0 || E <= 0 || E > kMaxExperts || top_k <= 0 || top_k > E || top_k > kMaxTopK || tile_rows <= 0 ||
+      max_tiles < 0) {
+    set_error("ql_moe_route: bad sizes (T=%d E=%d top_k=%d; E <= %d, top_k <= %d)", T, E, top_k, kMaxExperts,
+              kMaxTopK);
     return QL_ERR_ARG;
   }
   if (!logits || !topk_idx || !topk_w || !counts || !offsets || !cursor || !active || !n_active || !tiles ||
@@ -187,8 +221,8 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
     moe_topk_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, T, E, top_k, norm_topk_prob, topk_idx, topk_w, counts);
     if ((rc = cuda_status(cudaGetLastError(), "moe_topk launch"))) return rc;
   }
-  moe_scan_kernel<<<1, 32, 0, st>>>(counts, E, tile_rows, offsets, cursor, active, n_active, tiles, n_tiles,
-                                    max_tiles);
+  moe_scan_kernel<<<1, (E + 31) & ~31, 0, st>>>(counts, E, tile_rows, offsets, cursor, active, n_active, tiles,
+                                                n_tiles, max_tiles);
   if ((rc = cuda_status(cudaGetLastError(), "moe_scan launch"))) return rc;
   if (T > 0) {
     const int pairs = T * top_k;
@@ -213,9 +247,10 @@ extern "C" int ql_moe_act(const float* y, long P, int I, void* a, int a_dtype, v
 }
 
 extern "C" int ql_moe_combine(const float* z, const int32_t* pair_row, const float* topk_w, int T, int top_k, int H,
-                              void* out, int out_dtype, long ldo, void* stream) {
+                              const float* shared, long lds, const float* shared_gate, long ldg, void* out,
+                              int out_dtype, long ldo, void* stream) {
   if (T < 0 || top_k <= 0 || H <= 0 || !z || !pair_row || !topk_w || !out || ldo < H || out_dtype < QL_F32 ||
-      out_dtype > QL_BF16) {
+      out_dtype > QL_BF16 || (shared && lds < H) || (shared_gate && (!shared || ldg < 1))) {
     set_error("ql_moe_combine: bad arguments");
     return QL_ERR_ARG;
   }
@@ -223,6 +258,87 @@ extern "C" int ql_moe_combine(const float* z, const int32_t* pair_row, const flo
   const long total = (long)T * H;
   const long blocks = (total + 255) / 256;
   moe_combine_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, (cudaStream_t)stream>>>(
-      z, pair_row, topk_w, T, top_k, H, out, out_dtype, ldo);
+      z, pair_row, topk_w, T, top_k, H, shared, lds, shared_gate, ldg, out, out_dtype, ldo);
   return cuda_status(cudaGetLastError(), "moe_combine launch");
+}
+
+namespace ql {
+int gptq_gemv_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_rows, const int32_t* qweight,
+                      const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
+                      long sc_estride, const int32_t* offsets, const int32_t* active, const int32_t* n_active,
+                      int max_active, int rows_hint, void* out, int out_dtype, long ldo, int K, int N, int gs,
+                      int bits, float zoff, cudaStream_t st);
+int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_map, int P, const int32_t* qweight,
+                      const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
+                      long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
+                      int max_tiles, int tile_rows_n, void* out, int out_dtype, long ldo, int K, int N, int gs,
+                      int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st);
+size_t gptq_gemm_workspace(int M, int K);
+}  // namespace ql
+
+// True when a grouped call over P rows and E experts takes the tensor-core GEMM: the average
+// active expert then holds enough rows to fill a good part of a 128-row tile.
+static bool grouped_uses_gemm(long P, int E, int K, int gs) {
+  static int min_avg = -1;
+  if (min_avg < 0) min_avg = env_int("QL_MOE_GEMM_MIN_ROWS", 32);
+  const long act = P < E ? P : E;
+  return act > 0 && P >= (long)min_avg * act && K % 64 == 0 && (gs % 64 == 0 || gs == 32);
+}
+
+extern "C" size_t ql_moe_grouped_workspace(long P, int E, int K, int gs) {
+  return grouped_uses_gemm(P, E, K, gs) ? gptq_gemm_workspace((int)P, K) : 0;
+}
+
+extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int32_t* row_token, long P,
+                                     const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                     int scales_dtype, int E, const int32_t* offsets, const int32_t* active,
+                                     const int32_t* n_active, const int32_t* tiles, const int32_t* n_tiles,
+                                     int max_tiles, int tile_rows, int max_rows_per_expert, void* out, int out_dtype,
+                                     long ldo, int K, int N, int gs, int bits, float zero_offset, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  if (bits != 4 && bits != 8) {
+    set_error("ql_moe_grouped_matmul: bits must be 4 or 8 (got %d)", bits);
+    return QL_ERR_UNSUPPORTED;
+  }
+  const int per = 32 / bits;
+  if (P < 0 || P > 0x7fffffffL || E <= 0 || K <= 0 || N <= 0 || gs <= 0 || K % gs || gs % per || N % 8 ||
+      ldx < K || ldo < N || max_rows_per_expert < 0) {
+    set_error("ql_moe_grouped_matmul: bad sizes (P=%ld E=%d K=%d N=%d gs=%d; N %% 8 == 0, gs | K)", P, E, K, N, gs);
+    return QL_ERR_ARG;
+  }
+  if (gs % 32 != 0 || (zero_offset != 0.f && zero_offset != 1.f)) {
+    set_error("ql_moe_grouped_matmul: gs %% 32 == 0 and zero_offset in {0, 1} are supported");
+    return QL_ERR_UNSUPPORTED;
+  }
+  if ((x_dtype != QL_F32 && x_dtype != QL_F16 && x_dtype != QL_BF16) ||
+      (out_dtype != QL_F32 && out_dtype != QL_F16 && out_dtype != QL_BF16) ||
+      (scales_dtype != QL_F32 && scales_dtype != QL_F16 && scales_dtype != QL_BF16)) {
+    set_error("ql_moe_grouped_matmul: unknown dtype code");
+    return QL_ERR_ARG;
+  }
+  if (!x || !qweight || !qzeros || !scales || !offsets || !active || !n_active || !out) {
+    set_error("ql_moe_grouped_matmul: null pointer");
+    return QL_ERR_ARG;
+  }
+  if ((reinterpret_cast<uintptr_t>(qweight) | reinterpret_cast<uintptr_t>(scales)) & 15) {
+    set_error("ql_moe_grouped_matmul: qweight and scales must be 16-byte aligned");
+    return QL_ERR_ALIGN;
+  }
+  if (P == 0) return QL_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const long qw_es = (long)(K / per) * N, qz_es = (long)(K / gs) * (N / per), sc_es = (long)(K / gs) * N;
+  if (grouped_uses_gemm(P, E, K, gs)) {
+    if (!tiles || !n_tiles || max_tiles <= 0) {
+      set_error("ql_moe_grouped_matmul: the tensor-core path needs the routing tile table");
+      return QL_ERR_ARG;
+    }
+    int rc = gptq_gemm_grouped(x, x_dtype, ldx, row_token, (int)P, qweight, qzeros, scales, scales_dtype, qw_es,
+                               qz_es, sc_es, offsets, tiles, n_tiles, max_tiles, tile_rows, out, out_dtype, ldo, K,
+                               N, gs, bits, zero_offset, workspace, workspace_bytes, st);
+    if (rc != QL_ERR_UNSUPPORTED) return rc;
+  }
+  const int max_active = (int)(P < E ? P : E);
+  return gptq_gemv_grouped(x, x_dtype, ldx, row_token, qweight, qzeros, scales, scales_dtype, qw_es, qz_es, sc_es,
+                           offsets, active, n_active, max_active, max_rows_per_expert, out, out_dtype, ldo, K, N, gs,
+                           bits, zero_offset, st);
 }
