@@ -57,6 +57,179 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+MOE_E, MOE_TOPK, MOE_H, MOE_I = 128, 8, 2048, 768
+MOE_TOKENS = (1, 32, 256, 2048)
+Q4K_K, Q4K_N, Q4K_MS, Q4K_COPIES = 4096, 14336, (1, 8, 64), 8
+
+
+def rand_gptq(K, N, dev, g, E=None, bits=4):
+    """Config-0 distributions on the device: uniform packed words, fp16 scales U[0.002, 0.02]."""
+    per = 32 // bits
+    lead = () if E is None else (E,)
+    qw = torch_mod().randint(-2 ** 31, 2 ** 31 - 1, lead + (K // per, N), dtype=torch_mod().int32, device=dev,
+                             generator=g)
+    qz = torch_mod().randint(-2 ** 31, 2 ** 31 - 1, lead + (K // GS, N // per), dtype=torch_mod().int32,
+                             device=dev, generator=g)
+    sc = (torch_mod().rand(lead + (K // GS, N), device=dev, generator=g) * 0.018 + 0.002).half()
+    return qw, qz, sc
+
+
+def rand_q4k(N, K, dev, g):
+    """Config-2 super-blocks on the device: uniform bytes, then fp16 d and dmin U[1e-3, 1e-2]."""
+    torch = torch_mod()
+    nb = N * (K // 256)
+    raw = torch.randint(0, 256, (nb, 144), dtype=torch.uint8, device=dev, generator=g)
+    dd = (torch.rand((nb, 2), device=dev, generator=g) * 9e-3 + 1e-3).half()
+    raw[:, 0:4] = dd.view(torch.uint8).reshape(nb, 4)
+    return raw.reshape(N, (K // 256) * 144).contiguous()
+
+
+def torch_mod():
+    import torch
+    return torch
+
+
+def event_time(fn, reps):
+    """Average device ms of fn() over reps calls (CUDA events on the current stream)."""
+    torch = torch_mod()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def bench_moe(dev, g, hbm, bf16_peak):
+    """Config 4: Qwen3-MoE-shaped block (128 experts, top-8, H=2048, I=768, int4 g128, bf16 x).
+    Each timed step is a CUDA graph over L independent layers (own experts, logits and x) so
+    that the active experts' weights come from HBM, not L2."""
+    torch = torch_mod()
+    from webpytorch_b200 import moe
+    out = {}
+    for T in MOE_TOKENS:
+        L = 8 if T <= 256 else 2
+        layers = []
+        for _ in range(L):
+            gu = moe.StackedExperts.from_packed(*rand_gptq(MOE_H, 2 * MOE_I, dev, g, E=MOE_E), GS, 4)
+            dn = moe.StackedExperts.from_packed(*rand_gptq(MOE_I, MOE_H, dev, g, E=MOE_E), GS, 4)
+            logits = torch.randn((T, MOE_E), device=dev, generator=g)
+            blk = moe.MoEBlock.from_stacked(lambda t, _l=logits: _l, gu, dn, MOE_TOPK)
+            x = torch.randn((T, MOE_H), device=dev, generator=g).to(torch.bfloat16)
+            layers.append((blk, x, logits))
+        act = sum(int(torch.topk(lg, MOE_TOPK, dim=1).indices.unique().numel()) for _, _, lg in layers)
+
+        def fwd():
+            for blk, x, _ in layers:
+                blk(x)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fwd()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                fwd()
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            gr.replay()
+        reps = 50 if T <= 256 else 10
+        ms = event_time(gr.replay, reps) / L
+        exp_bytes = layers[0][0].gate_up.expert_nbytes() + layers[0][0].down.expert_nbytes()
+        wbytes = act / L * exp_bytes
+        flops = 2.0 * T * MOE_TOPK * (MOE_H * 2 * MOE_I + MOE_I * MOE_H)
+        r = {"us": round(ms * 1e3, 2), "tokens/s": round(T / (ms / 1e3), 1),
+             "active_experts": round(act / L, 2), "expert_GB/s": round(wbytes / (ms / 1e3) / 1e9, 1),
+             "expert_frac_of_hbm": round(wbytes / (ms / 1e3) / 1e9 / hbm, 4),
+             "TFLOP/s": round(flops / (ms / 1e3) / 1e12, 1),
+             "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / bf16_peak, 4), "layers_per_graph": L}
+        out["T%d" % T] = r
+        del gr, layers
+        torch.cuda.empty_cache()
+    return out
+
+
+def bench_q4k(dev, g, hbm):
+    """Config 2: Q4_K dequant-GEMV/GEMM, K=4096, N=14336, fp32 x, M in {1, 8, 64}; rotating copies."""
+    torch = torch_mod()
+    from webpytorch_b200.ggml import ggml_matmul
+    raws = [rand_q4k(Q4K_N, Q4K_K, dev, g) for _ in range(Q4K_COPIES)]
+    res = {}
+    for M in Q4K_MS:
+        x = torch.randn((M, Q4K_K), device=dev, generator=g)
+        y = torch.empty((M, Q4K_N), device=dev)
+
+        def run():
+            for r in raws:
+                ggml_matmul(x, r, "Q4_K", Q4K_K, Q4K_N, out=y)
+        gr = torch.cuda.CUDAGraph()
+        run()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gr):
+            run()
+        for _ in range(3):
+            gr.replay()
+        ms = event_time(gr.replay, 20) / Q4K_COPIES
+        nbytes = raws[0].numel() + M * Q4K_K * 4 + M * Q4K_N * 4
+        res["M%d" % M] = {"us": round(ms * 1e3, 2), "GB/s": round(nbytes / (ms / 1e3) / 1e9, 1),
+                          "frac_of_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm, 4)}
+        del gr
+    return res
+
+
+def profile_case(name):
+    """A small, fixed launch sequence of one kernel for `ncu` (few launches, a few GB at most;
+    inputs larger than L2 where the kernel streams weights)."""
+    torch = torch_mod()
+    from webpytorch_b200 import _ffi
+    from webpytorch_b200.qlinear import QuantizedLinear, _gptq_matmul
+    dev = torch.device("cuda", 0)
+    _ffi.load(build_if_missing=False)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    if name == "gemv":                       # gptq_gemv_tma_kernel, 4096 x 14336, M=1, 6 copies (176 MB)
+        K, N = 4096, 14336
+        ws = [rand_gptq(K, N, dev, g) for _ in range(6)]
+        x = torch.randn((1, K), device=dev, generator=g).half()
+        y = torch.empty((1, N), device=dev)
+        for qw, qz, sc in ws:
+            _gptq_matmul(x, qw, qz, sc, K, N, GS, 4, 1.0, out=y)
+    elif name == "gemm":                     # prep_x_kernel + gptq_gemm_tc_kernel, config 3 shape 1
+        K, N, M = 4096, 11008, 2048
+        qw, qz, sc = rand_gptq(K, N, dev, g)
+        gidx = (torch.arange(K, device=dev) // GS)[torch.randperm(K, device=dev, generator=g)]
+        ql = QuantizedLinear.from_autogptq(qw, qz, sc, None, GS, 4, g_idx=gidx, device=dev)
+        x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+        yb = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            ql(x, out=yb, out_dtype=torch.bfloat16)
+    elif name in ("moe_decode", "moe_prefill"):   # config 4, T = 32 (grouped GEMV) / 2048 (grouped GEMM)
+        from webpytorch_b200 import moe
+        T = 32 if name == "moe_decode" else 2048
+        gu = moe.StackedExperts.from_packed(*rand_gptq(MOE_H, 2 * MOE_I, dev, g, E=MOE_E), GS, 4)
+        dn = moe.StackedExperts.from_packed(*rand_gptq(MOE_I, MOE_H, dev, g, E=MOE_E), GS, 4)
+        logits = torch.randn((T, MOE_E), device=dev, generator=g)
+        blk = moe.MoEBlock.from_stacked(lambda t: logits, gu, dn, MOE_TOPK)
+        x = torch.randn((T, MOE_H), device=dev, generator=g).to(torch.bfloat16)
+        for _ in range(2):
+            blk(x)
+    elif name == "q4k":                      # q4k_gemv_kernel, config 2, M=1, 8 copies (264 MB)
+        from webpytorch_b200.ggml import ggml_matmul
+        raws = [rand_q4k(Q4K_N, Q4K_K, dev, g) for _ in range(Q4K_COPIES)]
+        x = torch.randn((1, Q4K_K), device=dev, generator=g)
+        y = torch.empty((1, Q4K_N), device=dev)
+        for r in raws:
+            ggml_matmul(x, r, "Q4_K", Q4K_K, Q4K_N, out=y)
+    else:
+        raise SystemExit("unknown profile case %r" % name)
+    torch.cuda.synchronize()
+    rc = _ffi.load().ql_device_status()
+    print(json.dumps({"profile_case": name, "device_status": rc}))
+    return 1 if rc else 0
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons, sampled in the background."""
 
@@ -189,8 +362,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--skip-extra", action="store_true", help="skip the config-2 and config-4 sections")
+    ap.add_argument("--profile", default=None,
+                    help="run one small fixed case for ncu: gemv | gemm | moe_decode | moe_prefill | q4k")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.profile:
+        return profile_case(args.profile)
     if args.impl == "reference":
         return run_reference(args)
 
@@ -281,30 +459,37 @@ def main():
         clocks = sampler.summary(t0, t1)
     ms_plain, _, _ = timed(graph_plain.replay, args.steps)
 
-    # ---- per-shape launch durations: a graph of 40 launches per shape (10 passes over the
-    # 4 copies, so each launch still reads its weights from HBM), timed with CUDA events
+    # ---- per-shape launch durations: a graph of 10 passes over >= 320 MB of one shape's
+    # weight copies (each launch reads its weights from HBM), timed with CUDA events
     per_shape = {}
     for (K, N) in SHAPES:
         Ls = [L for L in lay if (L[0], L[1]) == (K, N)]
+        # rotate over at least 320 MB of this shape's weights so no launch finds them in L2
+        extra = max(0, -(-320_000_000 // gemv_bytes(K, N)) - len(Ls))
+        for _ in range(extra):
+            qw, qz, sc = rand_gptq(K, N, dev, g)
+            Ls.append((K, N, qw, qz, sc, Ls[0][5], Ls[0][6]))
+        nl = 10 * len(Ls)
         res = {}
         for pdl in (False, True):
             _ffi.set_launch_flags(_ffi.LAUNCH_PDL if pdl else 0)
             gr = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gr):
-                for i in range(40):
+                for i in range(nl):
                     launch(Ls[i % len(Ls)])
             _ffi.set_launch_flags(0)
             gr.replay()
             torch.cuda.synchronize()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for _ in range(10):
+            for _ in range(3):
                 gr.replay()
             e1.record()
             torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / 400
+            us = e0.elapsed_time(e1) * 1e3 / (3 * nl)
             res["pdl" if pdl else "plain"] = us
             del gr
+        del Ls
         per_shape["%dx%d" % (K, N)] = {"us": round(res["pdl"], 3), "us_plain": round(res["plain"], 3),
                                        "GB/s": round(gemv_bytes(K, N) / res["pdl"] / 1e3, 1),
                                        "GB/s_plain": round(gemv_bytes(K, N) / res["plain"] / 1e3, 1)}
@@ -357,6 +542,12 @@ def main():
             del ql, qw, qz, sc, x, yb
         torch.cuda.empty_cache()
 
+    moe_res, q4k_res = {}, {}
+    if not args.skip_extra:
+        hbm0, bf0, _ = peaks()
+        q4k_res = bench_q4k(dev, g, hbm0)
+        moe_res = bench_moe(dev, g, hbm0, bf0)
+
     tot_bytes = step_bytes() * args.steps * world
     value = tot_bytes / (ms / 1e3) / 1e9
     value_plain = tot_bytes / (ms_plain / 1e3) / 1e9
@@ -384,6 +575,14 @@ def main():
         "gemm": {"workload": "config3: int4 g128 desc_act dequant-GEMM, bf16 x/out, M=%d (act-order gather "
                              "+ fp16 staging + tcgen05 GEMM per call)" % GEMM_M,
                  "bound": "tensor", "peak_TFLOP/s": peaks()[1], "shapes": gemm},
+        "q4k": {"workload": "config2: Q4_K K=%d N=%d fp32 x/out, %d rotating copies (%.0f MB)"
+                            % (Q4K_K, Q4K_N, Q4K_COPIES, Q4K_COPIES * Q4K_N * Q4K_K / 256 * 144 / 1e6),
+                "bound": "hbm", "M": q4k_res},
+        "moe": {"workload": "config4: %d experts top-%d, H=%d I=%d, int4 g128, bf16 x, device routing + "
+                            "grouped gate|up + act + grouped down + combine per layer, CUDA graph over "
+                            "independent layers" % (MOE_E, MOE_TOPK, MOE_H, MOE_I),
+                "expert_GB/s basis": "active experts' packed weights+scales+zeros per layer / layer time",
+                "T": moe_res},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "QuantizedLinear boundary (_gptq_matmul via ctypes) with pinned host x/y copies"},

@@ -28,7 +28,8 @@ def route(logits, top_k, norm_topk_prob=True):
 def silu(x):
     """x * sigmoid(x) (webtorch/_core.py:502-503), in float32."""
     x = np.asarray(x, np.float32)
-    return (x * (1.0 / (1.0 + np.exp(-x)))).astype(np.float32)
+    with np.errstate(over="ignore"):         # exp(-x) -> inf gives silu -> -0, as in the reference
+        return (x * (1.0 / (1.0 + np.exp(-x)))).astype(np.float32)
 
 
 def moe_mlp(x, logits, experts, top_k, norm_topk_prob=True, shared=None, shared_gate=None):

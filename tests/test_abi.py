@@ -97,6 +97,7 @@ def test_moe_entry_points_reject_bad_arguments(lib):
     for T, E, k in [(4, 1025, 2), (4, 8, 9), (4, 64, 17), (-1, 8, 2)]:
         assert lib.ql_moe_route(p[0], T, E, k, 1, 128, *p[:9], 4, *p[:2], None) == 1
     assert lib.ql_moe_route(p[0], 4, 8, 2, 1, 128, *p[:9], 4, None, p[0], None) == 1   # null buffer
+    assert lib.ql_moe_route(None, 4, 8, 2, 1, 128, *p[:9], 4, *p[:2], None) == 1
 
     def gm(**kw):
         a = dict(x=16, x_dtype=0, ldx=256, P=8, qw=16, sc=16, sc_dtype=1, E=4, K=256, N=64, gs=128, bits=4,

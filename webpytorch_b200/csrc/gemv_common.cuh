@@ -177,6 +177,156 @@ __device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half*
   sync();
 }
 
+// Stage x[:, kbase : kbase + klen] for M <= 16 tokens as the B operand of the integer MMA
+// (mma.m16n8k32, A = u8 weights, B = s8 activations):
+//   * each token row is scaled by an exact power of two, v = rint(x * 2^-e) with |v| <= 2^14
+//     (sh_exp[m] = e), and split into two signed bytes v = 256 * hi + lo, which become two
+//     MMA columns ("slots" 2m and 2m + 1) so that one MMA yields both partial dot products;
+//   * the MMA K order follows the weight unpack. An int4 packed row r (K = 8r .. 8r+7) is
+//     unpacked into bytes of even offsets (MMA k 4t + i <- K 8r + 2i) and odd offsets (MMA k
+//     16 + 4t + i <- K 8r + 2i + 1), lane t of a 32-K step taking row 4s + t. An int8 packed row
+//     (K = 4r .. 4r+3) is a register as it is: rows 8s + t and 8s + 4 + t feed MMA k 4t + i and
+//     16 + 4t + i;
+//   * xb[(s * 4 + t) * 2M + slot] holds lane t's two B registers of step s for that slot;
+//   * gsum[m * gstride + g] = sum of v over group g (exact integers), for the zero point.
+// sh_max must be zero and visible before the call.
+template <int BITS, int GS, bool NAMED, class Args>
+__device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint2* xb, int* gsum, int* sh_exp,
+                           unsigned* sh_max, int tid, int nthr) {
+  constexpr int CH = 4;          // 8-value chunks a thread keeps in registers on the one-pass path
+  constexpr int SEG = GS / 8;    // chunks per group (lanes reduced together)
+  const int M = a.M;
+  const int slots = 2 * M;
+  auto sync = [&]() {
+    if constexpr (NAMED) {
+      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    } else {
+      __syncthreads();
+    }
+  };
+  const int cpr = klen / 8;
+  const int nchunk = M * cpr;
+  auto store_chunk = [&](int idx, const float (&v)[8]) {
+    const int m = idx / cpr, kc = idx - m * cpr;
+    const float s = exp2i(-sh_exp[m]);
+    uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int q = __float2int_rn(v[j] * s);
+      const int l = (int)(int8_t)(q & 0xff);
+      const int h = (q - l) >> 8;
+      sum += q;
+      // int4: even offsets -> register 0, odd -> register 1; int8: first row -> 0, second -> 1
+      const int reg = BITS == 4 ? (j & 1) : (j >> 2);
+      const int byte = BITS == 4 ? (j >> 1) : (j & 3);
+      hi[reg] |= (uint32_t)(h & 0xff) << (8 * byte);
+      lo[reg] |= (uint32_t)(l & 0xff) << (8 * byte);
+    }
+    if constexpr (BITS == 4) {
+      const int s4 = kc >> 2, t = kc & 3;
+      uint2* dst = xb + (s4 * 4 + t) * slots + 2 * m;
+      dst[0] = make_uint2(hi[0], hi[1]);
+      dst[1] = make_uint2(lo[0], lo[1]);
+    } else {
+      const int r0 = 2 * kc;                // rows r0, r0 + 1 of the same half of a step
+      const int s8 = r0 >> 3, j = r0 & 7;
+      const int half = j >> 2, t0 = j & 3;
+      uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * slots + 2 * m) + half;
+      uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * slots + 2 * m) + half;
+      d0[0] = hi[0];
+      d0[2] = lo[0];
+      d1[0] = hi[1];
+      d1[2] = lo[1];
+    }
+    // the SEG chunks of one group sit in SEG consecutive lanes
+#pragma unroll
+    for (int o = SEG / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if ((kc % SEG) == 0) gsum[m * gstride + kc / SEG] = sum;
+  };
+  auto row_max = [&](int m, float mx) { atomicMax(&sh_max[m], __float_as_uint(mx)); };
+  if (nchunk <= nthr * CH) {
+    float v[CH][8];
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (idx < nchunk) {
+        const int m = idx / cpr;
+        load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      float mx = 0.f;
+      if (idx < nchunk) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
+        if (mx != mx) mx = __int_as_float(0x7f800000);   // NaN counts as non-finite
+      }
+      const int base_idx = tid - (tid & 31) + c * nthr;
+      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;
+      if (uniform) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if ((tid & 31) == 0) row_max(base_idx / cpr, mx);
+      } else if (idx < nchunk) {
+        row_max(idx / cpr, mx);
+      }
+    }
+    sync();
+    if (tid < M) sh_exp[tid] = stage_exponent_i15(__uint_as_float(sh_max[tid]));
+    sync();
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int idx = tid + c * nthr;
+      if (tid - (tid & 31) + c * nthr < nchunk) {   // warp-uniform: whole groups per warp
+        float w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = idx < nchunk ? v[c][j] : 0.f;
+        if (idx < nchunk) store_chunk(idx, w);
+        else {
+          int z = 0;   // keep the group-sum shuffles converged
+#pragma unroll
+          for (int o = SEG / 2; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        }
+      }
+    }
+  } else {
+    for (int m = 0; m < M; ++m) {
+      float mx = 0.f;
+      for (int kc = tid; kc < cpr; kc += nthr) {
+        float v[8];
+        load_x8(a, m, kbase + kc * 8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+        if (mx != mx) mx = __int_as_float(0x7f800000);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if ((tid & 31) == 0) row_max(m, mx);
+    }
+    sync();
+    if (tid < M) sh_exp[tid] = stage_exponent_i15(__uint_as_float(sh_max[tid]));
+    sync();
+    for (int base = 0; base < nchunk; base += nthr) {
+      const int idx = base + tid;
+      if (base + (tid - (tid & 31)) < nchunk) {      // warp-uniform
+        float v[8];
+        if (idx < nchunk) {
+          const int m = idx / cpr;
+          load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
+          store_chunk(idx, v);
+        } else {
+          int z = 0;
+#pragma unroll
+          for (int o = SEG / 2; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+        }
+      }
+    }
+  }
+  sync();
+}
 
 }  // namespace gemv
 }  // namespace ql

@@ -76,15 +76,15 @@ struct TmaLayout {
   static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + abort flag
 };
 
-template <int BITS, int GS, int MT, int NST, int SCB>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BITS, int GS, int NQ, int NST, int SCB>
+__global__ void __launch_bounds__(kThreads, 2)
     gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                          const __grid_constant__ CUtensorMap tmap_z, const TmaGemvArgs a) {
   using L = TmaLayout<BITS, GS, NST, SCB>;
   constexpr int PER = L::PER;
   constexpr int GPS = L::GPS;
-  constexpr int SPG = GS / (4 * PER);                      // 4-row steps per group
-  constexpr int MAXM = 8 * MT;
+  constexpr int SPG = GS / 32;                             // 32-K MMA steps per group
+  constexpr int MAXM = 4 * NQ;
   constexpr uint32_t MASK = (1u << BITS) - 1u;
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -107,10 +107,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int klen_max = nst_max * kStageK;
   const int ng_max = nst_max * GPS;
   const int M = a.M, N = a.N;
-  __half* xs = reinterpret_cast<__half*>(smem + L::kXsOff);
+  uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
   const int xs_bytes = (M * klen_max * 2 + 15) & ~15;
-  float2* gsum = reinterpret_cast<float2*>(smem + L::kXsOff + xs_bytes);
-  const int gs_bytes = (M * ng_max * 8 + 15) & ~15;
+  int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
+  const int gs_bytes = (M * ng_max * 4 + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
 
   if (a.cs > 1) cluster_arrive_relaxed();
@@ -160,22 +160,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ consumer warps
+    // Lane (g, t) owns columns 4g .. 4g+3 of its warp's 32-column strip and, per token quad
+    // mq, token 4 mq + t. Integer MMA m16n8k32: rows g / g + 8 of tile 0 are columns 4g /
+    // 4g + 1, of tile 1 columns 4g + 2 / 4g + 3; MMA columns 2t / 2t + 1 are the high / low
+    // activation bytes of token t.
     const int gq = lane >> 2, t = lane & 3;
     const int lcol = warp * 32 + gq * 4;                    // first of this lane's 4 columns
     const int c0 = blockIdx.y * kTileCols + lcol;
     const bool col_ok = c0 < N;
+    const int slots = 2 * M;
+    const int zoff = (int)a.zoff;
     pdl_wait();   // x may be the previous kernel's output
-    gemv::stage_x<BITS, GS, true>(a, s0 * kStageK, klen, ng_max, xs, gsum, sh_exp, sh_max, tid, kCW * 32);
+    gemv::stage_x_i8<BITS, GS, true>(a, s0 * kStageK, klen, ng_max, xb, gsum, sh_exp, sh_max, tid, kCW * 32);
 
-    float acc[2][MT][4];
+    float acc[NQ][4];
 #pragma unroll
-    for (int p = 0; p < 2; ++p)
+    for (int mq = 0; mq < NQ; ++mq)
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[p][mt][i] = 0.f;
+      for (int c = 0; c < 4; ++c) acc[mq][c] = 0.f;
 
     const uint32_t strip_off = warp * L::kStripBytes;
+    const uint32_t xb_base = ptx::smem_addr(xb);
     for (int i = 0; i < nst; ++i) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
@@ -183,7 +188,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       const unsigned char* stp = smem + s * L::kStageBytes;
 #pragma unroll
       for (int u = 0; u < GPS; ++u) {
-        // this group's scales and zeros for the lane's 4 columns
+        int d[NQ][2][4];
+#pragma unroll
+        for (int mq = 0; mq < NQ; ++mq)
+#pragma unroll
+          for (int p = 0; p < 2; ++p)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) d[mq][p][q] = 0;
+#pragma unroll
+        for (int sp = 0; sp < SPG; ++sp) {
+          const int step = (i * GPS + u) * SPG + sp;                // 32-K step inside the slice
+          uint32_t A0[4], A1[4];                                    // tile 0 / tile 1 A registers
+          if constexpr (BITS == 4) {
+            const int row = (u * SPG + sp) * 4 + t;                 // packed row inside the stage
+            const uint32_t addr = st + strip_off + row * 128 + ((gq ^ (row & 7)) << 4);
+            uint4 w;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                         : "r"(addr));
+            // even K offsets of each word -> bytes of register 0, odd -> register 1
+            A0[0] = w.x & 0x0F0F0F0Fu; A0[1] = w.y & 0x0F0F0F0Fu;
+            A0[2] = (w.x >> 4) & 0x0F0F0F0Fu; A0[3] = (w.y >> 4) & 0x0F0F0F0Fu;
+            A1[0] = w.z & 0x0F0F0F0Fu; A1[1] = w.w & 0x0F0F0F0Fu;
+            A1[2] = (w.z >> 4) & 0x0F0F0F0Fu; A1[3] = (w.w >> 4) & 0x0F0F0F0Fu;
+          } else {
+            const int r0 = (u * SPG + sp) * 8 + t, r1 = r0 + 4;
+            const uint32_t ad0 = st + strip_off + r0 * 128 + ((gq ^ (r0 & 7)) << 4);
+            const uint32_t ad1 = st + strip_off + r1 * 128 + ((gq ^ (r1 & 7)) << 4);
+            uint4 w, v;
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(w.x), "=r"(w.y), "=r"(w.z), "=r"(w.w)
+                         : "r"(ad0));
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                         : "r"(ad1));
+            A0[0] = w.x; A0[1] = w.y; A0[2] = v.x; A0[3] = v.y;
+            A1[0] = w.z; A1[1] = w.w; A1[2] = v.z; A1[3] = v.w;
+          }
+#pragma unroll
+          for (int mq = 0; mq < NQ; ++mq) {
+            const int slot = 8 * mq + gq;
+            uint32_t b0 = 0u, b1 = 0u;
+            if (slot < slots) {
+              const uint32_t xa = xb_base + ((step * 4 + t) * slots + slot) * 8;
+              asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
+            }
+            mma_16832_u8s8(d[mq][0], A0[0], A0[1], A0[2], A0[3], b0, b1);
+            mma_16832_u8s8(d[mq][1], A1[0], A1[1], A1[2], A1[3], b0, b1);
+          }
+        }
+        // fold the group: acc += scale * (C - (z + off) * S), C = 256 * hi + lo (exact)
+        const int gl = i * GPS + u;
         float scv[4];
         if constexpr (SCB == 2) {
           const uint2 h = *reinterpret_cast<const uint2*>(stp + L::kWBytes + (u * kTileCols + lcol) * 2);
@@ -201,141 +256,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t zw = *reinterpret_cast<const uint32_t*>(stp + L::kWBytes + L::kScBytes +
                                                                (u * (kTileCols / PER) + lcol / PER) * 4) >>
                             (BITS * (lcol % PER));
-        // two accumulator sets, alternating by step, halve the dependent MMA chain
-        float gacc2[2][2][MT][4];
+        int zo[4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int c = 0; c < 4; ++c) zo[c] = (int)((zw >> (BITS * c)) & MASK) + zoff;
 #pragma unroll
-          for (int p = 0; p < 2; ++p)
+        for (int mq = 0; mq < NQ; ++mq) {
+          const int tok = 4 * mq + t;
+          const int S = tok < M ? gsum[tok * ng_max + gl] : 0;
+          const int C[4] = {d[mq][0][0] * 256 + d[mq][0][1], d[mq][0][2] * 256 + d[mq][0][3],
+                            d[mq][1][0] * 256 + d[mq][1][1], d[mq][1][2] * 256 + d[mq][1][3]};
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-              for (int q = 0; q < 4; ++q) gacc2[h][p][mt][q] = 0.f;
-#pragma unroll
-        for (int sp = 0; sp < SPG; ++sp) {
-          float (&gacc)[2][MT][4] = gacc2[sp & 1];
-          const int row = (u * SPG + sp) * 4 + t;                  // packed row inside the stage
-          const uint32_t addr = st + strip_off + row * 128 + ((gq ^ (row & 7)) << 4);
-          uint4 wv;
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
-                       : "r"(addr));
-          const uint32_t wcol[4] = {wv.x, wv.y, wv.z, wv.w};
-          const int koff = i * kStageK + row * PER;                // offset inside the staged x slice
-          if constexpr (BITS == 4) {
-            uint32_t P[4][4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint32_t w8 = wcol[q] >> 8;
-              P[q][0] = lop3_andor(wcol[q], 0x000F000Fu, kMagicF16x2);
-              P[q][1] = lop3_andor(wcol[q], 0x00F000F0u, kMagicF16x2);
-              P[q][2] = lop3_andor(w8, 0x000F000Fu, kMagicF16x2);
-              P[q][3] = lop3_andor(w8, 0x00F000F0u, kMagicF16x2);
-            }
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const int tok = gq + 8 * mt;
-              uint4 xv = make_uint4(0, 0, 0, 0);
-              if (tok < M) xv = *reinterpret_cast<const uint4*>(xs + (long)tok * klen + koff);
-#pragma unroll
-              for (int p = 0; p < 2; ++p) {
-                mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
-                mma_16816_f16(gacc[p][mt], P[2 * p][2], P[2 * p + 1][2], P[2 * p][3], P[2 * p + 1][3], xv.z, xv.w);
-              }
-            }
-          } else {
-            uint32_t P[4][2];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              P[q][0] = lop3_andor(wcol[q], 0x00FF00FFu, kMagicF16x2);
-              P[q][1] = lop3_andor(wcol[q] >> 8, 0x00FF00FFu, kMagicF16x2);
-            }
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt) {
-              const int tok = gq + 8 * mt;
-              uint2 xv = make_uint2(0, 0);
-              if (tok < M) xv = *reinterpret_cast<const uint2*>(xs + (long)tok * klen + koff);
-#pragma unroll
-              for (int p = 0; p < 2; ++p)
-                mma_16816_f16(gacc[p][mt], P[2 * p][0], P[2 * p + 1][0], P[2 * p][1], P[2 * p + 1][1], xv.x, xv.y);
-            }
-          }
-        }
-        float gacc[2][MT][4];
-#pragma unroll
-        for (int p = 0; p < 2; ++p)
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) gacc[p][mt][q] = gacc2[0][p][mt][q] + gacc2[1][p][mt][q];
-        // acc += scale * (C - (1024 A + (z + off) S))
-        const int gl = i * GPS + u;
-        float zc[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) zc[q] = (float)((zw >> (BITS * q)) & MASK) + a.zoff;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          float A[2], S[2];
-#pragma unroll
-          for (int tk = 0; tk < 2; ++tk) {
-            const int tok = 8 * mt + 2 * t + tk;
-            const float2 as = tok < M ? gsum[tok * ng_max + gl] : make_float2(0.f, 0.f);
-            A[tk] = 1024.f * as.x;
-            S[tk] = as.y;
-          }
-#pragma unroll
-          for (int p = 0; p < 2; ++p)
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int col = 2 * p + (q >> 1), tk = q & 1;
-              const float v = gacc[p][mt][q] - fmaf(zc[col], S[tk], A[tk]);
-              acc[p][mt][q] = fmaf(scv[col], v, acc[p][mt][q]);
-            }
+          for (int c = 0; c < 4; ++c) acc[mq][c] = fmaf(scv[c], (float)(C[c] - zo[c] * S), acc[mq][c]);
         }
       }
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
     }
 
+    // non-finite activation rows give NaN (the integer staging cannot carry inf / nan)
+    auto finish = [&](int tok, float v) {
+      const float mx = __uint_as_float(sh_max[tok]);
+      return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+    };
     if (a.cs == 1) {
 #pragma unroll
-      for (int p = 0; p < 2; ++p)
+      for (int mq = 0; mq < NQ; ++mq) {
+        const int tok = 4 * mq + t;
+        if (tok < M && col_ok) {
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int tok = 8 * mt + 2 * t + (q & 1);
-            const int col = c0 + 2 * p + (q >> 1);
-            if (tok < M && col_ok) {
-              float v = acc[p][mt][q] * exp2i(sh_exp[tok]);
-              if (a.bias) v += a.bias[col];
-              store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
-            }
+          for (int c = 0; c < 4; ++c) {
+            float v = finish(tok, acc[mq][c]);
+            if (a.bias) v += a.bias[c0 + c];
+            store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + c0 + c, v);
           }
+        }
+      }
     } else {
       // partials pushed into the owning rank's shared memory (rank q owns columns
-      // [q * cpo, (q + 1) * cpo) of the CTA tile, cpo = 256 / cs)
+      // [ceil(q * 256 / cs), ceil((q + 1) * 256 / cs)) of the CTA tile)
       cg::cluster_group cluster = cg::this_cluster();
       const int cpo_max = (kTileCols + a.cs - 1) / a.cs;
       const int chunk = cpo_max * MAXM;
       __syncwarp();
       cluster_wait_acquire();
 #pragma unroll
-      for (int p = 0; p < 2; ++p)
+      for (int c = 0; c < 4; ++c) {
+        const int lc = lcol + c;
+        const int owner = (lc * a.cs) >> 8;
+        const int ostart = (owner * kTileCols + a.cs - 1) / a.cs;
+        float* dst = cluster.map_shared_rank(red, owner) + rank * chunk + (lc - ostart) * MAXM;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int lc = lcol + 2 * p + h;
-          const int owner = (lc * a.cs) >> 8;
-          const int ostart = (owner * kTileCols + a.cs - 1) / a.cs;
-          float* dst = cluster.map_shared_rank(red, owner) + rank * chunk + (lc - ostart) * MAXM;
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int tk = 0; tk < 2; ++tk) {
-              const int tok = 8 * mt + 2 * t + tk;
-              if (tok < M) dst[tok] = acc[p][mt][2 * h + tk] * exp2i(sh_exp[tok]);
-            }
+        for (int mq = 0; mq < NQ; ++mq) {
+          const int tok = 4 * mq + t;
+          if (tok < M) dst[tok] = finish(tok, acc[mq][c]);
         }
+      }
     }
   }
 
@@ -390,7 +365,7 @@ bool encode_2d(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const 
          CUDA_SUCCESS;
 }
 
-template <int BITS, int GS, int MT, int NST, int SCB>
+template <int BITS, int GS, int NQ, int NST, int SCB>
 int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qzeros, const void* scales,
                cudaStream_t st) {
   using L = TmaLayout<BITS, GS, NST, SCB>;
@@ -415,11 +390,11 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   if (!encode_2d(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, qzeros, a.N / L::PER, G, (uint64_t)(a.N / L::PER) * 4,
                  kTileCols / L::PER, L::GPS))
     return -1;
-  auto kern = gptq_gemv_tma_kernel<BITS, GS, MT, NST, SCB>;
+  auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB>;
   const int sq = a.nstage / a.cs;
   const int nst_max = sq + (a.nstage % a.cs ? 1 : 0);
   const size_t smem = 1024 + L::kXsOff + (((size_t)a.M * nst_max * kStageK * 2 + 15) & ~(size_t)15) +
-                      (((size_t)a.M * nst_max * L::GPS * 8 + 15) & ~(size_t)15) + (size_t)(kTileCols + 16) * 8 * MT * 4;
+                      (((size_t)a.M * nst_max * L::GPS * 4 + 15) & ~(size_t)15) + (size_t)(kTileCols + 16) * 4 * NQ * 4;
   if (smem > 200 * 1024) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -457,9 +432,12 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
 template <int BITS, int GS>
 int tma_mt(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
   constexpr int NST = BITS == 4 ? 4 : 3;
-  if (a.sc_dtype == QL_F32)
-    return a.M <= 8 ? launch_tma<BITS, GS, 1, NST, 4>(a, qw, qz, sc, st) : launch_tma<BITS, GS, 2, NST, 4>(a, qw, qz, sc, st);
-  return a.M <= 8 ? launch_tma<BITS, GS, 1, NST, 2>(a, qw, qz, sc, st) : launch_tma<BITS, GS, 2, NST, 2>(a, qw, qz, sc, st);
+  if (a.sc_dtype == QL_F32) {
+    if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 4>(a, qw, qz, sc, st);
+    return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 4>(a, qw, qz, sc, st) : launch_tma<BITS, GS, 4, NST, 4>(a, qw, qz, sc, st);
+  }
+  if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 2>(a, qw, qz, sc, st);
+  return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 2>(a, qw, qz, sc, st) : launch_tma<BITS, GS, 4, NST, 2>(a, qw, qz, sc, st);
 }
 
 template <int BITS>

@@ -209,8 +209,8 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
               kMaxTopK);
     return QL_ERR_ARG;
   }
-  if (!logits || !topk_idx || !topk_w || !counts || !offsets || !cursor || !active || !n_active || !tiles ||
-      !n_tiles || !row_token || !pair_row) {
+  if (!counts || !offsets || !cursor || !active || !n_active || !n_tiles || (max_tiles > 0 && !tiles) ||
+      (T > 0 && (!logits || !topk_idx || !topk_w || !row_token || !pair_row))) {
     set_error("ql_moe_route: null pointer");
     return QL_ERR_ARG;
   }
@@ -234,7 +234,7 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
 }
 
 extern "C" int ql_moe_act(const float* y, long P, int I, void* a, int a_dtype, void* stream) {
-  if (P < 0 || I <= 0 || !y || !a || a_dtype < QL_F32 || a_dtype > QL_BF16) {
+  if (P < 0 || I <= 0 || (P > 0 && (!y || !a)) || a_dtype < QL_F32 || a_dtype > QL_BF16) {
     set_error("ql_moe_act: bad arguments");
     return QL_ERR_ARG;
   }
@@ -249,8 +249,8 @@ extern "C" int ql_moe_act(const float* y, long P, int I, void* a, int a_dtype, v
 extern "C" int ql_moe_combine(const float* z, const int32_t* pair_row, const float* topk_w, int T, int top_k, int H,
                               const float* shared, long lds, const float* shared_gate, long ldg, void* out,
                               int out_dtype, long ldo, void* stream) {
-  if (T < 0 || top_k <= 0 || H <= 0 || !z || !pair_row || !topk_w || !out || ldo < H || out_dtype < QL_F32 ||
-      out_dtype > QL_BF16 || (shared && lds < H) || (shared_gate && (!shared || ldg < 1))) {
+  if (T < 0 || top_k <= 0 || H <= 0 || (T > 0 && (!z || !pair_row || !topk_w || !out)) || ldo < H ||
+      out_dtype < QL_F32 || out_dtype > QL_BF16 || (shared && lds < H) || (shared_gate && (!shared || ldg < 1))) {
     set_error("ql_moe_combine: bad arguments");
     return QL_ERR_ARG;
   }
@@ -316,7 +316,7 @@ extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const
     set_error("ql_moe_grouped_matmul: unknown dtype code");
     return QL_ERR_ARG;
   }
-  if (!x || !qweight || !qzeros || !scales || !offsets || !active || !n_active || !out) {
+  if (!qweight || !qzeros || !scales || !offsets || !active || !n_active || (P > 0 && (!x || !out))) {
     set_error("ql_moe_grouped_matmul: null pointer");
     return QL_ERR_ARG;
   }

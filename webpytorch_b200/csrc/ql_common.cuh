@@ -131,4 +131,24 @@ __device__ __forceinline__ int stage_exponent(float absmax) {
   return e;
 }
 
+// Exponent e such that m * 2^-e lies in [2^13, 2^14): activations staged as integers
+// rint(x * 2^-e) then fit 15 bits (|v| <= 2^14), which two signed bytes hold as 256 * hi + lo.
+// Clamped so that both 2^e and 2^-e are normal floats; zero / non-finite rows get 0.
+__device__ __forceinline__ int stage_exponent_i15(float absmax) {
+  if (!(absmax > 0.f) || !(absmax < 3.0e38f)) return 0;
+  int be = ((__float_as_int(absmax) >> 23) & 0xff) - 127;  // floor(log2(absmax)) for normals
+  int e = be - 13;
+  if (e < -110) e = -110;
+  if (e > 114) e = 114;
+  return e;
+}
+
+// integer MMA: D(16x8 s32) += A(16x32 u8, row) * B(32x8 s8, col)
+__device__ __forceinline__ void mma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 }  // namespace ql

@@ -75,9 +75,26 @@ class StackedExperts:
         self.qzeros = torch.stack(qzs).to(dev).contiguous()
         self.scales = torch.stack(scs).to(dev).contiguous()
 
+    @classmethod
+    def from_packed(cls, qweight, qzeros, scales, gs, bits, zero_offset=1.0):
+        """Wrap already-stacked device tensors: qweight [E, K/per, N], qzeros [E, K/gs, N/per],
+        scales [E, K/gs, N] (AutoGPTQ packing per expert)."""
+        self = cls.__new__(cls)
+        per = 32 // bits
+        self.E, kp, self.N = (int(v) for v in qweight.shape)
+        self.K, self.gs, self.bits, self.zoff = kp * per, int(gs), int(bits), float(zero_offset)
+        if tuple(qzeros.shape) != (self.E, self.K // gs, self.N // per) or \
+                tuple(scales.shape) != (self.E, self.K // gs, self.N):
+            raise ValueError("qzeros/scales shapes do not match qweight")
+        self.qweight, self.qzeros, self.scales = qweight.contiguous(), qzeros.contiguous(), scales.contiguous()
+        return self
+
     def nbytes(self):
         return int(self.qweight.numel() * 4 + self.qzeros.numel() * 4 +
                    self.scales.numel() * self.scales.element_size())
+
+    def expert_nbytes(self):
+        return self.nbytes() // self.E
 
 
 class Routing:
@@ -172,6 +189,17 @@ class MoEBlock(torch.nn.Module):
             sp = self._parts(shared)
             self.shared = (StackedExperts([sp], ("gate", "up"), dev), StackedExperts([sp], ("down",), dev))
             self.SI = self.shared[0].N // 2
+
+    @classmethod
+    def from_stacked(cls, gate, gate_up, down, top_k, norm_topk_prob=True):
+        """A block over pre-stacked StackedExperts (gate_up: [E] x [H -> 2I], down: [E] x [I -> H])."""
+        self = cls.__new__(cls)
+        torch.nn.Module.__init__(self)
+        self.router, self.top_k, self.norm_topk_prob = gate, int(top_k), bool(norm_topk_prob)
+        self.gate_up, self.down = gate_up, down
+        self.E, self.H, self.I = gate_up.E, gate_up.K, gate_up.N // 2
+        self.shared = self.shared_gate = None
+        return self
 
     @staticmethod
     def _parts(e):
