@@ -189,7 +189,7 @@ __device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half*
 //     16 + 4t + i;
 //   * xb[(s * 4 + t) * 2M + slot] holds lane t's two B registers of step s for that slot;
 //   * gsum[m * gstride + g] = sum of v over group g (exact integers), for the zero point.
-// sh_max must be zero and visible before the call.
+// sh_max must be zero and visible before the call; sh_exp is valid after it returns.
 template <int BITS, int GS, bool NAMED, class Args>
 __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint2* xb, int* gsum, int* sh_exp,
                            unsigned* sh_max, int tid, int nthr) {
@@ -207,8 +207,8 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint
   const int cpr = klen / 8;
   const int nchunk = M * cpr;
   auto store_chunk = [&](int idx, const float (&v)[8]) {
-    const int m = idx / cpr, kc = idx - m * cpr;
-    const float s = exp2i(-sh_exp[m]);
+    const int m = M == 1 ? 0 : idx / cpr, kc = idx - m * cpr;
+    const float s = exp2i(-stage_exponent_i15(__uint_as_float(sh_max[m])));
     uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
     int sum = 0;
 #pragma unroll
@@ -251,7 +251,7 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint
     for (int c = 0; c < CH; ++c) {
       const int idx = tid + c * nthr;
       if (idx < nchunk) {
-        const int m = idx / cpr;
+        const int m = M == 1 ? 0 : idx / cpr;
         load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
       }
     }
@@ -275,8 +275,9 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint
       }
     }
     sync();
+    // every thread derives its row's exponent from the maxima; sh_exp is read only after the
+    // final barrier
     if (tid < M) sh_exp[tid] = stage_exponent_i15(__uint_as_float(sh_max[tid]));
-    sync();
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
       const int idx = tid + c * nthr;
@@ -308,7 +309,6 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint
     }
     sync();
     if (tid < M) sh_exp[tid] = stage_exponent_i15(__uint_as_float(sh_max[tid]));
-    sync();
     for (int base = 0; base < nchunk; base += nthr) {
       const int idx = base + tid;
       if (base + (tid - (tid & 31)) < nchunk) {      // warp-uniform

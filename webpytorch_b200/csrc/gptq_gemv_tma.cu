@@ -39,10 +39,12 @@ int take_tma_gemv_status() {
 
 namespace {
 
-constexpr int kCW = 8;                 // consumer warps (one 32-column strip each)
+constexpr int kCW = 8;                 // consumer warps
 constexpr int kThreads = (kCW + 1) * 32;
-constexpr int kTileCols = kCW * 32;    // 256 columns per CTA
 constexpr int kStageK = 128;           // K per ring stage
+// A CTA covers SW 32-column strips (tile of 32 * SW columns); its kCW consumer warps are
+// SW strips x KW = kCW / SW ways along K (K-way j consumes the stages i with i % KW == j).
+// SW = 8 suits wide layers; SW = 4 doubles the CTAs of narrow ones so every SM gets two.
 
 struct TmaGemvArgs {
   const void* x;
@@ -59,28 +61,32 @@ struct TmaGemvArgs {
   int M, K, N, gs;
   int nstage;   // K / kStageK
   int cs;       // cluster size along K
+  int sw;       // 32-column strips per CTA (8 or 4; host-side choice)
   float zoff;
 };
 
-template <int BITS, int GS, int NST, int SCB>
+template <int BITS, int GS, int NST, int SCB, int SW>
 struct TmaLayout {
   static constexpr int PER = 32 / BITS;
+  static constexpr int TC = 32 * SW;                       // columns per CTA tile
   static constexpr int GPS = kStageK / GS;                 // groups per stage (>= 1)
   static constexpr int ROWS = kStageK / PER;               // packed rows per stage
   static constexpr int kStripBytes = ROWS * 128;
-  static constexpr int kWBytes = kCW * kStripBytes;        // 16 KB (int4) / 32 KB (int8)
-  static constexpr int kScBytes = GPS * kTileCols * SCB;   // scales of the stage
-  static constexpr int kZBytes = GPS * (kTileCols / PER) * 4;
+  static constexpr int kWBytes = SW * kStripBytes;         // 2 KB per strip (int4) / 4 KB (int8)
+  static constexpr int kScBytes = GPS * TC * SCB;          // scales of the stage
+  static constexpr int kZBytes = GPS * (TC / PER) * 4;
   static constexpr int kStageBytes = (kWBytes + kScBytes + kZBytes + 1023) & ~1023;
   static constexpr int kBarOff = NST * kStageBytes;
   static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + abort flag
 };
 
-template <int BITS, int GS, int NQ, int NST, int SCB>
+template <int BITS, int GS, int NQ, int NST, int SCB, int SW>
 __global__ void __launch_bounds__(kThreads, 2)
     gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                          const __grid_constant__ CUtensorMap tmap_z, const TmaGemvArgs a) {
-  using L = TmaLayout<BITS, GS, NST, SCB>;
+  using L = TmaLayout<BITS, GS, NST, SCB, SW>;
+  constexpr int TC = L::TC;
+  constexpr int KW = kCW / SW;
   constexpr int PER = L::PER;
   constexpr int GPS = L::GPS;
   constexpr int SPG = GS / 32;                             // 32-K MMA steps per group
@@ -95,6 +101,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_full = sbase + L::kBarOff;
   const uint32_t bar_empty = bar_full + 8 * NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kBarOff + 16 * NST);
+  const uint32_t bar_red = bar_full + 16 * NST + 8;   // partial sums received from the cluster
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -112,18 +119,30 @@ __global__ void __launch_bounds__(kThreads, 2)
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
   const int gs_bytes = (M * ng_max * 4 + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
+  // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16
+  float* kred = red + (TC + 64) * MAXM;   // K-way partials (KW == 2): [SW * 32 lanes][NQ * 4]
 
-  if (a.cs > 1) cluster_arrive_relaxed();
+  // Split-K reduction over the cluster: rank q owns the column quads [qs(q), qs(q + 1)) of
+  // the tile, qs(q) = ceil(q * Q / cs), Q = TC / 4; every rank sends each owner its partial
+  // sums for the owner's columns with 16-byte st.async stores that count down the owner's
+  // mbarrier, so each CTA waits only for the partials it reduces.
+  constexpr int Q = TC / 4;
+  const int cs = a.cs;
+  const int cq_max = (Q + cs - 1) / cs;                     // column quads per owner (max)
+  const int oq0 = (rank * Q + cs - 1) / cs, oq1 = ((rank + 1) * Q + cs - 1) / cs;
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) {
       ptx::mbar_init(bar_full + 8 * s, 1);
-      ptx::mbar_init(bar_empty + 8 * s, kCW);
+      ptx::mbar_init(bar_empty + 8 * s, SW);
     }
+    ptx::mbar_init(bar_red, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
+    if (cs > 1) ptx::mbar_arrive_expect_tx(bar_red, (uint32_t)(cs * M * (oq1 - oq0) * 16));
   }
   if (tid < 16) sh_max[tid] = 0u;
   __syncthreads();
+  if (cs > 1) cluster_arrive_relaxed();   // waited for before the first remote store
 
   if (warp == kCW) {
     // ------------------------------------------------------------ producer warp
@@ -131,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::tma_prefetch(&tmap_w);
       ptx::tma_prefetch(&tmap_s);
       ptx::tma_prefetch(&tmap_z);
-      const int strip0 = blockIdx.y * kCW;
+      const int strip0 = blockIdx.y * SW;
       int i = 0;
       bool ok = true;
       for (; i < nst; ++i) {
@@ -150,14 +169,16 @@ __global__ void __launch_bounds__(kThreads, 2)
             "[%2];" ::"r"(st),
             "l"(reinterpret_cast<uint64_t>(&tmap_w)), "r"(fb), "r"(0), "r"((s0 + i) * L::ROWS), "r"(strip0)
             : "memory");
-        ptx::tma_load_2d(st + L::kWBytes, &tmap_s, fb, blockIdx.y * kTileCols, srow);
-        ptx::tma_load_2d(st + L::kWBytes + L::kScBytes, &tmap_z, fb, blockIdx.y * (kTileCols / PER), srow);
+        ptx::tma_load_2d(st + L::kWBytes, &tmap_s, fb, blockIdx.y * TC, srow);
+        ptx::tma_load_2d(st + L::kWBytes + L::kScBytes, &tmap_z, fb, blockIdx.y * (TC / PER), srow);
       }
       if (nst <= NST) pdl_trigger();
       if (!ok) {
         for (int j = i > NST ? i - NST : 0; j < i; ++j) ptx::mbar_wait_drain(bar_full + 8 * (j % NST), (j / NST) & 1);
       }
     }
+    __syncwarp();
+    if (cs > 1) cluster_wait_acquire();   // pairs with the arrive above (every thread once)
   } else {
     // ------------------------------------------------------------ consumer warps
     // Lane (g, t) owns columns 4g .. 4g+3 of its warp's 32-column strip and, per token quad
@@ -165,8 +186,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     // 4g + 1, of tile 1 columns 4g + 2 / 4g + 3; MMA columns 2t / 2t + 1 are the high / low
     // activation bytes of token t.
     const int gq = lane >> 2, t = lane & 3;
-    const int lcol = warp * 32 + gq * 4;                    // first of this lane's 4 columns
-    const int c0 = blockIdx.y * kTileCols + lcol;
+    const int strip = warp % SW, kway = warp / SW;
+    const int lcol = strip * 32 + gq * 4;                   // first of this lane's 4 columns
+    const int c0 = blockIdx.y * TC + lcol;
     const bool col_ok = c0 < N;
     const int slots = 2 * M;
     const int zoff = (int)a.zoff;
@@ -179,9 +201,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[mq][c] = 0.f;
 
-    const uint32_t strip_off = warp * L::kStripBytes;
+    const uint32_t strip_off = strip * L::kStripBytes;
     const uint32_t xb_base = ptx::smem_addr(xb);
-    for (int i = 0; i < nst; ++i) {
+    for (int i = kway; i < nst; i += KW) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
       const uint32_t st = sbase + s * L::kStageBytes;
@@ -241,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int gl = i * GPS + u;
         float scv[4];
         if constexpr (SCB == 2) {
-          const uint2 h = *reinterpret_cast<const uint2*>(stp + L::kWBytes + (u * kTileCols + lcol) * 2);
+          const uint2 h = *reinterpret_cast<const uint2*>(stp + L::kWBytes + (u * TC + lcol) * 2);
           if (a.sc_dtype == QL_BF16) {
             scv[0] = __uint_as_float(h.x << 16); scv[1] = __uint_as_float(h.x & 0xffff0000u);
             scv[2] = __uint_as_float(h.y << 16); scv[3] = __uint_as_float(h.y & 0xffff0000u);
@@ -250,11 +272,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             scv[0] = f0.x; scv[1] = f0.y; scv[2] = f1.x; scv[3] = f1.y;
           }
         } else {
-          const float4 f = *reinterpret_cast<const float4*>(stp + L::kWBytes + (u * kTileCols + lcol) * 4);
+          const float4 f = *reinterpret_cast<const float4*>(stp + L::kWBytes + (u * TC + lcol) * 4);
           scv[0] = f.x; scv[1] = f.y; scv[2] = f.z; scv[3] = f.w;
         }
         const uint32_t zw = *reinterpret_cast<const uint32_t*>(stp + L::kWBytes + L::kScBytes +
-                                                               (u * (kTileCols / PER) + lcol / PER) * 4) >>
+                                                               (u * (TC / PER) + lcol / PER) * 4) >>
                             (BITS * (lcol % PER));
         int zo[4];
 #pragma unroll
@@ -273,16 +295,34 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
     }
 
+    if constexpr (KW == 2) {
+      // the second K-way hands its partial sums to the first through shared memory
+      float* kr = kred + (strip * 32 + lane) * (NQ * 4);
+      if (kway == 1) {
+#pragma unroll
+        for (int mq = 0; mq < NQ; ++mq)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) kr[mq * 4 + c] = acc[mq][c];
+      }
+      asm volatile("bar.sync 2, %0;" ::"r"(kCW * 32) : "memory");
+      if (kway == 0) {
+#pragma unroll
+        for (int mq = 0; mq < NQ; ++mq)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[mq][c] += kr[mq * 4 + c];
+      }
+    }
+    const bool writer = kway == 0;
     // non-finite activation rows give NaN (the integer staging cannot carry inf / nan)
     auto finish = [&](int tok, float v) {
       const float mx = __uint_as_float(sh_max[tok]);
       return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
     };
-    if (a.cs == 1) {
+    if (cs == 1) {
 #pragma unroll
       for (int mq = 0; mq < NQ; ++mq) {
         const int tok = 4 * mq + t;
-        if (tok < M && col_ok) {
+        if (writer && tok < M && col_ok) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float v = finish(tok, acc[mq][c]);
@@ -292,46 +332,41 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     } else {
-      // partials pushed into the owning rank's shared memory (rank q owns columns
-      // [ceil(q * 256 / cs), ceil((q + 1) * 256 / cs)) of the CTA tile)
-      cg::cluster_group cluster = cg::this_cluster();
-      const int cpo_max = (kTileCols + a.cs - 1) / a.cs;
-      const int chunk = cpo_max * MAXM;
       __syncwarp();
-      cluster_wait_acquire();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int lc = lcol + c;
-        const int owner = (lc * a.cs) >> 8;
-        const int ostart = (owner * kTileCols + a.cs - 1) / a.cs;
-        float* dst = cluster.map_shared_rank(red, owner) + rank * chunk + (lc - ostart) * MAXM;
+      cluster_wait_acquire();   // every CTA of the cluster has initialised its mbarriers
+      if (writer) {
+        const int lq = lcol >> 2;
+        const int owner = (lq * cs) / Q;
+        const int oq = (owner * Q + cs - 1) / cs;
+        const uint32_t rbase = ptx::mapa(ptx::smem_addr(red), owner);
+        const uint32_t rbar = ptx::mapa(bar_red, owner);
 #pragma unroll
         for (int mq = 0; mq < NQ; ++mq) {
           const int tok = 4 * mq + t;
-          if (tok < M) dst[tok] = finish(tok, acc[mq][c]);
+          if (tok < M) {
+            const uint32_t dst = rbase + (((rank * MAXM + tok) * cq_max + (lq - oq)) * 4) * 4;
+            ptx::st_async_v4(dst, finish(tok, acc[mq][0]), finish(tok, acc[mq][1]), finish(tok, acc[mq][2]),
+                             finish(tok, acc[mq][3]), rbar);
+          }
         }
       }
     }
   }
 
-  __syncwarp();  // cluster barriers are .aligned: every warp reaches them converged
-  if (a.cs > 1) {
-    if (warp == kCW) cluster_wait_acquire();   // the producer joins the cluster barrier phases
-    cluster_arrive_release();
-    cluster_wait_acquire();
-    const int cpo_max = (kTileCols + a.cs - 1) / a.cs;
-    const int chunk = cpo_max * MAXM;
-    const int ostart = (rank * kTileCols + a.cs - 1) / a.cs;
-    const int oend = ((rank + 1) * kTileCols + a.cs - 1) / a.cs;
-    const int cpo = oend - ostart;
-    for (int s = tid; s < cpo * M; s += blockDim.x) {
-      const int c = s / M, tok = s - c * M;
-      float v = 0.f;
-      for (int q = 0; q < a.cs; ++q) v += red[q * chunk + c * MAXM + tok];
-      const int col = blockIdx.y * kTileCols + ostart + c;
-      if (col < N) {
-        if (a.bias) v += a.bias[col];
-        store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
+  if (cs > 1) {
+    // reduce the owned columns over the ranks in rank order (deterministic) and store
+    const bool got = ptx::mbar_wait(bar_red, 0, abort_flag);
+    const int ncol = (oq1 - oq0) * 4;
+    if (got) {
+      for (int s = tid; s < ncol * M; s += blockDim.x) {
+        const int tok = s / ncol, c = s - tok * ncol;
+        float v = 0.f;
+        for (int q = 0; q < cs; ++q) v += red[(q * MAXM + tok) * cq_max * 4 + c];
+        const int col = blockIdx.y * TC + oq0 * 4 + c;
+        if (col < N) {
+          if (a.bias) v += a.bias[col];
+          store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
+        }
       }
     }
   }
@@ -365,17 +400,18 @@ bool encode_2d(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const 
          CUDA_SUCCESS;
 }
 
-template <int BITS, int GS, int NQ, int NST, int SCB>
+template <int BITS, int GS, int NQ, int NST, int SCB, int SW>
 int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qzeros, const void* scales,
                cudaStream_t st) {
-  using L = TmaLayout<BITS, GS, NST, SCB>;
+  using L = TmaLayout<BITS, GS, NST, SCB, SW>;
+  constexpr int TC = L::TC;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
   CUtensorMap tw, ts, tz;
   {
     const cuuint64_t dims[3] = {32, (cuuint64_t)(a.K / L::PER), (cuuint64_t)(a.N / 32)};
     const cuuint64_t strides[2] = {(cuuint64_t)a.N * 4, 128};
-    const cuuint32_t box[3] = {32, (cuuint32_t)L::ROWS, (cuuint32_t)kCW};
+    const cuuint32_t box[3] = {32, (cuuint32_t)L::ROWS, (cuuint32_t)SW};
     const cuuint32_t estr[3] = {1, 1, 1};
     if (enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint32_t*>(qweight), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
@@ -386,15 +422,16 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   const CUtensorMapDataType sdt = SCB == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                            : (a.sc_dtype == QL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-  if (!encode_2d(enc, &ts, sdt, scales, a.N, G, (uint64_t)a.N * SCB, kTileCols, L::GPS)) return -1;
+  if (!encode_2d(enc, &ts, sdt, scales, a.N, G, (uint64_t)a.N * SCB, TC, L::GPS)) return -1;
   if (!encode_2d(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, qzeros, a.N / L::PER, G, (uint64_t)(a.N / L::PER) * 4,
-                 kTileCols / L::PER, L::GPS))
+                 TC / L::PER, L::GPS))
     return -1;
-  auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB>;
+  auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB, SW>;
   const int sq = a.nstage / a.cs;
   const int nst_max = sq + (a.nstage % a.cs ? 1 : 0);
   const size_t smem = 1024 + L::kXsOff + (((size_t)a.M * nst_max * kStageK * 2 + 15) & ~(size_t)15) +
-                      (((size_t)a.M * nst_max * L::GPS * 4 + 15) & ~(size_t)15) + (size_t)(kTileCols + 16) * 4 * NQ * 4;
+                      (((size_t)a.M * nst_max * L::GPS * 4 + 15) & ~(size_t)15) + (size_t)(TC + 64) * 4 * NQ * 4 +
+                      (SW < kCW ? (size_t)SW * 32 * NQ * 4 * 4 : 0);
   if (smem > 200 * 1024) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -409,7 +446,7 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
     configured_dev = dev;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.cs, (a.N + kTileCols - 1) / kTileCols, 1);
+  cfg.gridDim = dim3(a.cs, (a.N + TC - 1) / TC, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -429,15 +466,23 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, tw, ts, tz, a), "gptq_gemv_tma launch");
 }
 
+template <int BITS, int GS, int SW>
+int tma_nq(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
+  // the same bytes in flight per CTA for both tile widths
+  constexpr int NST = (BITS == 4 ? 4 : 3) * (kCW / SW);
+  if (a.sc_dtype == QL_F32) {
+    if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 4, SW>(a, qw, qz, sc, st);
+    return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 4, SW>(a, qw, qz, sc, st)
+                    : launch_tma<BITS, GS, 4, NST, 4, SW>(a, qw, qz, sc, st);
+  }
+  if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 2, SW>(a, qw, qz, sc, st);
+  return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 2, SW>(a, qw, qz, sc, st)
+                  : launch_tma<BITS, GS, 4, NST, 2, SW>(a, qw, qz, sc, st);
+}
+
 template <int BITS, int GS>
 int tma_mt(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
-  constexpr int NST = BITS == 4 ? 4 : 3;
-  if (a.sc_dtype == QL_F32) {
-    if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 4>(a, qw, qz, sc, st);
-    return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 4>(a, qw, qz, sc, st) : launch_tma<BITS, GS, 4, NST, 4>(a, qw, qz, sc, st);
-  }
-  if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 2>(a, qw, qz, sc, st);
-  return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 2>(a, qw, qz, sc, st) : launch_tma<BITS, GS, 4, NST, 2>(a, qw, qz, sc, st);
+  return a.sw == 8 ? tma_nq<BITS, GS, 8>(a, qw, qz, sc, st) : tma_nq<BITS, GS, 4>(a, qw, qz, sc, st);
 }
 
 template <int BITS>
@@ -480,23 +525,28 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
-  // cluster size (K split): the CTA count tiles * cs should fill one resident wave of
-  // ctas_per_sm CTAs per SM as evenly as possible (the busiest SM sets the time)
-  const int tiles = (N + kTileCols - 1) / kTileCols;
-  int cs = 1;
+  // tile width and cluster size (K split): the CTA count tiles * cs should fill one resident
+  // wave of ctas_per_sm CTAs per SM as evenly as possible (the busiest SM sets the time); the
+  // wider tile wins ties (fewer partial sums to reduce)
+  int cs = 1, sw = 8;
   double best = -1.0;
-  for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-    const int ctas = tiles * c;
-    if (ctas > sms * ctas_per_sm && c > 1) break;
-    if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;
-    const double per_sm = (double)ctas / sms;
-    const double busiest = (double)((ctas + sms - 1) / sms);
-    const double score = per_sm / busiest * (per_sm < ctas_per_sm ? per_sm / ctas_per_sm : 1.0);
-    if (score > best + 1e-9) {
-      best = score;
-      cs = c;
+  for (int w = 8; w >= 4; w /= 2) {
+    const int tiles = (N + 32 * w - 1) / (32 * w);
+    for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
+      const int ctas = tiles * c;
+      if (ctas > sms * ctas_per_sm && c > 1) break;
+      if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;
+      const double per_sm = (double)ctas / sms;
+      const double busiest = (double)((ctas + sms - 1) / sms);
+      const double score = per_sm / busiest * (per_sm < ctas_per_sm ? per_sm / ctas_per_sm : 1.0);
+      if (score > best + 1e-9) {
+        best = score;
+        cs = c;
+        sw = w;
+      }
     }
   }
+  a.sw = sw;
   a.cs = cs;
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);

@@ -75,6 +75,23 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------------------
+// distributed shared memory
+// ---------------------------------------------------------------------------------------
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// 16-byte store into another CTA's shared memory that completes 16 bytes of transaction count
+// on that CTA's mbarrier (no cluster barrier needed on either side).
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, float a, float b, float c, float d, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(rbar)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
 // TMA (tiled, no multicast)
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
