@@ -35,6 +35,10 @@ METRIC = "int4 GEMV HBM GB/s at M=1 (config 1 sweep)"
 GEMM_SHAPES = [(4096, 11008), (3584, 18944)]
 GEMM_M = 2048
 L2_BYTES = 126 * 2 ** 20
+# DRAM bytes per launch of gptq_gemv_tma_kernel over its algorithmic bytes, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum = 30.606 MB for the K=4096, N=14336 launch whose
+# algorithmic bytes are 30.906 MB); traffic grows with the weight bytes, so it scales per shape
+GEMV_TRAFFIC_RATIO = 30.606 / 30.906
 
 
 def gemv_bytes(K, N, M=1, bits=4, gs=GS, x_bytes=2, out_bytes=4):
@@ -189,8 +193,8 @@ def profile_case(name):
     _ffi.load(build_if_missing=False)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
-    if name == "gemv":                       # gptq_gemv_tma_kernel, 4096 x 14336, M=1, 6 copies (176 MB)
-        K, N = 4096, 14336
+    if name in ("gemv", "gemv_narrow"):      # gptq_gemv_tma_kernel, M=1, 6 copies (> L2)
+        K, N = (4096, 14336) if name == "gemv" else (14336, 4096)   # 256- / 128-column tiles
         ws = [rand_gptq(K, N, dev, g) for _ in range(6)]
         x = torch.randn((1, K), device=dev, generator=g).half()
         y = torch.empty((1, N), device=dev)
@@ -364,7 +368,8 @@ def main():
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--skip-extra", action="store_true", help="skip the config-2 and config-4 sections")
     ap.add_argument("--profile", default=None,
-                    help="run one small fixed case for ncu: gemv | gemm | moe_decode | moe_prefill | q4k")
+                    help="run one small fixed case for ncu: gemv | gemv_narrow | gemm | moe_decode | "
+                         "moe_prefill | q4k")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:
@@ -409,9 +414,8 @@ def main():
         for L in lay:
             launch(L)
 
-    # ---- capture one step into a CUDA graph (launch-bound otherwise), warm up first.
-    # Headline graph uses programmatic dependent launch (each GEMV streams its weights while
-    # the previous one finishes); the plain-launch graph is timed too, for comparison.
+    # ---- capture one step into a CUDA graph (launch-bound otherwise), warm up first; a second
+    # graph with programmatic dependent launch is timed for comparison.
     def capture(pdl):
         _ffi.set_launch_flags(_ffi.LAUNCH_PDL if pdl else 0)
         for _ in range(3):
@@ -569,7 +573,10 @@ def main():
                    "l2": "inputs larger than L2 (rotating copies)", "cuda_graph": True,
                    "launch": "plain graph launches (value_with_pdl: QL_LAUNCH_PDL)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None,
+                     "frac": round(achieved / hbm, 4),
+                     "traffic": round(GEMV_TRAFFIC_RATIO * step_bytes() / launches_per_step),
+                     "traffic_basis": "ncu dram read+write of one 4096x14336 launch, scaled per launch by "
+                                      "algorithmic bytes (bytes per launch, averaged over the sweep)",
                      "peak_source": "%s (MEASURED_PEAKS.json hbm_gbs)" % src if src == "measured" else src,
                      "avg_launch_us": round(avg_launch_us, 3)},
         "value_with_pdl": round(value_pdl, 2),
