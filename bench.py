@@ -8,8 +8,10 @@ copies (20 GEMVs, 466 MB of packed weights > 2 x L2), so no launch finds its wei
 resident in HBM. `e2e` = the same bytes through the public Python operator with pinned host
 x copied in and y copied out every step.
 
-N > 1 (torchrun): every rank runs the same per-rank workload on its own weights (weak
-scaling; independent layers need no collective); value = all ranks' bytes / max time.
+N > 1 (torchrun): every rank holds the column shard of layers N times wider (its shard has
+the 1-GPU shape, so per-rank work is fixed: weak scaling) and each step ends with one NCCL
+all-gather of the step's 20 outputs; value = all ranks' bytes / max time over ranks. The
+`moe_ep` section runs config 4 expert-parallel (128 / N experts per rank, T tokens per rank).
 
 --impl reference: the reference's CPU algorithm (the numpy port in oracle/, the reference
 package itself cannot travel) on a bounded sample of the same workload, same metric.
@@ -151,6 +153,41 @@ def bench_moe(dev, g, hbm, bf16_peak):
              "frac_of_bf16_peak": round(flops / (ms / 1e3) / 1e12 / bf16_peak, 4), "layers_per_graph": L}
         out["T%d" % T] = r
         del gr, layers
+        torch.cuda.empty_cache()
+    return out
+
+
+def bench_moe_ep(dev, g, world, timed):
+    """Config 4 across `world` GPUs, expert parallel: each rank holds 128 / world experts, routes
+    its own T tokens (weak scaling in tokens) and exchanges rows with two all-to-alls per layer.
+    Timed eagerly (the dispatch sizes are read back to the host every layer), max over ranks."""
+    torch = torch_mod()
+    from webpytorch_b200 import moe
+    from webpytorch_b200.shard import ExpertParallelMoE
+    Ep = MOE_E // world
+    out = {}
+    for T in (32, 256, 2048):
+        L = 4
+        layers = []
+        for _ in range(L):
+            gu = moe.StackedExperts.from_packed(*rand_gptq(MOE_H, 2 * MOE_I, dev, g, E=Ep), GS, 4)
+            dn = moe.StackedExperts.from_packed(*rand_gptq(MOE_I, MOE_H, dev, g, E=Ep), GS, 4)
+            logits = torch.randn((T, MOE_E), device=dev, generator=g)
+            x = torch.randn((T, MOE_H), device=dev, generator=g).to(torch.bfloat16)
+            layers.append((ExpertParallelMoE(lambda t, _l=logits: _l, gu, dn, MOE_E, MOE_H, MOE_I, MOE_TOPK), x))
+
+        def fwd():
+            for blk, x in layers:
+                blk(x)
+        for _ in range(2):
+            fwd()
+        reps = 5
+        ms, _, _ = timed(lambda: [fwd() for _ in range(reps)], 1)
+        ms_layer = ms / (reps * L)
+        out["T%d_per_rank" % T] = {"us_per_layer": round(ms_layer * 1e3, 2),
+                                   "tokens/s": round(T * world / (ms_layer / 1e3), 1),
+                                   "experts_per_rank": Ep, "tokens_per_rank": T}
+        del layers
         torch.cuda.empty_cache()
     return out
 
@@ -383,6 +420,11 @@ def main():
     from webpytorch_b200 import _ffi
     from webpytorch_b200.qlinear import _gptq_matmul
 
+    # stdout carries exactly one JSON line (rank 0): anything libraries print there (NCCL's
+    # version banner, for one) goes to stderr instead
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -396,15 +438,20 @@ def main():
     # ---- synthetic weights (config-1 distributions), R copies per shape, generated on device
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
+    # Every GEMV writes its [1, N] output into one packed per-rank buffer. With N > 1 ranks each
+    # rank holds the column shard of layers N times wider (its shard has the 1-GPU shape, weak
+    # scaling) and a step ends with one all-gather of all 20 output slices.
     lay = []
+    n_out = COPIES * sum(N for _, N in SHAPES)
+    y_all = torch.empty((1, n_out), device=dev, dtype=torch.float32)
+    gathered = torch.empty((world, n_out), device=dev, dtype=torch.float32) if world > 1 else None
+    off = 0
     for c in range(COPIES):
         for (K, N) in SHAPES:
-            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=g)
-            qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // GS, N // 8), dtype=torch.int32, device=dev, generator=g)
-            sc = (torch.rand((K // GS, N), device=dev, generator=g) * 0.018 + 0.002).half()
+            qw, qz, sc = rand_gptq(K, N, dev, g)
             x = torch.randn((1, K), device=dev, generator=g).half()
-            y = torch.empty((1, N), device=dev, dtype=torch.float32)
-            lay.append((K, N, qw, qz, sc, x, y))
+            lay.append((K, N, qw, qz, sc, x, y_all[:, off:off + N]))
+            off += N
 
     def launch(L):
         K, N, qw, qz, sc, x, y = L
@@ -413,6 +460,8 @@ def main():
     def step():
         for L in lay:
             launch(L)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, y_all)
 
     # ---- capture one step into a CUDA graph (launch-bound otherwise), warm up first; a second
     # graph with programmatic dependent launch is timed for comparison.
@@ -468,7 +517,7 @@ def main():
     # ---- per-shape launch durations: a graph of 10 passes over >= 320 MB of one shape's
     # weight copies (each launch reads its weights from HBM), timed with CUDA events
     per_shape = {}
-    for (K, N) in SHAPES:
+    for (K, N) in (SHAPES if world == 1 else []):
         Ls = [L for L in lay if (L[0], L[1]) == (K, N)]
         # rotate over at least 320 MB of this shape's weights so no launch finds them in L2
         extra = max(0, -(-320_000_000 // gemv_bytes(K, N)) - len(Ls))
@@ -503,14 +552,19 @@ def main():
     # ---- e2e: public operator path with pinned host buffers, copies inside the timed region
     hx = [torch.empty(L[5].shape, dtype=L[5].dtype, pin_memory=True).copy_(L[5].cpu()) for L in lay]
     hy = [torch.empty(L[6].shape, dtype=L[6].dtype, pin_memory=True) for L in lay]
+    hg = torch.empty(gathered.shape, dtype=gathered.dtype, pin_memory=True) if world > 1 else None
     h2d = sum(t.numel() * t.element_size() for t in hx)
-    d2h = sum(t.numel() * t.element_size() for t in hy)
+    d2h = sum(t.numel() * t.element_size() for t in hy) if world == 1 else hg.numel() * hg.element_size()
 
     def e2e_step():
         for i, L in enumerate(lay):
             L[5].copy_(hx[i], non_blocking=True)
             launch(L)
-            hy[i].copy_(L[6], non_blocking=True)
+            if world == 1:
+                hy[i].copy_(L[6], non_blocking=True)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, y_all)
+            hg.copy_(gathered, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -519,7 +573,7 @@ def main():
 
     # ---- config 3: prefill dequant-GEMM (tcgen05), desc_act, bf16 x, M = 2048
     gemm = {}
-    if not args.skip_gemm:
+    if not args.skip_gemm and world == 1:
         from webpytorch_b200.qlinear import QuantizedLinear
         _, bf16_peak, _ = peaks()
         for (K, N) in GEMM_SHAPES:
@@ -548,11 +602,13 @@ def main():
             del ql, qw, qz, sc, x, yb
         torch.cuda.empty_cache()
 
-    moe_res, q4k_res = {}, {}
+    moe_res, q4k_res, moe_ep = {}, {}, {}
     if not args.skip_extra:
         hbm0, bf0, _ = peaks()
-        q4k_res = bench_q4k(dev, g, hbm0)
-        moe_res = bench_moe(dev, g, hbm0, bf0)
+        if world == 1:
+            q4k_res = bench_q4k(dev, g, hbm0)
+            moe_res = bench_moe(dev, g, hbm0, bf0)
+        moe_ep = bench_moe_ep(dev, g, world, timed)
 
     tot_bytes = step_bytes() * args.steps * world
     value = tot_bytes / (ms / 1e3) / 1e9
@@ -569,7 +625,10 @@ def main():
         "data": "synthetic",
         "config": {"workload": "config1: int4 g128 GEMV M=1 over (K,N) in %s, %d weight copies per step "
                                "(%.0f MB/step > 2x L2, no L2 flush needed)" % (SHAPES, COPIES, step_bytes() / 1e6),
-                   "bits": 4, "group_size": GS, "M": 1, "parallelism": "replicas x%d" % world,
+                   "bits": 4, "group_size": GS, "M": 1,
+                   "parallelism": ("N-sharded x%d: each rank holds the column shard (the 1-GPU shape) of layers "
+                                   "%d times wider; one NCCL all-gather of the step's 20 outputs per step"
+                                   % (world, world)) if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (rotating copies)", "cuda_graph": True,
                    "launch": "plain graph launches (value_with_pdl: QL_LAUNCH_PDL)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
@@ -592,6 +651,7 @@ def main():
                             "independent layers" % (MOE_E, MOE_TOPK, MOE_H, MOE_I),
                 "expert_GB/s basis": "active experts' packed weights+scales+zeros per layer / layer time",
                 "T": moe_res},
+        "moe_ep": moe_ep,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "QuantizedLinear boundary (_gptq_matmul via ctypes) with pinned host x/y copies"},
@@ -601,7 +661,8 @@ def main():
     if world == 1 and rank == 0 and args.cpu_seconds > 0:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        json_out.write(json.dumps(result) + "\n")
+        json_out.flush()
     del graph, graph_pdl
     if world > 1:
         dist.barrier()

@@ -196,6 +196,15 @@ QL_API int ql_moe_route(const float* logits, int T, int E, int top_k, int norm_t
                         int32_t* active, int32_t* n_active, int32_t* tiles, int32_t* n_tiles, int max_tiles,
                         int32_t* row_token, int32_t* pair_row, void* stream);
 
+/* Grouping of n rows by given ids in [0, G) (the expert-parallel dispatch groups (token, k)
+ * pairs by destination rank, the receiving rank groups its rows by local expert): counts, offsets
+ * [G+1], active list, tile table as ql_moe_route; row_src[r] = the input row placed at sorted row
+ * r, pos_of[i] = the sorted row of input row i. Replaces the host-side `np.where(topk_idx == e)`
+ * gathers of lm_engine.py:311-316. */
+QL_API int ql_moe_group(const int32_t* ids, int n, int G, int tile_rows, int32_t* counts, int32_t* offsets,
+                        int32_t* cursor, int32_t* active, int32_t* n_active, int32_t* tiles, int32_t* n_tiles,
+                        int max_tiles, int32_t* row_src, int32_t* pos_of, void* stream);
+
 QL_API size_t ql_moe_grouped_workspace(long P, int E, int K, int gs);
 
 QL_API int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int32_t* row_token, long P,

@@ -160,6 +160,12 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int T, 
   pair_row[i] = r;
 }
 
+// Histogram of given group ids (expert-parallel dispatch and the receiving side's local grouping).
+__global__ void moe_hist_kernel(const int32_t* __restrict__ ids, int n, int32_t* __restrict__ counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) atomicAdd(&counts[ids[i]], 1);
+}
+
 // a[r, n] = silu(y[r, n]) * y[r, I + n]  (gate | up fused along columns), silu = v * sigmoid(v)
 __global__ void moe_act_kernel(const float* __restrict__ y, long P, int I, void* __restrict__ a, int a_dtype) {
   const long total = P * I;
@@ -228,6 +234,35 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
     const int pairs = T * top_k;
     moe_scatter_kernel<<<(pairs + 255) / 256, 256, 0, st>>>(topk_idx, T, top_k, offsets, cursor, row_token,
                                                              pair_row);
+    if ((rc = cuda_status(cudaGetLastError(), "moe_scatter launch"))) return rc;
+  }
+  return QL_OK;
+}
+
+extern "C" int ql_moe_group(const int32_t* ids, int n, int G, int tile_rows, int32_t* counts, int32_t* offsets,
+                            int32_t* cursor, int32_t* active, int32_t* n_active, int32_t* tiles, int32_t* n_tiles,
+                            int max_tiles, int32_t* row_src, int32_t* pos_of, void* stream) {
+  if (n < 0 || G <= 0 || G > kMaxExperts || tile_rows <= 0 || max_tiles < 0) {
+    set_error("ql_moe_group: bad sizes (n=%d G=%d; G <= %d)", n, G, kMaxExperts);
+    return QL_ERR_ARG;
+  }
+  if (!counts || !offsets || !cursor || !active || !n_active || !n_tiles || (max_tiles > 0 && !tiles) ||
+      (n > 0 && (!ids || !row_src || !pos_of))) {
+    set_error("ql_moe_group: null pointer");
+    return QL_ERR_ARG;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc = cuda_status(cudaMemsetAsync(counts, 0, sizeof(int32_t) * G, st), "ql_moe_group memset");
+  if (rc) return rc;
+  if (n > 0) {
+    moe_hist_kernel<<<(n + 255) / 256, 256, 0, st>>>(ids, n, counts);
+    if ((rc = cuda_status(cudaGetLastError(), "moe_hist launch"))) return rc;
+  }
+  moe_scan_kernel<<<1, (G + 31) & ~31, 0, st>>>(counts, G, tile_rows, offsets, cursor, active, n_active, tiles,
+                                                n_tiles, max_tiles);
+  if ((rc = cuda_status(cudaGetLastError(), "moe_scan launch"))) return rc;
+  if (n > 0) {
+    moe_scatter_kernel<<<(n + 255) / 256, 256, 0, st>>>(ids, n, 1, offsets, cursor, row_src, pos_of);
     if ((rc = cuda_status(cudaGetLastError(), "moe_scatter launch"))) return rc;
   }
   return QL_OK;
