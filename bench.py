@@ -35,6 +35,7 @@ GS = 128
 COPIES = 4
 METRIC = "int4 GEMV HBM GB/s at M=1 (config 1 sweep)"
 GEMM_SHAPES = [(4096, 11008), (3584, 18944)]
+GEMM_MS = (128, 512, 2048)
 GEMM_M = 2048
 L2_BYTES = 126 * 2 ** 20
 # DRAM bytes per launch of gptq_gemv_tma_kernel over its algorithmic bytes, from one ncu capture
@@ -577,29 +578,20 @@ def main():
         from webpytorch_b200.qlinear import QuantizedLinear
         _, bf16_peak, _ = peaks()
         for (K, N) in GEMM_SHAPES:
-            M = GEMM_M
-            qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // 8, N), dtype=torch.int32, device=dev, generator=g)
-            qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (K // GS, N // 8), dtype=torch.int32, device=dev, generator=g)
-            sc = (torch.rand((K // GS, N), device=dev, generator=g) * 0.018 + 0.002).half()
+            qw, qz, sc = rand_gptq(K, N, dev, g)
             gidx = (torch.arange(K, device=dev) // GS)[torch.randperm(K, device=dev, generator=g)]
             ql = QuantizedLinear.from_autogptq(qw, qz, sc, None, GS, 4, g_idx=gidx, device=dev)
-            x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
-            yb = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
-            for _ in range(3):
-                ql(x, out=yb, out_dtype=torch.bfloat16)
-            torch.cuda.synchronize()
-            reps = 20
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(reps):
-                ql(x, out=yb, out_dtype=torch.bfloat16)
-            e1.record()
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
-            tflops = 2.0 * M * N * K / (us * 1e-6) / 1e12
-            gemm["%dx%d_M%d" % (K, N, M)] = {"us": round(us, 2), "TFLOP/s": round(tflops, 1),
-                                              "frac_of_bf16_peak": round(tflops / bf16_peak, 4)}
-            del ql, qw, qz, sc, x, yb
+            for M in GEMM_MS:
+                x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+                yb = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+                for _ in range(3):
+                    ql(x, out=yb, out_dtype=torch.bfloat16)
+                us = event_time(lambda: ql(x, out=yb, out_dtype=torch.bfloat16), 20) * 1e3
+                tflops = 2.0 * M * N * K / (us * 1e-6) / 1e12
+                gemm["%dx%d_M%d" % (K, N, M)] = {"us": round(us, 2), "TFLOP/s": round(tflops, 1),
+                                                  "frac_of_bf16_peak": round(tflops / bf16_peak, 4)}
+                del x, yb
+            del ql, qw, qz, sc
         torch.cuda.empty_cache()
 
     moe_res, q4k_res, moe_ep = {}, {}, {}
@@ -640,8 +632,8 @@ def main():
                      "avg_launch_us": round(avg_launch_us, 3)},
         "value_with_pdl": round(value_pdl, 2),
         "per_shape": per_shape,
-        "gemm": {"workload": "config3: int4 g128 desc_act dequant-GEMM, bf16 x/out, M=%d (act-order gather "
-                             "+ fp16 staging + tcgen05 GEMM per call)" % GEMM_M,
+        "gemm": {"workload": "config3: int4 g128 desc_act dequant-GEMM, bf16 x/out, M in %s (act-order gather "
+                             "+ fp16 staging + tcgen05 GEMM per call)" % (GEMM_MS,),
                  "bound": "tensor", "peak_TFLOP/s": peaks()[1], "shapes": gemm},
         "q4k": {"workload": "config2: Q4_K K=%d N=%d fp32 x/out, %d rotating copies (%.0f MB)"
                             % (Q4K_K, Q4K_N, Q4K_COPIES, Q4K_COPIES * Q4K_N * Q4K_K / 256 * 144 / 1e6),

@@ -3,14 +3,17 @@
 // y[M, N] = x[M, K] @ W[K, N], W = scales[g, n] * (q[k, n] - (z[g, n] + zero_offset)).
 //
 // The product is computed transposed, D^T[n, m] = W^T[n, :] . x^T[:, m], so that
-//  * the dequantised weights are the MMA's A operand held in tensor memory: each of 128
-//    dequant threads owns one TMEM lane (one output column n), unpacks its packed words in
-//    registers and writes the fp16 values straight into TMEM with tcgen05.st. Weights never
-//    pass through shared memory, which keeps shared-memory traffic to the activation tile.
-//  * the activations are the B operand: a 256-token x 64-k fp16 tile per stage, loaded by TMA
-//    into 128-byte-swizzled shared memory.
-//  * the fp32 accumulator D (128 columns n x 256 tokens) lives in TMEM; the epilogue warps read
-//    it with tcgen05.ld, undo the activation row scale, add the bias and store y.
+//  * the dequantised weights are the MMA's A operand held in tensor memory: 8 dequant warps
+//    (two per TMEM lane quadrant, each taking half of a 64-K slab) own one output column per
+//    lane, unpack the packed words in registers and write fp16 straight into TMEM with
+//    tcgen05.st;
+//  * the activations are the B operand: a 128-token x 64-k fp16 tile per stage, 128-byte
+//    swizzled;
+//  * one TMA producer warp streams every operand of a slab into a shared-memory ring: the
+//    activation tile, the packed weight box [rows of the slab][128 columns], and the slab's
+//    scale and zero rows, so no compute warp ever waits on a global load;
+//  * the fp32 accumulator (128 columns x 128 tokens) is double-buffered in TMEM: epilogue warps
+//    drain one buffer with tcgen05.ld while the MMAs of the next tile fill the other.
 //
 // Numerics: the MMA runs in fp16 with fp32 accumulation. x is staged once (prep_x_kernel) as
 // fp16 scaled per row by an exact power of two (largest |x| in [2^14, 2^15)), which keeps
@@ -19,11 +22,11 @@
 // act-order permutation x[:, perm[k]] and stores each 8-value block in the (j, j+4) pair order
 // that the register unpack produces, so weights and activations agree on K order.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over output tiles):
-//   warp 0       TMA producer for activation tiles
+// Warp roles (512 threads, one CTA per SM, persistent over output tiles):
+//   warp 0       TMA producer
 //   warp 1       TMEM allocator and MMA issuer (one elected lane)
-//   warps 4-7    dequant producers (TMEM lanes 0-127)
-//   warps 8-11   epilogue (TMEM lanes 0-127)
+//   warps 4-11   dequant producers (TMEM lane quadrant = warp % 4, slab half = (warp - 4) / 4)
+//   warps 12-15  epilogue (TMEM lanes 0-127)
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -41,9 +44,11 @@ namespace {
 
 constexpr int kSlabK = 64;          // K per pipeline stage
 constexpr int kTileN = 128;         // output columns per tile (MMA M, TMEM lanes)
-constexpr int kThreads = 384;
+constexpr int kBT = 128;            // tokens per tile (MMA N)
+constexpr int kThreads = 512;
 constexpr int kDequantWarp0 = 4;
-constexpr int kEpilogueWarp0 = 8;
+constexpr int kDequantWarps = 8;
+constexpr int kEpilogueWarp0 = 12;
 
 // ---------------------------------------------------------------------------------------
 // activation staging: fp16, power-of-two row scale, act-order gather, (j, j+4) pair order
@@ -105,6 +110,7 @@ struct GemmArgs {
   int M, K, N, gs;
   float zoff;
   int n_wtiles, n_ttiles;
+  int gb;            // scale/zero rows per slab: 2 when gs == 32, else 1
   // grouped (MoE) mode when tiles != NULL: token tile i is rows [offsets[e] + r, offsets[e + 1])
   // capped at BT rows, with (e, r) = tiles[2i], tiles[2i + 1]; *n_tiles tiles are valid
   const int32_t* tiles;
@@ -131,15 +137,23 @@ __device__ __forceinline__ TileRows tile_rows(const GemmArgs& a, int tt, int BT)
   return r;
 }
 
-template <int BT, int NS>
+template <int BITS, int NS>
 struct SmemLayout {
-  static constexpr int kStageBytes = BT * kSlabK * 2;  // BT rows of 128 bytes
-  static constexpr int kXOff = 0;
+  static constexpr int PER = 32 / BITS;
+  static constexpr int ROWS = kSlabK / PER;                // packed rows per slab (8 int4 / 16 int8)
+  static constexpr int kXBytes = kBT * kSlabK * 2;         // activation tile, 128-byte swizzled rows
+  static constexpr int kWOff = kXBytes;
+  static constexpr int kWBytes = ROWS * kTileN * 4;        // packed weights [ROWS][128]
+  static constexpr int kSOff = kWOff + kWBytes;
+  static constexpr int kSBytes = 2 * kTileN * 4;           // scales [<= 2 groups][128] (up to fp32)
+  static constexpr int kZOff = kSOff + kSBytes;
+  static constexpr int kZBytes = 2 * (kTileN / PER) * 4;   // zeros [<= 2 groups][128 / PER]
+  static constexpr int kStageBytes = (kZOff + kZBytes + 1023) & ~1023;
   static constexpr int kBarOff = NS * kStageBytes;
-  // barriers: x_full[NS], a_full[NS], slab_free[NS], d_full, d_empty, final
-  static constexpr int kNumBars = 3 * NS + 3;
+  // barriers: full[NS], a_full[NS], slab_free[NS], d_full[2], d_empty[2], final
+  static constexpr int kNumBars = 3 * NS + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kBytes = kMiscOff + 16 + 1024;  // + tmem slot, abort flag, alignment slack
+  static constexpr int kBytes = kMiscOff + 16 + 1024;      // + tmem slot, abort flag, alignment slack
 };
 
 // Unpack one packed int4 word (8 values along K) for one column into 4 fp16 pairs
@@ -164,16 +178,19 @@ __device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, ui
   out2[1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)), s2));
 }
 
-template <int BITS, int BT, int NS>
+template <int BITS, int NS>
 __global__ void __launch_bounds__(kThreads, 1)
-    gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs a) {
-  using L = SmemLayout<BT, NS>;
-  constexpr int PER = 32 / BITS;
-  constexpr int ROWS = kSlabK / PER;            // packed rows per slab (8 for int4, 16 for int8)
+    gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                        const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
+                        const GemmArgs a) {
+  using L = SmemLayout<BITS, NS>;
+  constexpr int PER = L::PER;
+  constexpr int ROWS = L::ROWS;
+  constexpr int HROWS = ROWS / 2;               // packed rows per dequant half
   constexpr int TCOLS_A = kSlabK / 2;           // TMEM columns per A stage (fp16 pairs)
-  constexpr int D_COL = 0;
-  constexpr int A_COL = BT;                     // A stages start after the accumulator
-  constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, BT);
+  constexpr int A_COL = 2 * kBT;                // A stages start after the two accumulators
+  constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, kBT);
+  constexpr uint32_t MASK = (1u << BITS) - 1u;
   static_assert(A_COL + NS * TCOLS_A <= 512, "TMEM budget");
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -181,24 +198,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = ptx::smem_addr(smem);
   const uint32_t bar0 = sbase + L::kBarOff;
-  auto x_full = [&](int s) { return bar0 + 8u * s; };
+  auto full = [&](int s) { return bar0 + 8u * s; };
   auto a_full = [&](int s) { return bar0 + 8u * (NS + s); };
   auto slab_free = [&](int s) { return bar0 + 8u * (2 * NS + s); };
-  const uint32_t d_full = bar0 + 8u * (3 * NS);
-  const uint32_t d_empty = bar0 + 8u * (3 * NS + 1);
-  const uint32_t fin_bar = bar0 + 8u * (3 * NS + 2);
+  auto d_full = [&](int b) { return bar0 + 8u * (3 * NS + b); };
+  auto d_empty = [&](int b) { return bar0 + 8u * (3 * NS + 2 + b); };
+  const uint32_t fin_bar = bar0 + 8u * (3 * NS + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
-      ptx::mbar_init(x_full(s), 1);
-      ptx::mbar_init(a_full(s), 128);
+      ptx::mbar_init(full(s), 1);
+      ptx::mbar_init(a_full(s), kDequantWarps);
       ptx::mbar_init(slab_free(s), 1);
     }
-    ptx::mbar_init(d_full, 1);
-    ptx::mbar_init(d_empty, 128);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(d_full(b), 1);
+      ptx::mbar_init(d_empty(b), 128);
+    }
     ptx::mbar_init(fin_bar, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -207,7 +226,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tmem_alloc(ptx::smem_addr(tmem_slot), 512);
     ptx::tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) ptx::tma_prefetch(&tmap_x);
+  if (warp == 0 && lane == 0) {
+    ptx::tma_prefetch(&tmap_x);
+    ptx::tma_prefetch(&tmap_w);
+    ptx::tma_prefetch(&tmap_s);
+    ptx::tma_prefetch(&tmap_z);
+  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -215,26 +239,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int nslab = a.K / kSlabK;
   const int ntiles = a.n_wtiles * (a.tiles ? *a.n_tiles : a.n_ttiles);
+  const int G = a.K / a.gs;
+  const int sc_bytes = a.sc_dtype == QL_F32 ? 4 : 2;
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer: activation tile, packed weights, scales, zeros per slab
     if (lane == 0) {
+      const uint32_t stage_tx = L::kXBytes + L::kWBytes + a.gb * kTileN * sc_bytes + a.gb * (kTileN / PER) * 4;
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
-        const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
+        const int wt = tile % a.n_wtiles;
+        const TileRows tr = tile_rows(a, tile / a.n_wtiles, kBT);
+        const int wrow0 = tr.e * (a.K / PER), grow0 = tr.e * G;
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
           if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(x_full(s), L::kStageBytes);
-          ptx::tma_load_2d(sbase + L::kXOff + s * L::kStageBytes, &tmap_x, x_full(s), kb * kSlabK, tr.row0);
+          const uint32_t st = sbase + s * L::kStageBytes;
+          const int g0 = (kb * kSlabK) / a.gs;
+          ptx::mbar_arrive_expect_tx(full(s), stage_tx);
+          ptx::tma_load_2d(st, &tmap_x, full(s), kb * kSlabK, tr.row0);
+          ptx::tma_load_2d(st + L::kWOff, &tmap_w, full(s), wt * kTileN, wrow0 + kb * ROWS);
+          ptx::tma_load_2d(st + L::kSOff, &tmap_s, full(s), wt * kTileN, grow0 + g0);
+          ptx::tma_load_2d(st + L::kZOff, &tmap_z, full(s), wt * (kTileN / PER), grow0 + g0);
         }
       }
       if (!ok) {  // let the copies already in flight land before the CTA releases its smem
-        for (int j = it > NS ? it - NS : 0; j < it; ++j) ptx::mbar_wait_drain(x_full(j % NS), (j / NS) & 1);
+        for (int j = it > NS ? it - NS : 0; j < it; ++j) ptx::mbar_wait_drain(full(j % NS), (j / NS) & 1);
       }
     }
   } else if (warp == 1) {
@@ -243,89 +277,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0, tcount = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tcount) {
-        if (!ptx::mbar_wait(d_empty, (tcount & 1) ^ 1, abort_flag)) break;
+        const int b = tcount & 1;
+        if (!ptx::mbar_wait(d_empty(b), ((tcount >> 1) & 1) ^ 1, abort_flag)) break;
         ptx::tc_fence_after();
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
           const uint32_t par = (it / NS) & 1;
-          if (!ptx::mbar_wait(x_full(s), par, abort_flag) || !ptx::mbar_wait(a_full(s), par, abort_flag)) {
+          if (!ptx::mbar_wait(full(s), par, abort_flag) || !ptx::mbar_wait(a_full(s), par, abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t xs = sbase + L::kXOff + s * L::kStageBytes;
+          const uint32_t xs = sbase + s * L::kStageBytes;
 #pragma unroll
           for (int j = 0; j < kSlabK / 16; ++j) {
-            ptx::mma_f16_ts(tmem + D_COL, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
+            ptx::mma_f16_ts(tmem + b * kBT, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
                             IDESC, (kb | j) != 0);
           }
-          ptx::mma_commit(slab_free(s));  // frees the activation stage and the TMEM A stage
+          ptx::mma_commit(slab_free(s));  // frees the stage's shared memory and its TMEM A columns
         }
-        if (ok) ptx::mma_commit(d_full);
+        if (ok) ptx::mma_commit(d_full(b));
       }
       // every MMA this thread issued has completed before TMEM is released (also on abort)
       ptx::mma_commit(fin_bar);
       ptx::mbar_wait_drain(fin_bar, 0);
     }
-  } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + 4) {
-    // ---------------- dequant producers: thread = TMEM lane = output column of the tile
-    const int q = warp & 3;
+  } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
+    // ---------------- dequant: lane = TMEM lane = output column; half h of each slab's K
+    const int q = warp & 3, h = (warp - kDequantWarp0) >> 2;
     const int lrow = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    const int gi = a.gb == 2 ? h : 0;   // scale/zero row of this half inside the slab
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int wt = tile % a.n_wtiles;
-      const int n = wt * kTileN + lrow;
-      const bool ok = n < a.N;
-      const int nn = ok ? n : 0;
-      const int e = a.tiles ? a.tiles[2 * (tile / a.n_wtiles)] : 0;
-      const uint32_t* qw = a.qw + (size_t)e * a.qw_estride;
-      const uint32_t* qz = a.qz + (size_t)e * a.qz_estride;
-      const char* scb = reinterpret_cast<const char*>(a.sc) + (size_t)e * a.sc_estride * (a.sc_dtype == QL_F32 ? 4 : 2);
-      uint32_t w[ROWS];
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(qw + (long)r * a.N + nn) : 0u;
       for (int kb = 0; kb < nslab; ++kb, ++it) {
         const int s = it % NS;
-        // scale and zero of this slab's group(s): a slab of 64 never straddles a group of >= 64,
-        // and a group of 32 is half a slab
-        uint32_t zlo[2], zhi[2];
-        __half2 s2[2];
+        if (!ptx::mbar_wait(full(s), (it / NS) & 1, abort_flag)) goto done;
+        const unsigned char* stp = smem + s * L::kStageBytes;
+        const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
+        uint32_t w[HROWS];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int g = (kb * kSlabK + h * (kSlabK / 2)) / a.gs;
-          float scv = 0.f;
-          uint32_t z = 0;
-          if (ok) {
-            scv = load_as_float(scb, a.sc_dtype, (long)g * a.N + nn);
-            z = (qz[(long)g * (a.N / PER) + nn / PER] >> (BITS * (nn % PER))) & MASK;
-          }
-          const float zf = (float)z + a.zoff;
-          zlo[h] = h2_as_u32(__float2half2_rn(1024.f + zf));
-          zhi[h] = h2_as_u32(__float2half2_rn(-(64.f + zf)));
-          s2[h] = __float2half2_rn(scv);
-        }
-        uint32_t v[32];
+        for (int r = 0; r < HROWS; ++r) w[r] = wsm[(h * HROWS + r) * kTileN + lrow];
+        const float scv = load_as_float(stp + L::kSOff, a.sc_dtype, gi * kTileN + lrow);
+        const uint32_t zw = reinterpret_cast<const uint32_t*>(stp + L::kZOff)[gi * (kTileN / PER) + lrow / PER];
+        const float zf = (float)((zw >> (BITS * (lrow % PER))) & MASK) + a.zoff;
+        const uint32_t zlo = h2_as_u32(__float2half2_rn(1024.f + zf));
+        const uint32_t zhi = h2_as_u32(__float2half2_rn(-(64.f + zf)));
+        const __half2 s2 = __float2half2_rn(scv);
+        uint32_t v[16];
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-          const int h = (r * PER) / (kSlabK / 2);
+        for (int r = 0; r < HROWS; ++r) {
           if constexpr (BITS == 4) {
-            dq_int4(w[r], zlo[h], zhi[h], s2[h], &v[r * 4]);
+            dq_int4(w[r], zlo, zhi, s2, &v[r * 4]);
           } else {
-            dq_int8(w[r], zlo[h], s2[h], &v[r * 2]);
+            dq_int8(w[r], zlo, s2, &v[r * 2]);
           }
         }
-        // prefetch the next slab's packed words (next tile's first slab after the last)
-        if (kb + 1 < nslab) {
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) w[r] = ok ? __ldg(qw + (long)((kb + 1) * ROWS + r) * a.N + nn) : 0u;
-        }
-        if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) goto done;
-        ptx::tmem_st32(lane_addr + A_COL + s * TCOLS_A, v);
+        ptx::tmem_st16(lane_addr + A_COL + s * TCOLS_A + h * (TCOLS_A / 2), v);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
-        ptx::mbar_arrive(a_full(s));
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(a_full(s));
       }
     }
   } else if (warp >= kEpilogueWarp0) {
@@ -335,29 +347,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     int tcount = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
+      const int b = tcount & 1;
       const int wt = tile % a.n_wtiles;
-      const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
+      const TileRows tr = tile_rows(a, tile / a.n_wtiles, kBT);
       const int n = wt * kTileN + lrow;
-      const float b = (a.bias && n < a.N) ? a.bias[n] : 0.f;
-      if (!ptx::mbar_wait(d_full, tcount & 1, abort_flag)) goto done;
-      ptx::tc_fence_after();
-#pragma unroll 1
-      for (int c = 0; c < BT / 32; ++c) {
-        uint32_t v[32];
-        ptx::tmem_ld32(lane_addr + D_COL + c * 32, v);
-        ptx::tmem_wait_ld();
-        if (c == BT / 32 - 1) {
-          ptx::tc_fence_before();
-          ptx::mbar_arrive(d_empty);  // accumulator drained into registers
-        }
-        if (n < a.N) {
+      const float bias = (a.bias && n < a.N) ? a.bias[n] : 0.f;
+      int rexp[kBT / 32];   // row exponent of token c * 32 + lane (broadcast with shuffles below)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int tok = tr.row0 + c * 32 + j;
-            if (tok < tr.row_end) {
-              const float val = __uint_as_float(v[j]) * exp2i(a.row_exp[tok]) + b;
-              store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + n, val);
-            }
+      for (int c = 0; c < kBT / 32; ++c) {
+        const int tok = tr.row0 + c * 32 + lane;
+        rexp[c] = tok < tr.row_end ? a.row_exp[tok] : 0;
+      }
+      if (!ptx::mbar_wait(d_full(b), (tcount >> 1) & 1, abort_flag)) goto done;
+      ptx::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kBT / 32; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld32(lane_addr + b * kBT + c * 32, v);
+        ptx::tmem_wait_ld();
+        if (c == kBT / 32 - 1) {
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(d_empty(b));  // accumulator drained into registers
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int tok = tr.row0 + c * 32 + j;
+          const int e = __shfl_sync(0xffffffffu, rexp[c], j);
+          if (n < a.N && tok < tr.row_end) {
+            const float val = __uint_as_float(v[j]) * exp2i(e) + bias;
+            store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + n, val);
           }
         }
       }
@@ -389,27 +407,46 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int BITS, int BT, int NS>
-int launch_gemm(const GemmArgs& a, const __half* x16, cudaStream_t st) {
+bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+            uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// n_experts: stacked weight matrices (grouped mode), 1 otherwise.
+template <int BITS>
+int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
+  constexpr int NS = BITS == 4 ? 8 : 7;
+  constexpr int PER = 32 / BITS;
+  using L = SmemLayout<BITS, NS>;
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled is unavailable");
     return QL_ERR_CUDA;
   }
-  CUtensorMap tmap;
-  const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-  const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kSlabK, (cuuint32_t)BT};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(x16), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  const int G = a.K / a.gs;
+  const int scb = a.sc_dtype == QL_F32 ? 4 : 2;
+  const CUtensorMapDataType sdt = a.sc_dtype == QL_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : a.sc_dtype == QL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMap tx, tw, ts, tz;
+  if (!encode(enc, &tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, a.K, a.M, (uint64_t)a.K * 2, kSlabK, kBT,
+              CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode(enc, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qw, a.N, (uint64_t)n_experts * (a.K / PER),
+              (uint64_t)a.N * 4, kTileN, L::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode(enc, &ts, sdt, a.sc, a.N, (uint64_t)n_experts * G, (uint64_t)a.N * scb, kTileN, a.gb,
+              CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qz, a.N / PER, (uint64_t)n_experts * G,
+              (uint64_t)(a.N / PER) * 4, kTileN / PER, a.gb, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+    set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed");
     return QL_ERR_CUDA;
   }
-  auto kern = gptq_gemm_tc_kernel<BITS, BT, NS>;
-  const int smem = SmemLayout<BT, NS>::kBytes;
+  auto kern = gptq_gemm_tc_kernel<BITS, NS>;
+  const int smem = L::kBytes;
   static int configured_dev = -1;
   static int sms = 0;
   int dev = 0;
@@ -423,7 +460,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, cudaStream_t st) {
   }
   const int ntiles = a.n_wtiles * a.n_ttiles;   // grouped mode: n_ttiles is the table's capacity
   const int grid = ntiles < sms ? ntiles : sms;
-  kern<<<grid, kThreads, smem, st>>>(tmap, a);
+  kern<<<grid, kThreads, smem, st>>>(tx, tw, ts, tz, a);
   return cuda_status(cudaGetLastError(), "gptq_gemm_tc launch");
 }
 
@@ -447,6 +484,8 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
                     void* workspace, size_t ws_bytes, bool* handled) {
   *handled = false;
   if (!gemm_path_taken(M, K, gs)) return QL_OK;
+  // TMA of the zero points: rows of N / per words must be whole 16-byte units, 16-byte aligned
+  if (N % (4 * (32 / bits)) != 0 || (reinterpret_cast<uintptr_t>(qzeros) & 15)) return QL_OK;
   *handled = true;
   const size_t need = gptq_gemm_workspace(M, K);
   void* ws = workspace;
@@ -475,13 +514,9 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
     a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
     a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
     a.n_wtiles = (N + kTileN - 1) / kTileN;
-    if (M <= 128) {
-      a.n_ttiles = (M + 127) / 128;
-      rc = bits == 4 ? launch_gemm<4, 128, 8>(a, x16, st) : launch_gemm<8, 128, 8>(a, x16, st);
-    } else {
-      a.n_ttiles = (M + 255) / 256;
-      rc = bits == 4 ? launch_gemm<4, 256, 4>(a, x16, st) : launch_gemm<8, 256, 4>(a, x16, st);
-    }
+    a.n_ttiles = (M + kBT - 1) / kBT;
+    a.gb = gs == 32 ? 2 : 1;
+    rc = bits == 4 ? launch_gemm<4>(a, x16, 1, st) : launch_gemm<8>(a, x16, 1, st);
   }
   if (owned) {
     const int rc2 = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(workspace)");
@@ -495,14 +530,16 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
 int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_map, int P, const int32_t* qweight,
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
-                      int max_tiles, int tile_rows_n, void* out, int out_dtype, long ldo, int K, int N, int gs,
-                      int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st) {
-  if (K % kSlabK != 0 || (gs % 64 != 0 && gs != 32)) {
-    set_error("grouped GEMM: K=%d must be a multiple of 64 and gs=%d a multiple of 64 or 32", K, gs);
+                      int max_tiles, int tile_rows_n, int n_experts, void* out, int out_dtype, long ldo, int K,
+                      int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  if (K % kSlabK != 0 || (gs % 64 != 0 && gs != 32) || N % (4 * (32 / bits)) != 0 ||
+      (reinterpret_cast<uintptr_t>(qzeros) & 15)) {
+    set_error("grouped GEMM: K=%d must be a multiple of 64, gs=%d a multiple of 64 or 32, N=%d of 32 (int4) / 16 "
+              "(int8), qzeros 16-byte aligned", K, gs, N);
     return QL_ERR_UNSUPPORTED;
   }
-  if (tile_rows_n != 128 && tile_rows_n != 256) {
-    set_error("grouped GEMM: tile rows must be 128 or 256 (got %d)", tile_rows_n);
+  if (tile_rows_n != kBT) {
+    set_error("grouped GEMM: tile rows must be %d (got %d)", kBT, tile_rows_n);
     return QL_ERR_ARG;
   }
   const size_t need = gptq_gemm_workspace(P, K);
@@ -529,9 +566,8 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
   a.n_ttiles = max_tiles;
   a.tiles = tiles; a.n_tiles = n_tiles; a.offsets = offsets;
   a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
-  if (tile_rows_n == 128)
-    return bits == 4 ? launch_gemm<4, 128, 8>(a, x16, st) : launch_gemm<8, 128, 8>(a, x16, st);
-  return bits == 4 ? launch_gemm<4, 256, 4>(a, x16, st) : launch_gemm<8, 256, 4>(a, x16, st);
+  a.gb = gs == 32 ? 2 : 1;
+  return bits == 4 ? launch_gemm<4>(a, x16, n_experts, st) : launch_gemm<8>(a, x16, n_experts, st);
 }
 
 int take_tc_status() {

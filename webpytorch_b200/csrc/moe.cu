@@ -306,8 +306,8 @@ int gptq_gemv_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_row
 int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_map, int P, const int32_t* qweight,
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
-                      int max_tiles, int tile_rows_n, void* out, int out_dtype, long ldo, int K, int N, int gs,
-                      int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st);
+                      int max_tiles, int tile_rows_n, int n_experts, void* out, int out_dtype, long ldo, int K,
+                      int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st);
 size_t gptq_gemm_workspace(int M, int K);
 }  // namespace ql
 
@@ -368,8 +368,8 @@ extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const
       return QL_ERR_ARG;
     }
     int rc = gptq_gemm_grouped(x, x_dtype, ldx, row_token, (int)P, qweight, qzeros, scales, scales_dtype, qw_es,
-                               qz_es, sc_es, offsets, tiles, n_tiles, max_tiles, tile_rows, out, out_dtype, ldo, K,
-                               N, gs, bits, zero_offset, workspace, workspace_bytes, st);
+                               qz_es, sc_es, offsets, tiles, n_tiles, max_tiles, tile_rows, E, out, out_dtype, ldo,
+                               K, N, gs, bits, zero_offset, workspace, workspace_bytes, st);
     if (rc != QL_ERR_UNSUPPORTED) return rc;
   }
   const int max_active = (int)(P < E ? P : E);
