@@ -53,20 +53,62 @@ constexpr int kEpilogueWarp0 = 12;
 // ---------------------------------------------------------------------------------------
 // activation staging: fp16, power-of-two row scale, act-order gather, (j, j+4) pair order
 // ---------------------------------------------------------------------------------------
+// Position of value j of an 8-value block in the staging: int4 words pair (j, j+4) of each
+// 8-block, int8 words pair (j, j+2) of each 4-block (the order the register unpack produces).
+template <int BITS>
+__device__ __forceinline__ int pair_pos(int j) {
+  return BITS == 4 ? (j & 3) * 2 + (j >> 2) : (j & 4) + (j & 1) * 2 + ((j >> 1) & 1);
+}
+
+// Largest |value| of a 16-byte vector of x_dtype elements.
+__device__ __forceinline__ float absmax16(uint4 u, int x_dtype) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (x_dtype == QL_F32) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[i])));
+    } else if (x_dtype == QL_BF16) {
+      m = fmaxf(m, fmaxf(fabsf(__uint_as_float(w[i] << 16)), fabsf(__uint_as_float(w[i] & 0xffff0000u))));
+    } else {
+      const float2 f = __half22float2(u32_as_h2(w[i]));
+      m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  return m;
+}
+
+constexpr int kPrepSmemMax = 96 * 1024;   // rows up to this many bytes are staged through smem
+
+// One CTA per row: the row is copied into shared memory with 16-byte loads (taking the row
+// maximum on the way), then gathered through the act-order permutation from shared memory.
 template <int BITS>
 __global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x, int x_dtype, long ldx,
                                                      const int32_t* __restrict__ perm,
                                                      const int32_t* __restrict__ row_map, int M, int K,
                                                      __half* __restrict__ x16, int* __restrict__ row_exp) {
+  extern __shared__ __align__(16) unsigned char xrow[];
   __shared__ float wmax[8];
   __shared__ int sh_e;
   const int m = blockIdx.x;
   const int tid = threadIdx.x;
-  const long base = (long)(row_map ? row_map[m] : m) * ldx;   // row_map: MoE token gather
+  const int esz = x_dtype == QL_F32 ? 4 : 2;
+  const long row = row_map ? row_map[m] : m;   // row_map: MoE token gather
+  const unsigned char* src = reinterpret_cast<const unsigned char*>(x) + (size_t)row * ldx * esz;
   float mx = 0.f;
-  for (int k = tid; k < K; k += blockDim.x) {
-    const int src = perm ? perm[k] : k;
-    mx = fmaxf(mx, fabsf(load_as_float(x, x_dtype, base + src)));
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {   // K * esz is a multiple of 128 (K % 64 == 0)
+    for (int i = tid; i < K * esz / 16; i += blockDim.x) {
+      const uint4 u = reinterpret_cast<const uint4*>(src)[i];
+      reinterpret_cast<uint4*>(xrow)[i] = u;
+      mx = fmaxf(mx, absmax16(u, x_dtype));
+    }
+  } else {
+    for (int k = tid; k < K; k += blockDim.x) {
+      const float v = load_as_float(x, x_dtype, row * ldx + k);
+      if (esz == 4) reinterpret_cast<float*>(xrow)[k] = v;
+      else reinterpret_cast<uint16_t*>(xrow)[k] = reinterpret_cast<const uint16_t*>(src)[k];
+      mx = fmaxf(mx, fabsf(v));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -85,13 +127,79 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x,
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = b * 8 + j;
-      const int src = perm ? perm[k] : k;
-      // int4 words pair (j, j+4) of each 8-block; int8 words pair (j, j+2) of each 4-block
-      const int pos = BITS == 4 ? (j & 3) * 2 + (j >> 2) : (j & 4) + (j & 1) * 2 + ((j >> 1) & 1);
-      h[pos] = __float2half_rn(load_as_float(x, x_dtype, base + src) * s);
+      const int srck = perm ? perm[k] : k;
+      h[pair_pos<BITS>(j)] = __float2half_rn(load_as_float(xrow, x_dtype, srck) * s);
     }
     *reinterpret_cast<uint4*>(x16 + (long)m * K + b * 8) = *reinterpret_cast<uint4*>(h);
   }
+}
+
+// The same for rows larger than kPrepSmemMax: gathers straight from global memory.
+template <int BITS>
+__global__ void __launch_bounds__(256) prep_x_global_kernel(const void* __restrict__ x, int x_dtype, long ldx,
+                                                            const int32_t* __restrict__ perm,
+                                                            const int32_t* __restrict__ row_map, int M, int K,
+                                                            __half* __restrict__ x16, int* __restrict__ row_exp) {
+  __shared__ float wmax[8];
+  __shared__ int sh_e;
+  const int m = blockIdx.x;
+  const int tid = threadIdx.x;
+  const long base = (long)(row_map ? row_map[m] : m) * ldx;
+  float mx = 0.f;
+  for (int k = tid; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(load_as_float(x, x_dtype, base + k)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) wmax[tid >> 5] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float v = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) v = fmaxf(v, wmax[i]);
+    sh_e = stage_exponent(v);
+    row_exp[m] = sh_e;
+  }
+  __syncthreads();
+  const float s = exp2i(-sh_e);
+  for (int b = tid; b < K / 8; b += blockDim.x) {
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = b * 8 + j;
+      const int src = perm ? perm[k] : k;
+      h[pair_pos<BITS>(j)] = __float2half_rn(load_as_float(x, x_dtype, base + src) * s);
+    }
+    *reinterpret_cast<uint4*>(x16 + (long)m * K + b * 8) = *reinterpret_cast<uint4*>(h);
+  }
+}
+
+// Launch the activation staging for M rows.
+int launch_prep_x(int bits, const void* x, int x_dtype, long ldx, const int32_t* perm, const int32_t* row_map, int M,
+                  int K, __half* x16, int* row_exp, cudaStream_t st) {
+  const size_t bytes = (size_t)K * (x_dtype == QL_F32 ? 4 : 2);
+  static int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    int rc = cuda_status(cudaFuncSetAttribute(prep_x_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              kPrepSmemMax),
+                         "cudaFuncSetAttribute(prep_x)");
+    if (!rc)
+      rc = cuda_status(cudaFuncSetAttribute(prep_x_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kPrepSmemMax),
+                       "cudaFuncSetAttribute(prep_x)");
+    if (rc) return rc;
+    configured_dev = dev;
+  }
+  if (bytes <= (size_t)kPrepSmemMax) {
+    if (bits == 4)
+      prep_x_kernel<4><<<M, 256, bytes, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+    else
+      prep_x_kernel<8><<<M, 256, bytes, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+  } else if (bits == 4) {
+    prep_x_global_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+  } else {
+    prep_x_global_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+  }
+  return cuda_status(cudaGetLastError(), "prep_x launch");
 }
 
 // ---------------------------------------------------------------------------------------
@@ -501,11 +609,7 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
   }
   __half* x16 = reinterpret_cast<__half*>(ws);
   int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * K * 2 + 255) & ~(size_t)255));
-  if (bits == 4)
-    prep_x_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, nullptr, M, K, x16, row_exp);
-  else
-    prep_x_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, x_perm, nullptr, M, K, x16, row_exp);
-  int rc = cuda_status(cudaGetLastError(), "prep_x launch");
+  int rc = launch_prep_x(bits, x, x_dtype, ldx, x_perm, nullptr, M, K, x16, row_exp, st);
   if (!rc) {
     GemmArgs a = {};
     a.qw = reinterpret_cast<const uint32_t*>(qweight);
@@ -550,11 +654,7 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
   __half* x16 = reinterpret_cast<__half*>(workspace);
   int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + (((size_t)P * K * 2 + 255) & ~(size_t)255));
   if (P == 0) return QL_OK;
-  if (bits == 4)
-    prep_x_kernel<4><<<P, 256, 0, st>>>(x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp);
-  else
-    prep_x_kernel<8><<<P, 256, 0, st>>>(x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp);
-  int rc = cuda_status(cudaGetLastError(), "prep_x launch");
+  int rc = launch_prep_x(bits, x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp, st);
   if (rc) return rc;
   GemmArgs a = {};
   a.qw = reinterpret_cast<const uint32_t*>(qweight);
