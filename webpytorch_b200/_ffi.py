@@ -74,7 +74,7 @@ def load(build_if_missing=True):
     global _lib
     if _lib is not None:
         return _lib
-    path = _build.LIB
+    path = os.environ.get("QL_LIBRARY", _build.LIB)   # a library built elsewhere (same ABI)
     if not os.path.exists(path):
         if not build_if_missing:
             raise RuntimeError("libqlinear.so is not built (run webpytorch_b200._build.build())")

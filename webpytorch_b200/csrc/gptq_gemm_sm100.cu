@@ -245,11 +245,11 @@ __device__ __forceinline__ TileRows tile_rows(const GemmArgs& a, int tt, int BT)
   return r;
 }
 
-template <int BITS, int NS>
+template <int BITS, int NS, int BT>
 struct SmemLayout {
   static constexpr int PER = 32 / BITS;
   static constexpr int ROWS = kSlabK / PER;                // packed rows per slab (8 int4 / 16 int8)
-  static constexpr int kXBytes = kBT * kSlabK * 2;         // activation tile, 128-byte swizzled rows
+  static constexpr int kXBytes = BT * kSlabK * 2;          // activation tile, 128-byte swizzled rows
   static constexpr int kWOff = kXBytes;
   static constexpr int kWBytes = ROWS * kTileN * 4;        // packed weights [ROWS][128]
   static constexpr int kSOff = kWOff + kWBytes;
@@ -286,18 +286,22 @@ __device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, ui
   out2[1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)), s2));
 }
 
-template <int BITS, int NS>
+// BT = tokens per tile (MMA N). BT = 128 keeps two accumulators in TMEM (the epilogue drains one
+// while the next tile's MMAs fill the other); BT = 256 halves the dequant work per MMA flop with
+// one accumulator (the next tile waits for the drain into registers).
+template <int BITS, int NS, int BT>
 __global__ void __launch_bounds__(kThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const GemmArgs a) {
-  using L = SmemLayout<BITS, NS>;
+  using L = SmemLayout<BITS, NS, BT>;
   constexpr int PER = L::PER;
   constexpr int ROWS = L::ROWS;
   constexpr int HROWS = ROWS / 2;               // packed rows per dequant half
   constexpr int TCOLS_A = kSlabK / 2;           // TMEM columns per A stage (fp16 pairs)
-  constexpr int A_COL = 2 * kBT;                // A stages start after the two accumulators
-  constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, kBT);
+  constexpr int ND = BT == 128 ? 2 : 1;         // accumulator buffers
+  constexpr int A_COL = ND * BT;                // A stages start after the accumulators
+  constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, BT);
   constexpr uint32_t MASK = (1u << BITS) - 1u;
   static_assert(A_COL + NS * TCOLS_A <= 512, "TMEM budget");
 
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
         const int wt = tile % a.n_wtiles;
-        const TileRows tr = tile_rows(a, tile / a.n_wtiles, kBT);
+        const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
         const int wrow0 = tr.e * (a.K / PER), grow0 = tr.e * G;
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
@@ -385,8 +389,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0, tcount = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tcount) {
-        const int b = tcount & 1;
-        if (!ptx::mbar_wait(d_empty(b), ((tcount >> 1) & 1) ^ 1, abort_flag)) break;
+        const int b = ND == 2 ? (tcount & 1) : 0;
+        const int use = ND == 2 ? (tcount >> 1) : tcount;   // earlier uses of this buffer
+        if (!ptx::mbar_wait(d_empty(b), (use & 1) ^ 1, abort_flag)) break;
         ptx::tc_fence_after();
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
@@ -399,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t xs = sbase + s * L::kStageBytes;
 #pragma unroll
           for (int j = 0; j < kSlabK / 16; ++j) {
-            ptx::mma_f16_ts(tmem + b * kBT, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
+            ptx::mma_f16_ts(tmem + b * BT, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
                             IDESC, (kb | j) != 0);
           }
           ptx::mma_commit(slab_free(s));  // frees the stage's shared memory and its TMEM A columns
@@ -455,25 +460,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     int tcount = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
-      const int b = tcount & 1;
+      const int b = ND == 2 ? (tcount & 1) : 0;
+      const int use = ND == 2 ? (tcount >> 1) : tcount;
       const int wt = tile % a.n_wtiles;
-      const TileRows tr = tile_rows(a, tile / a.n_wtiles, kBT);
+      const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
       const int n = wt * kTileN + lrow;
       const float bias = (a.bias && n < a.N) ? a.bias[n] : 0.f;
-      int rexp[kBT / 32];   // row exponent of token c * 32 + lane (broadcast with shuffles below)
+      int rexp[BT / 32];   // row exponent of token c * 32 + lane (broadcast with shuffles below)
 #pragma unroll
-      for (int c = 0; c < kBT / 32; ++c) {
+      for (int c = 0; c < BT / 32; ++c) {
         const int tok = tr.row0 + c * 32 + lane;
         rexp[c] = tok < tr.row_end ? a.row_exp[tok] : 0;
       }
-      if (!ptx::mbar_wait(d_full(b), (tcount >> 1) & 1, abort_flag)) goto done;
+      if (!ptx::mbar_wait(d_full(b), use & 1, abort_flag)) goto done;
       ptx::tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kBT / 32; ++c) {
+      for (int c = 0; c < BT / 32; ++c) {
         uint32_t v[32];
-        ptx::tmem_ld32(lane_addr + b * kBT + c * 32, v);
+        ptx::tmem_ld32(lane_addr + b * BT + c * 32, v);
         ptx::tmem_wait_ld();
-        if (c == kBT / 32 - 1) {
+        if (c == BT / 32 - 1) {
           ptx::tc_fence_before();
           ptx::mbar_arrive(d_empty(b));  // accumulator drained into registers
         }
@@ -526,11 +532,11 @@ bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const voi
 }
 
 // n_experts: stacked weight matrices (grouped mode), 1 otherwise.
-template <int BITS>
+template <int BITS, int BT>
 int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
-  constexpr int NS = BITS == 4 ? 8 : 7;
+  constexpr int NS = BT == 128 ? (BITS == 4 ? 8 : 7) : 4;
   constexpr int PER = 32 / BITS;
-  using L = SmemLayout<BITS, NS>;
+  using L = SmemLayout<BITS, NS, BT>;
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled is unavailable");
@@ -542,7 +548,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_
                                   : a.sc_dtype == QL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tx, tw, ts, tz;
-  if (!encode(enc, &tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, a.K, a.M, (uint64_t)a.K * 2, kSlabK, kBT,
+  if (!encode(enc, &tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, a.K, a.M, (uint64_t)a.K * 2, kSlabK, BT,
               CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode(enc, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qw, a.N, (uint64_t)n_experts * (a.K / PER),
               (uint64_t)a.N * 4, kTileN, L::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
@@ -553,7 +559,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed");
     return QL_ERR_CUDA;
   }
-  auto kern = gptq_gemm_tc_kernel<BITS, NS>;
+  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT>;
   const int smem = L::kBytes;
   static int configured_dev = -1;
   static int sms = 0;
@@ -618,9 +624,17 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
     a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
     a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
     a.n_wtiles = (N + kTileN - 1) / kTileN;
-    a.n_ttiles = (M + kBT - 1) / kBT;
     a.gb = gs == 32 ? 2 : 1;
-    rc = bits == 4 ? launch_gemm<4>(a, x16, 1, st) : launch_gemm<8>(a, x16, 1, st);
+    // 256-token tiles once they still give every SM a tile; 128 below (small M)
+    static int min_m256 = -1;
+    if (min_m256 < 0) min_m256 = env_int("QL_GEMM_BT256_MIN_M", 1 << 30);   // measured slower so far
+    if (M >= min_m256) {
+      a.n_ttiles = (M + 255) / 256;
+      rc = bits == 4 ? launch_gemm<4, 256>(a, x16, 1, st) : launch_gemm<8, 256>(a, x16, 1, st);
+    } else {
+      a.n_ttiles = (M + 127) / 128;
+      rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
+    }
   }
   if (owned) {
     const int rc2 = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(workspace)");
@@ -667,7 +681,7 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
   a.tiles = tiles; a.n_tiles = n_tiles; a.offsets = offsets;
   a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
   a.gb = gs == 32 ? 2 : 1;
-  return bits == 4 ? launch_gemm<4>(a, x16, n_experts, st) : launch_gemm<8>(a, x16, n_experts, st);
+  return bits == 4 ? launch_gemm<4, 128>(a, x16, n_experts, st) : launch_gemm<8, 128>(a, x16, n_experts, st);
 }
 
 int take_tc_status() {
