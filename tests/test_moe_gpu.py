@@ -195,3 +195,43 @@ def test_moe_step_replays_in_a_cuda_graph():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("E,K,N,T,k,bits,gs", [
+    (16, 256, 256, 12, 8, 4, 64),     # cluster split over 2 stages, 16-row chunks
+    (16, 128, 256, 12, 8, 4, 64),     # one stage, no split
+    (8, 256, 256, 5, 2, 4, 64),
+    (8, 1024, 512, 3, 2, 4, 128),
+    (8, 1024, 512, 12, 4, 8, 128),
+    (4, 2048, 1536, 40, 2, 4, 128),   # more rows than a chunk: several chunks per expert
+])
+@pytest.mark.parametrize("xdtype,gather", [(torch.float16, True), (torch.float32, True), (torch.float32, False)])
+@pytest.mark.parametrize("table", ["chosen", "128"])
+def test_grouped_matmul_vs_dense_per_expert(E, K, N, T, k, bits, gs, xdtype, gather, table):
+    """Every expert's sorted rows of ql_moe_grouped_matmul equal the dense operator on its weights
+    (rows gathered through row_token, or read in sorted order directly), with the tile table the
+    call asks for (tensor-core GEMM or decode GEMV) and with 128-row tiles (other paths)."""
+    exps = synth.moe_experts(E, K, N, bits=bits, gs=gs, seed=E * T + K)
+    experts = [{"gate": _ql(e["gate"], gs, bits), "up": _ql(e["up"], gs, bits), "down": _ql(e["down"], gs, bits)}
+               for e in exps]
+    w = moe.StackedExperts(experts, ("gate",), DEV)
+    rng = np.random.default_rng(T)
+    logits = torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).to(DEV)
+    x = torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32)).to(DEV).to(xdtype)
+    tr = moe.tile_rows_for(T * k, E, K, gs, T) if table == "chosen" else moe.TILE_ROWS
+    r = moe.route(logits, k, True, tr)
+    rows = r.row_token[:r.P].long()
+    if gather:
+        y = moe.grouped_matmul(x, r.row_token, r, w)
+    else:
+        xs = x[rows].contiguous()          # rows already in sorted order
+        y = moe.grouped_matmul(xs, None, r, w)
+    torch.cuda.synchronize()
+    offs = r.offsets.cpu().numpy()
+    rows = rows.cpu().numpy()
+    for e in range(E):
+        if offs[e + 1] == offs[e]:
+            continue
+        ref = experts[e]["gate"](x[torch.from_numpy(rows[offs[e]:offs[e + 1]]).long().to(DEV)])
+        got = y[offs[e]:offs[e + 1]]
+        assert max_rel_err(got.cpu().numpy(), ref.cpu().numpy()) < TOL, (e, offs[e + 1] - offs[e])

@@ -38,7 +38,7 @@ class OracleBackend:
         idx, w = om.route(logits.numpy(), top_k, norm)
         return torch.from_numpy(idx.astype(np.int32)), torch.from_numpy(w.astype(np.float32))
 
-    def group(self, ids, G):
+    def group(self, ids, G, tile_rows=128):
         ids = ids.numpy()
         row_src = np.argsort(ids, kind="stable").astype(np.int32)
         pos_of = np.empty_like(row_src)

@@ -41,6 +41,7 @@ SIGNATURES = {
     "ql_moe_group": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _vp, _vp,
                               _vp]),
     "ql_moe_grouped_workspace": (ctypes.c_size_t, [_c_long, _c_int, _c_int, _c_int]),
+    "ql_moe_tile_rows": (_c_int, [_c_long, _c_int, _c_int, _c_int, _c_int]),
     "ql_moe_grouped_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _c_long, _vp, _vp, _vp, _c_int, _c_int, _vp,
                                        _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_long, _c_int,
                                        _c_int, _c_int, _c_int, _c_float, _vp, ctypes.c_size_t, _vp]),

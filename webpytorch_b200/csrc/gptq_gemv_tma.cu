@@ -48,7 +48,7 @@ constexpr int kStageK = 128;           // K per ring stage
 
 struct TmaGemvArgs {
   const void* x;
-  const int32_t* x_rows;   // unused here (always null): row gathers take the register-fed kernel
+  const int32_t* x_rows;   // NULL, or the x row of each output row (MoE token gather)
   const int32_t* x_perm;
   long ldx;
   int x_dtype;
@@ -63,6 +63,26 @@ struct TmaGemvArgs {
   int cs;       // cluster size along K
   int sw;       // 32-column strips per CTA (8 or 4; host-side choice)
   float zoff;
+  // grouped (MoE) mode when g_offsets != NULL: blockIdx.z is an entry of the device-built tile
+  // table (expert e = g_tiles[2z], first row g_tiles[2z + 1] of its segment, MAXM rows at
+  // most); the expert's weights start at packed row e * g_wrows and group row e * g_grows
+  const int32_t* g_offsets;
+  const int32_t* g_tiles;
+  const int32_t* g_n_tiles;
+  int g_wrows, g_grows;
+  int g_max_tiles;  // host: table capacity (grid z)
+  int n_experts;    // host: stacked weight matrices (1 when dense)
+};
+
+// Activation source of one CTA (its rows of x, possibly gathered).
+struct XSrc {
+  const void* x;
+  const int32_t* x_rows;
+  const int32_t* x_perm;
+  long ldx;
+  int x_dtype;
+  int x_vec;
+  int M;
 };
 
 template <int BITS, int GS, int NST, int SCB, int SW>
@@ -103,6 +123,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kBarOff + 16 * NST);
   const uint32_t bar_red = bar_full + 16 * NST + 8;   // partial sums received from the cluster
 
+  // grouped mode: which expert and rows this cluster takes (uniform over the cluster, which
+  // shares blockIdx.z); slots and chunks without rows leave before any barrier
+  int M = a.M, e = 0;
+  long row0 = 0;
+  if (a.g_offsets) {
+    const int tz = blockIdx.z;
+    if (tz >= *a.g_n_tiles) return;
+    e = a.g_tiles[2 * tz];
+    row0 = a.g_offsets[e] + a.g_tiles[2 * tz + 1];
+    M = min(MAXM, a.g_offsets[e + 1] - (int)row0);
+  }
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int rank = blockIdx.x;
@@ -113,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int nst_max = sq + (srem ? 1 : 0);
   const int klen_max = nst_max * kStageK;
   const int ng_max = nst_max * GPS;
-  const int M = a.M, N = a.N;
+  const int N = a.N;
   uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
   const int xs_bytes = (M * klen_max * 2 + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
@@ -151,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::tma_prefetch(&tmap_s);
       ptx::tma_prefetch(&tmap_z);
       const int strip0 = blockIdx.y * SW;
+      const int wrow0 = e * a.g_wrows, grow0 = e * a.g_grows;   // expert's first rows (0 when dense)
       int i = 0;
       bool ok = true;
       for (; i < nst; ++i) {
@@ -162,12 +194,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         const uint32_t st = sbase + s * L::kStageBytes;
         const uint32_t fb = bar_full + 8 * s;
-        const int srow = ((s0 + i) * kStageK) / a.gs;   // first scale/zero row of the stage
+        const int srow = grow0 + ((s0 + i) * kStageK) / a.gs;   // first scale/zero row of the stage
         ptx::mbar_arrive_expect_tx(fb, L::kWBytes + L::kScBytes + L::kZBytes);
         asm volatile(
             "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
             "[%2];" ::"r"(st),
-            "l"(reinterpret_cast<uint64_t>(&tmap_w)), "r"(fb), "r"(0), "r"((s0 + i) * L::ROWS), "r"(strip0)
+            "l"(reinterpret_cast<uint64_t>(&tmap_w)), "r"(fb), "r"(0), "r"(wrow0 + (s0 + i) * L::ROWS), "r"(strip0)
             : "memory");
         ptx::tma_load_2d(st + L::kWBytes, &tmap_s, fb, blockIdx.y * TC, srow);
         ptx::tma_load_2d(st + L::kWBytes + L::kScBytes, &tmap_z, fb, blockIdx.y * (TC / PER), srow);
@@ -193,7 +225,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int slots = 2 * M;
     const int zoff = (int)a.zoff;
     pdl_wait();   // x may be the previous kernel's output
-    gemv::stage_x_i8<BITS, GS, true>(a, s0 * kStageK, klen, ng_max, xb, gsum, sh_exp, sh_max, tid, kCW * 32);
+    // this CTA's rows: gathered through x_rows, else x itself from row row0 on
+    const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
+    const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
+                    a.ldx, a.x_dtype, a.x_vec, M};
+    gemv::stage_x_i8<BITS, GS, true>(xsrc, s0 * kStageK, klen, ng_max, xb, gsum, sh_exp, sh_max, tid, kCW * 32);
 
     float acc[NQ][4];
 #pragma unroll
@@ -327,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < 4; ++c) {
             float v = finish(tok, acc[mq][c]);
             if (a.bias) v += a.bias[c0 + c];
-            store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + c0 + c, v);
+            store_from_float(a.out, a.out_dtype, (row0 + tok) * a.ldo + c0 + c, v);
           }
         }
       }
@@ -365,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int col = blockIdx.y * TC + oq0 * 4 + c;
         if (col < N) {
           if (a.bias) v += a.bias[col];
-          store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + col, v);
+          store_from_float(a.out, a.out_dtype, (row0 + tok) * a.ldo + col, v);
         }
       }
     }
@@ -409,7 +445,7 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   if (!enc) return -1;
   CUtensorMap tw, ts, tz;
   {
-    const cuuint64_t dims[3] = {32, (cuuint64_t)(a.K / L::PER), (cuuint64_t)(a.N / 32)};
+    const cuuint64_t dims[3] = {32, (cuuint64_t)a.n_experts * (a.K / L::PER), (cuuint64_t)(a.N / 32)};
     const cuuint64_t strides[2] = {(cuuint64_t)a.N * 4, 128};
     const cuuint32_t box[3] = {32, (cuuint32_t)L::ROWS, (cuuint32_t)SW};
     const cuuint32_t estr[3] = {1, 1, 1};
@@ -422,8 +458,9 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   const CUtensorMapDataType sdt = SCB == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                            : (a.sc_dtype == QL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-  if (!encode_2d(enc, &ts, sdt, scales, a.N, G, (uint64_t)a.N * SCB, TC, L::GPS)) return -1;
-  if (!encode_2d(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, qzeros, a.N / L::PER, G, (uint64_t)(a.N / L::PER) * 4,
+  if (!encode_2d(enc, &ts, sdt, scales, a.N, (uint64_t)a.n_experts * G, (uint64_t)a.N * SCB, TC, L::GPS)) return -1;
+  if (!encode_2d(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, qzeros, a.N / L::PER, (uint64_t)a.n_experts * G,
+                 (uint64_t)(a.N / L::PER) * 4,
                  TC / L::PER, L::GPS))
     return -1;
   auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB, SW>;
@@ -446,7 +483,7 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
     configured_dev = dev;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.cs, (a.N + TC - 1) / TC, 1);
+  cfg.gridDim = dim3(a.cs, (a.N + TC - 1) / TC, a.g_offsets ? a.g_max_tiles : 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -494,6 +531,33 @@ int tma_gs(const TmaGemvArgs& a, int kgs, const uint32_t* qw, const uint32_t* qz
   }
 }
 
+// Tile width (a.sw) and cluster size (a.cs, the K split): the CTA count tiles * zdim * cs should
+// fill resident waves of ctas_per_sm CTAs per SM as evenly as possible (the busiest SM sets the
+// time); the wider tile wins ties (fewer partial sums to reduce).
+void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_sm, int max_cluster) {
+  int cs = 1, sw = 8;
+  double best = -1.0;
+  const int slots = sms * ctas_per_sm;
+  for (int w = 8; w >= 4; w /= 2) {
+    const int tiles = (N + 32 * w - 1) / (32 * w) * zdim;
+    for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
+      const int ctas = tiles * c;
+      if (ctas > slots && c > 1) break;
+      if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;
+      const double waves = (double)ctas / slots;
+      const double busiest = (double)((ctas + slots - 1) / slots);
+      const double score = waves / busiest * (ctas < slots ? (double)ctas / slots : 1.0);
+      if (score > best + 1e-9) {
+        best = score;
+        cs = c;
+        sw = w;
+      }
+    }
+  }
+  a.sw = sw;
+  a.cs = cs;
+}
+
 }  // namespace
 
 // Returns true (and the launch status in *rc) when the TMA-fed GEMV handles this shape.
@@ -517,7 +581,8 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
       (reinterpret_cast<uintptr_t>(scales) & 15))
     return false;
   const int kgs = gs % 128 == 0 ? 128 : gs;
-  TmaGemvArgs a;
+  TmaGemvArgs a = {};
+  a.n_experts = 1;
   a.x = x; a.x_rows = nullptr; a.x_perm = x_perm; a.ldx = ldx; a.x_dtype = x_dtype;
   const int vec_elems = x_dtype == QL_F32 ? 4 : 8;
   a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
@@ -525,29 +590,50 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
-  // tile width and cluster size (K split): the CTA count tiles * cs should fill one resident
-  // wave of ctas_per_sm CTAs per SM as evenly as possible (the busiest SM sets the time); the
-  // wider tile wins ties (fewer partial sums to reduce)
-  int cs = 1, sw = 8;
-  double best = -1.0;
-  for (int w = 8; w >= 4; w /= 2) {
-    const int tiles = (N + 32 * w - 1) / (32 * w);
-    for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-      const int ctas = tiles * c;
-      if (ctas > sms * ctas_per_sm && c > 1) break;
-      if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;
-      const double per_sm = (double)ctas / sms;
-      const double busiest = (double)((ctas + sms - 1) / sms);
-      const double score = per_sm / busiest * (per_sm < ctas_per_sm ? per_sm / ctas_per_sm : 1.0);
-      if (score > best + 1e-9) {
-        best = score;
-        cs = c;
-        sw = w;
-      }
-    }
-  }
-  a.sw = sw;
-  a.cs = cs;
+  choose_split(a, N, M, 1, sms, ctas_per_sm, max_cluster);
+  const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
+  const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
+  const int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);
+  if (r < 0) return false;
+  *rc = r;
+  return true;
+}
+
+// Grouped (MoE) form: one launch over the tiles of a device-built table (tile_rows = 4, 8 or 16
+// rows of one expert per tile) for stacked weights (qweight [E][K/per][N], qzeros
+// [E][K/gs][N/per], scales [E][K/gs][N]); output row p of expert e's sorted rows is
+// x[x_rows[p]] (x[p] when x_rows is NULL) @ W_e.
+bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_rows, const int32_t* qweight,
+                           const int32_t* qzeros, const void* scales, int sc_dtype, int E, const int32_t* offsets,
+                           const int32_t* tiles, const int32_t* n_tiles, int max_tiles, int tile_rows, void* out,
+                           int out_dtype, long ldo, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
+                           int* rc) {
+  int sms = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (env_int("QL_GEMV_TMA", 1) == 0 || N % 32 != 0 || K % kStageK != 0 || (gs % 128 != 0 && gs != 32 && gs != 64))
+    return false;
+  if ((tile_rows != 4 && tile_rows != 8 && tile_rows != 16) || !tiles || !n_tiles || max_tiles <= 0) return false;
+  if ((reinterpret_cast<uintptr_t>(qweight) & 15) || (reinterpret_cast<uintptr_t>(qzeros) & 15) ||
+      (reinterpret_cast<uintptr_t>(scales) & 15))
+    return false;
+  const int kgs = gs % 128 == 0 ? 128 : gs;
+  const int per = 32 / bits;
+  TmaGemvArgs a = {};
+  a.x = x; a.x_rows = x_rows; a.x_perm = nullptr; a.ldx = ldx; a.x_dtype = x_dtype;
+  const int vec_elems = x_dtype == QL_F32 ? 4 : 8;
+  a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
+  a.sc_dtype = sc_dtype; a.bias = nullptr;
+  a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
+  a.M = tile_rows;   // rows per tile (selects NQ, sizes smem)
+  a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
+  a.nstage = K / kStageK;
+  a.g_offsets = offsets; a.g_tiles = tiles; a.g_n_tiles = n_tiles;
+  a.g_max_tiles = max_tiles;
+  a.g_wrows = K / per;
+  a.g_grows = K / gs;
+  a.n_experts = E;
+  choose_split(a, N, a.M, max_tiles, sms, 2, 8);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
   const int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);

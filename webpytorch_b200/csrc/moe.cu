@@ -309,6 +309,11 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
                       int max_tiles, int tile_rows_n, int n_experts, void* out, int out_dtype, long ldo, int K,
                       int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st);
 size_t gptq_gemm_workspace(int M, int K);
+bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_rows, const int32_t* qweight,
+                           const int32_t* qzeros, const void* scales, int sc_dtype, int E, const int32_t* offsets,
+                           const int32_t* tiles, const int32_t* n_tiles, int max_tiles, int tile_rows, void* out,
+                           int out_dtype, long ldo, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
+                           int* rc);
 }  // namespace ql
 
 // True when a grouped call over P rows and E experts takes the tensor-core GEMM: the average
@@ -318,6 +323,11 @@ static bool grouped_uses_gemm(long P, int E, int K, int gs) {
   if (min_avg < 0) min_avg = env_int("QL_MOE_GEMM_MIN_ROWS", 32);
   const long act = P < E ? P : E;
   return act > 0 && P >= (long)min_avg * act && K % 64 == 0 && (gs % 64 == 0 || gs == 32);
+}
+
+extern "C" int ql_moe_tile_rows(long P, int E, int K, int gs, int max_rows_per_expert) {
+  if (grouped_uses_gemm(P, E, K, gs)) return 128;
+  return max_rows_per_expert <= 4 ? 4 : max_rows_per_expert <= 8 ? 8 : 16;
 }
 
 extern "C" size_t ql_moe_grouped_workspace(long P, int E, int K, int gs) {
@@ -362,7 +372,7 @@ extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const
   if (P == 0) return QL_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const long qw_es = (long)(K / per) * N, qz_es = (long)(K / gs) * (N / per), sc_es = (long)(K / gs) * N;
-  if (grouped_uses_gemm(P, E, K, gs)) {
+  if (tile_rows == 128 && grouped_uses_gemm(P, E, K, gs)) {
     if (!tiles || !n_tiles || max_tiles <= 0) {
       set_error("ql_moe_grouped_matmul: the tensor-core path needs the routing tile table");
       return QL_ERR_ARG;
@@ -373,6 +383,11 @@ extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const
     if (rc != QL_ERR_UNSUPPORTED) return rc;
   }
   const int max_active = (int)(P < E ? P : E);
+  int trc = 0;
+  if (gptq_gemv_tma_grouped(x, x_dtype, ldx, row_token, qweight, qzeros, scales, scales_dtype, E, offsets, tiles,
+                            n_tiles, max_tiles, tile_rows, out, out_dtype, ldo, K, N, gs, bits, zero_offset, st,
+                            &trc))
+    return trc;
   return gptq_gemv_grouped(x, x_dtype, ldx, row_token, qweight, qzeros, scales, scales_dtype, qw_es, qz_es, sc_es,
                            offsets, active, n_active, max_active, max_rows_per_expert, out, out_dtype, ldo, K, N, gs,
                            bits, zero_offset, st);

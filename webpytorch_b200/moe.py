@@ -97,13 +97,20 @@ class StackedExperts:
         return self.nbytes() // self.E
 
 
+def tile_rows_for(P, E, K, gs, max_rows):
+    """Tile height of the routing table the grouped matmul wants for this call (128 for the
+    tensor-core GEMM, 4 / 8 / 16 for the decode GEMV)."""
+    return _ffi.load().ql_moe_tile_rows(P, E, K, gs, max_rows)
+
+
 class Routing:
     """Device buffers written by ql_moe_route for T tokens."""
 
-    def __init__(self, T, E, top_k, device):
+    def __init__(self, T, E, top_k, device, tile_rows=TILE_ROWS):
         P = T * top_k
         i32 = dict(dtype=torch.int32, device=device)
         self.T, self.E, self.top_k, self.P = T, E, top_k, P
+        self.tile_rows = tile_rows
         self.topk_idx = torch.empty((T, top_k), **i32)
         self.topk_w = torch.empty((T, top_k), dtype=torch.float32, device=device)
         self.counts = torch.empty(E, **i32)
@@ -111,21 +118,22 @@ class Routing:
         self.cursor = torch.empty(E, **i32)
         self.active = torch.empty(E, **i32)
         self.n_active = torch.empty(1, **i32)
-        self.max_tiles = P // TILE_ROWS + min(E, P) + 1
+        self.max_tiles = P // tile_rows + min(E, P) + 1
         self.tiles = torch.empty(2 * self.max_tiles, **i32)
         self.n_tiles = torch.empty(1, **i32)
         self.row_token = torch.empty(max(P, 1), **i32)
         self.pair_row = torch.empty((T, top_k), **i32)
 
 
-def route(logits, top_k, norm_topk_prob=True, stream=None):
-    """Device routing of [T, E] fp32 logits (lm_engine.py:299-307); returns a Routing."""
+def route(logits, top_k, norm_topk_prob=True, tile_rows=TILE_ROWS, stream=None):
+    """Device routing of [T, E] fp32 logits (lm_engine.py:299-307); returns a Routing whose tile
+    table has tiles of `tile_rows` rows."""
     if logits.dim() != 2:
         raise ValueError("logits must be [T, E]")
     logits = logits.to(torch.float32).contiguous()
     T, E = logits.shape
-    r = Routing(T, E, top_k, logits.device)
-    _ffi.call("ql_moe_route", _ffi.ptr(logits), T, E, top_k, int(bool(norm_topk_prob)), TILE_ROWS,
+    r = Routing(T, E, top_k, logits.device, tile_rows)
+    _ffi.call("ql_moe_route", _ffi.ptr(logits), T, E, top_k, int(bool(norm_topk_prob)), tile_rows,
               _ffi.ptr(r.topk_idx), _ffi.ptr(r.topk_w), _ffi.ptr(r.counts), _ffi.ptr(r.offsets),
               _ffi.ptr(r.cursor), _ffi.ptr(r.active), _ffi.ptr(r.n_active), _ffi.ptr(r.tiles),
               _ffi.ptr(r.n_tiles), r.max_tiles, _ffi.ptr(r.row_token), _ffi.ptr(r.pair_row),
@@ -145,7 +153,7 @@ def grouped_matmul(x, row_token, r, w, out_dtype=torch.float32, stream=None):
     _ffi.call("ql_moe_grouped_matmul", _ffi.ptr(x), _ffi.dtype_code(x.dtype), x.stride(0), _ffi.ptr(row_token),
               P, _ffi.ptr(w.qweight), _ffi.ptr(w.qzeros), _ffi.ptr(w.scales), _ffi.dtype_code(w.scales.dtype),
               w.E, _ffi.ptr(r.offsets), _ffi.ptr(r.active), _ffi.ptr(r.n_active), _ffi.ptr(r.tiles),
-              _ffi.ptr(r.n_tiles), r.max_tiles, TILE_ROWS, r.T, _ffi.ptr(y), _ffi.dtype_code(y.dtype),
+              _ffi.ptr(r.n_tiles), r.max_tiles, r.tile_rows, r.T, _ffi.ptr(y), _ffi.dtype_code(y.dtype),
               y.stride(0), w.K, w.N, w.gs, w.bits, float(w.zoff), _ffi.ptr(ws), ws_bytes, _ffi.stream_ptr(stream))
     return y
 
@@ -223,7 +231,7 @@ class MoEBlock(torch.nn.Module):
     def shared_ffn(self, x, stream=None):
         gu, dn = self.shared
         T = x.shape[0]
-        r1 = _single_expert_routing(T, x.device)
+        r1 = _single_expert_routing(T, x.device, tile_rows_for(T, 1, gu.K, gu.gs, T))
         y = grouped_matmul(x, None, r1, gu, stream=stream)
         a = act(y, self.SI, stream=stream)
         return grouped_matmul(a, None, r1, dn, stream=stream)
@@ -235,7 +243,8 @@ class MoEBlock(torch.nn.Module):
         T = x.shape[0]
         logits = self.router(x)
         logits = torch.as_tensor(logits, device=x.device).reshape(T, self.E)
-        r = route(logits, self.top_k, self.norm_topk_prob, stream)
+        tr = tile_rows_for(T * self.top_k, self.E, self.H, self.gate_up.gs, T)
+        r = route(logits, self.top_k, self.norm_topk_prob, tr, stream)
         z = self.expert_ffn(x, r, stream)
         ys = g = None
         if self.shared is not None:
@@ -259,19 +268,19 @@ class MoEBlock(torch.nn.Module):
 _single_cache = {}
 
 
-def _single_expert_routing(T, device):
+def _single_expert_routing(T, device, tile_rows=TILE_ROWS):
     """Routing of T tokens to one expert in token order (the shared expert): static buffers."""
-    key = (T, str(device))
+    key = (T, str(device), tile_rows)
     r = _single_cache.get(key)
     if r is None:
-        r = Routing(T, 1, 1, device)
+        r = Routing(T, 1, 1, device, tile_rows)
         r.offsets.copy_(torch.tensor([0, T], dtype=torch.int32))
         r.active.zero_()
         r.n_active.fill_(1 if T else 0)
-        n = (T + TILE_ROWS - 1) // TILE_ROWS
+        n = (T + tile_rows - 1) // tile_rows
         tiles = torch.zeros(2 * r.max_tiles, dtype=torch.int32)
         tiles[0:2 * n:2] = 0
-        tiles[1:2 * n:2] = torch.arange(n, dtype=torch.int32) * TILE_ROWS
+        tiles[1:2 * n:2] = torch.arange(n, dtype=torch.int32) * tile_rows
         r.tiles.copy_(tiles)
         r.n_tiles.fill_(n)
         _single_cache[key] = r

@@ -72,12 +72,12 @@ class CudaBackend:
         r = _moe.route(logits, top_k, norm)
         return r.topk_idx, r.topk_w
 
-    def group(self, ids, G):
-        """Sorted order of `ids` (values in [0, G)): (counts[G], row_src[n], pos_of[n])."""
+    def group(self, ids, G, tile_rows=_moe.TILE_ROWS):
+        """Sorted order of `ids` (values in [0, G)): (grouping, counts[G], row_src[n], pos_of[n])."""
         n = ids.numel()
-        r = _moe.Routing(n, G, 1, ids.device)
+        r = _moe.Routing(n, G, 1, ids.device, tile_rows)
         ids = ids.to(torch.int32).contiguous()
-        _ffi.call("ql_moe_group", _ffi.ptr(ids), n, G, _moe.TILE_ROWS, _ffi.ptr(r.counts), _ffi.ptr(r.offsets),
+        _ffi.call("ql_moe_group", _ffi.ptr(ids), n, G, tile_rows, _ffi.ptr(r.counts), _ffi.ptr(r.offsets),
                   _ffi.ptr(r.cursor), _ffi.ptr(r.active), _ffi.ptr(r.n_active), _ffi.ptr(r.tiles),
                   _ffi.ptr(r.n_tiles), r.max_tiles, _ffi.ptr(r.row_token), _ffi.ptr(r.pair_row.view(-1)),
                   _ffi.stream_ptr())
@@ -200,6 +200,12 @@ class ExpertParallelMoE(torch.nn.Module):
         self.Ep = E // self.P
         self.backend = backend or CudaBackend()
 
+    def _tile_rows(self, n):
+        """Tile height for grouping n received rows over the local experts (CUDA backend)."""
+        if not isinstance(self.backend, CudaBackend):
+            return _moe.TILE_ROWS
+        return _moe.tile_rows_for(n, self.Ep, self.H, getattr(self.gate_up, "gs", 128), n)
+
     def _all_to_all(self, out_rows, rows, out_splits, in_splits):
         if self.P == 1:
             return rows
@@ -230,7 +236,7 @@ class ExpertParallelMoE(torch.nn.Module):
         recv_x = self._all_to_all(torch.empty((n_recv, H), dtype=x.dtype, device=x.device), send_x, rc, sc)
         recv_e = self._all_to_all(torch.empty((n_recv,), dtype=torch.int32, device=x.device), send_e, rc, sc)
         # 3. local grouped expert FFN over the received rows
-        grouping, _, lsrc, lpos = be.group(recv_e, self.Ep)
+        grouping, _, lsrc, lpos = be.group(recv_e, self.Ep, self._tile_rows(n_recv))
         z_sorted = be.expert_ffn(recv_x, lsrc, grouping, self.gate_up, self.down, self.I)
         z_recv = z_sorted[lpos.long()]
         # 4. results back to the source ranks, in the order they were sent
