@@ -53,7 +53,8 @@ def _check_routing(r, logits, top_k, norm):
 
 
 @pytest.mark.parametrize("T,E,k,norm", [(1, 8, 2, True), (37, 64, 8, True), (300, 128, 8, False),
-                                        (5, 1000, 16, True), (64, 16, 1, True)])
+                                        (5, 1000, 16, True), (64, 16, 1, True),
+                                        (700, 64, 8, True), (2048, 128, 8, True)])   # multi-kernel route
 def test_route_matches_oracle(T, E, k, norm):
     rng = np.random.default_rng(T * 7 + E)
     logits = rng.standard_normal((T, E)).astype(np.float32)

@@ -28,15 +28,11 @@ namespace {
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 1024;
 
-__global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int norm,
-                                int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
-                                int32_t* __restrict__ counts) {
-  const int warps = blockDim.x >> 5;
-  const int t = blockIdx.x * warps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= T) return;
-  const float* row = logits + (long)t * E;
-  // softmax statistics: max and sum of exp (full softmax denominator, as the reference)
+// Top-k of one token's logits by one warp: softmax statistics over all E experts, then k
+// rounds of warp argmax (ties to the lower expert index). Lane j < k returns pick j in
+// (*idx, *w); the weights are the softmax probabilities, renormalised over the k when norm.
+__device__ __forceinline__ void topk_token(const float* __restrict__ row, int E, int k, int norm, int lane, int* idx,
+                                           float* w) {
   float mx = -INFINITY;
   for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
 #pragma unroll
@@ -45,7 +41,6 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, 
   for (int e = lane; e < E; e += 32) den += exp((double)row[e] - (double)mx);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-  // top-k by repeated argmax over the remaining logits
   int chosen[kMaxTopK];
   double pw[kMaxTopK];
   double psum = 0.0;
@@ -74,31 +69,41 @@ __global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, 
     pw[j] = exp((double)best - (double)mx) / den;
     psum += pw[j];
   }
+  *idx = 0;
+  *w = 0.f;
+  for (int j = 0; j < k; ++j)
+    if (j == lane) {
+      *idx = chosen[j];
+      *w = (float)(norm ? pw[j] / psum : pw[j]);
+    }
+}
+
+__global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int norm,
+                                int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                                int32_t* __restrict__ counts) {
+  const int warps = blockDim.x >> 5;
+  const int t = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  int my;
+  float w;
+  topk_token(logits + (long)t * E, E, k, norm, lane, &my, &w);
   if (lane < k) {
-    int my = 0;
-    double w = 0.0;
-    for (int j = 0; j < k; ++j)
-      if (j == lane) {
-        my = chosen[j];
-        w = pw[j];
-      }
     topk_idx[(long)t * k + lane] = my;
-    topk_w[(long)t * k + lane] = (float)(norm ? w / psum : w);
+    topk_w[(long)t * k + lane] = w;
     atomicAdd(&counts[my], 1);
   }
 }
 
-// One CTA, one thread per expert (E <= 1024): block-wide exclusive scans of the row counts
-// (-> segment offsets), of the active flags (-> compact active-expert list) and of the tile
-// counts (-> the grouped GEMM's tile table of `tile_rows`-row tiles); scatter cursors reset.
-__global__ void __launch_bounds__(1024) moe_scan_kernel(const int32_t* __restrict__ counts, int E, int tile_rows,
-                                                        int32_t* __restrict__ offsets, int32_t* __restrict__ cursor,
-                                                        int32_t* __restrict__ active, int32_t* __restrict__ n_active,
-                                                        int32_t* __restrict__ tiles, int32_t* __restrict__ n_tiles,
-                                                        int max_tiles) {
+// Block-wide scans over one thread per expert (blockDim >= E, a multiple of 32): exclusive
+// scans of the row counts (-> segment offsets), of the active flags (-> compact active-expert
+// list) and of the tile counts (-> the grouped matmul's tile table of `tile_rows`-row tiles).
+// Every thread of the block calls it; thread e gets its expert's offset back.
+__device__ int scan_experts(int c, int E, int tile_rows, int32_t* __restrict__ offsets, int32_t* __restrict__ active,
+                            int32_t* __restrict__ n_active, int32_t* __restrict__ tiles, int32_t* __restrict__ n_tiles,
+                            int max_tiles) {
   __shared__ int s_tot[3][32];
   const int e = threadIdx.x, lane = e & 31, w = e >> 5, nw = (blockDim.x + 31) >> 5;
-  const int c = e < E ? counts[e] : 0;
   const int v[3] = {c, c > 0 ? 1 : 0, (c + tile_rows - 1) / tile_rows};
   int inc[3] = {v[0], v[1], v[2]};
 #pragma unroll
@@ -131,7 +136,6 @@ __global__ void __launch_bounds__(1024) moe_scan_kernel(const int32_t* __restric
   for (int q = 0; q < 3; ++q) ex[q] = s_tot[q][w] + inc[q] - v[q];
   if (e < E) {
     offsets[e] = ex[0];
-    cursor[e] = 0;
     if (c > 0) active[ex[1]] = e;
     for (int i = 0; i < v[2]; ++i) {
       const int ti = ex[2] + i;
@@ -147,6 +151,18 @@ __global__ void __launch_bounds__(1024) moe_scan_kernel(const int32_t* __restric
       *n_tiles = nt < max_tiles ? nt : max_tiles;
     }
   }
+  return ex[0];
+}
+
+__global__ void __launch_bounds__(1024) moe_scan_kernel(const int32_t* __restrict__ counts, int E, int tile_rows,
+                                                        int32_t* __restrict__ offsets, int32_t* __restrict__ cursor,
+                                                        int32_t* __restrict__ active, int32_t* __restrict__ n_active,
+                                                        int32_t* __restrict__ tiles, int32_t* __restrict__ n_tiles,
+                                                        int max_tiles) {
+  const int e = threadIdx.x;
+  const int c = e < E ? counts[e] : 0;
+  scan_experts(c, E, tile_rows, offsets, active, n_active, tiles, n_tiles, max_tiles);
+  if (e < E) cursor[e] = 0;
 }
 
 __global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int T, int k, const int32_t* __restrict__ offsets,
@@ -158,6 +174,51 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int T, 
   const int r = offsets[e] + atomicAdd(&cursor[e], 1);
   row_token[r] = i / k;
   pair_row[i] = r;
+}
+
+// The whole route in one CTA for decode-sized batches (T * k <= kSmallPairs, E <= 1024): top-k
+// per token (one warp each), histogram in shared memory, the scans, and the scatter.
+constexpr int kSmallPairs = 4096;
+__global__ void __launch_bounds__(1024) moe_route_small_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                                               int norm, int tile_rows, int32_t* __restrict__ topk_idx,
+                                                               float* __restrict__ topk_w, int32_t* __restrict__ counts,
+                                                               int32_t* __restrict__ offsets, int32_t* __restrict__ active,
+                                                               int32_t* __restrict__ n_active, int32_t* __restrict__ tiles,
+                                                               int32_t* __restrict__ n_tiles, int max_tiles,
+                                                               int32_t* __restrict__ row_token,
+                                                               int32_t* __restrict__ pair_row) {
+  __shared__ int s_cnt[1024];
+  __shared__ int s_off[1024];
+  __shared__ int s_idx[kSmallPairs];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  if (tid < E) s_cnt[tid] = 0;
+  __syncthreads();
+  for (int t = warp; t < T; t += nw) {
+    int my;
+    float w;
+    topk_token(logits + (long)t * E, E, k, norm, lane, &my, &w);
+    if (lane < k) {
+      topk_idx[(long)t * k + lane] = my;
+      topk_w[(long)t * k + lane] = w;
+      s_idx[t * k + lane] = my;
+      atomicAdd(&s_cnt[my], 1);
+    }
+  }
+  __syncthreads();
+  const int c = tid < E ? s_cnt[tid] : 0;
+  if (tid < E) counts[tid] = c;
+  const int off = scan_experts(c, E, tile_rows, offsets, active, n_active, tiles, n_tiles, max_tiles);
+  if (tid < E) {
+    s_off[tid] = off;
+    s_cnt[tid] = 0;   // becomes the scatter cursor
+  }
+  __syncthreads();
+  for (int i = tid; i < T * k; i += blockDim.x) {
+    const int e = s_idx[i];
+    const int r = s_off[e] + atomicAdd(&s_cnt[e], 1);
+    row_token[r] = i / k;
+    pair_row[i] = r;
+  }
 }
 
 // Histogram of given group ids (expert-parallel dispatch and the receiving side's local grouping).
@@ -221,6 +282,12 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
     return QL_ERR_ARG;
   }
   cudaStream_t st = (cudaStream_t)stream;
+  if ((long)T * top_k <= kSmallPairs) {   // decode: one launch
+    moe_route_small_kernel<<<1, 1024, 0, st>>>(logits, T, E, top_k, norm_topk_prob, tile_rows, topk_idx, topk_w, counts,
+                                               offsets, active, n_active, tiles, n_tiles, max_tiles, row_token,
+                                               pair_row);
+    return cuda_status(cudaGetLastError(), "moe_route_small launch");
+  }
   int rc = cuda_status(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "ql_moe_route memset");
   if (rc) return rc;
   if (T > 0) {
@@ -320,7 +387,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
 // active expert then holds enough rows to fill a good part of a 128-row tile.
 static bool grouped_uses_gemm(long P, int E, int K, int gs) {
   static int min_avg = -1;
-  if (min_avg < 0) min_avg = env_int("QL_MOE_GEMM_MIN_ROWS", 32);
+  if (min_avg < 0) min_avg = env_int("QL_MOE_GEMM_MIN_ROWS", 12);   // measured crossover: 16 rows already faster
   const long act = P < E ? P : E;
   return act > 0 && P >= (long)min_avg * act && K % 64 == 0 && (gs % 64 == 0 || gs == 32);
 }
