@@ -20,9 +20,20 @@ __device__ __forceinline__ int chunk_pos(int j) {
   return (j / PER) * PER + stage_pos<PER>(j % PER);
 }
 
-// 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats.
+// silu(g) * u, as the MoE act kernel computes it (silu(v) = v / (1 + e^-v))
+__device__ __forceinline__ float swiglu(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+// 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats. With a.glu > 0
+// a row holds [gate | up] halves a.glu elements apart and the activation is silu(gate) * up.
 template <class Args>
 __device__ __forceinline__ void load_x8(const Args& a, int m, int k, float (&v)[8]) {
+  if (a.glu) {
+    const long base = (long)(a.x_rows ? a.x_rows[m] : m) * a.ldx;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = swiglu(load_as_float(a.x, a.x_dtype, base + k + j), load_as_float(a.x, a.x_dtype, base + a.glu + k + j));
+    return;
+  }
   const long base = (long)(a.x_rows ? a.x_rows[m] : m) * a.ldx;   // x_rows: gather of token rows
   if (a.x_perm == nullptr && a.x_vec) {
     if (a.x_dtype == QL_F16) {

@@ -117,6 +117,7 @@ struct GemvArgs {
   const int32_t* moe_active;
   const int32_t* moe_n_active;
   long qw_estride, qz_estride, sc_estride;   // elements between consecutive experts
+  int glu;   // > 0: x rows are [gate | up] glu elements apart (SwiGLU applied when staging)
 };
 
 // Register-resident batch of UG consecutive groups of one lane's weights, scales and zeros.
@@ -531,7 +532,7 @@ int gptq_gemv_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_row
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* active, const int32_t* n_active,
                       int max_active, int rows_hint, void* out, int out_dtype, long ldo, int K, int N, int gs,
-                      int bits, float zoff, cudaStream_t st) {
+                      int bits, float zoff, cudaStream_t st, int glu) {
   const int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
   GemvArgs a = {};
   a.x = x; a.x_rows = x_rows; a.x_perm = nullptr; a.ldx = ldx; a.x_dtype = x_dtype;
@@ -548,6 +549,7 @@ int gptq_gemv_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_row
   a.lg_gs_mult = (a.gs_mult & (a.gs_mult - 1)) == 0 ? 31 - __builtin_clz(a.gs_mult) : -1;
   a.zoff = zoff;
   a.moe_offsets = offsets; a.moe_active = active; a.moe_n_active = n_active;
+  a.glu = glu;
   a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
   int sms = 148, dev = 0;
   cudaGetDevice(&dev);

@@ -72,6 +72,7 @@ struct TmaGemvArgs {
   int g_wrows, g_grows;
   int g_max_tiles;  // host: table capacity (grid z)
   int n_experts;    // host: stacked weight matrices (1 when dense)
+  int glu;          // > 0: x rows are [gate | up] glu elements apart (SwiGLU applied when staging)
 };
 
 // Activation source of one CTA (its rows of x, possibly gathered).
@@ -83,6 +84,7 @@ struct XSrc {
   int x_dtype;
   int x_vec;
   int M;
+  int glu;   // > 0: rows are [gate | up] glu elements apart; the activation is silu(gate) * up
 };
 
 template <int BITS, int GS, int NST, int SCB, int SW>
@@ -228,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     // this CTA's rows: gathered through x_rows, else x itself from row row0 on
     const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
     const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
-                    a.ldx, a.x_dtype, a.x_vec, M};
+                    a.ldx, a.x_dtype, a.x_vec, M, a.glu};
     gemv::stage_x_i8<BITS, GS, true>(xsrc, s0 * kStageK, klen, ng_max, xb, gsum, sh_exp, sh_max, tid, kCW * 32);
 
     float acc[NQ][4];
@@ -607,7 +609,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
                            const int32_t* qzeros, const void* scales, int sc_dtype, int E, const int32_t* offsets,
                            const int32_t* tiles, const int32_t* n_tiles, int max_tiles, int tile_rows, void* out,
                            int out_dtype, long ldo, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
-                           int* rc) {
+                           int* rc, int glu) {
   int sms = 148, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -630,6 +632,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
   a.nstage = K / kStageK;
   a.g_offsets = offsets; a.g_tiles = tiles; a.g_n_tiles = n_tiles;
   a.g_max_tiles = max_tiles;
+  a.glu = glu;
   a.g_wrows = K / per;
   a.g_grows = K / gs;
   a.n_experts = E;

@@ -369,7 +369,7 @@ int gptq_gemv_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_row
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* active, const int32_t* n_active,
                       int max_active, int rows_hint, void* out, int out_dtype, long ldo, int K, int N, int gs,
-                      int bits, float zoff, cudaStream_t st);
+                      int bits, float zoff, cudaStream_t st, int glu);
 int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_map, int P, const int32_t* qweight,
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
@@ -380,7 +380,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
                            const int32_t* qzeros, const void* scales, int sc_dtype, int E, const int32_t* offsets,
                            const int32_t* tiles, const int32_t* n_tiles, int max_tiles, int tile_rows, void* out,
                            int out_dtype, long ldo, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
-                           int* rc);
+                           int* rc, int glu);
 }  // namespace ql
 
 // True when a grouped call over P rows and E experts takes the tensor-core GEMM: the average
@@ -401,20 +401,20 @@ extern "C" size_t ql_moe_grouped_workspace(long P, int E, int K, int gs) {
   return grouped_uses_gemm(P, E, K, gs) ? gptq_gemm_workspace((int)P, K) : 0;
 }
 
-extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int32_t* row_token, long P,
-                                     const int32_t* qweight, const int32_t* qzeros, const void* scales,
-                                     int scales_dtype, int E, const int32_t* offsets, const int32_t* active,
-                                     const int32_t* n_active, const int32_t* tiles, const int32_t* n_tiles,
-                                     int max_tiles, int tile_rows, int max_rows_per_expert, void* out, int out_dtype,
-                                     long ldo, int K, int N, int gs, int bits, float zero_offset, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
+static int grouped_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* row_token, long P,
+                               const int32_t* qweight, const int32_t* qzeros, const void* scales, int scales_dtype,
+                               int E, const int32_t* offsets, const int32_t* active, const int32_t* n_active,
+                               const int32_t* tiles, const int32_t* n_tiles, int max_tiles, int tile_rows,
+                               int max_rows_per_expert, void* out, int out_dtype, long ldo, int K, int N, int gs,
+                               int bits, float zero_offset, void* workspace, size_t workspace_bytes, void* stream,
+                               int glu) {
   if (bits != 4 && bits != 8) {
     set_error("ql_moe_grouped_matmul: bits must be 4 or 8 (got %d)", bits);
     return QL_ERR_UNSUPPORTED;
   }
   const int per = 32 / bits;
   if (P < 0 || P > 0x7fffffffL || E <= 0 || K <= 0 || N <= 0 || gs <= 0 || K % gs || gs % per || N % 8 ||
-      ldx < K || ldo < N || max_rows_per_expert < 0) {
+      ldx < (glu ? 2L * K : (long)K) || ldo < N || max_rows_per_expert < 0) {
     set_error("ql_moe_grouped_matmul: bad sizes (P=%ld E=%d K=%d N=%d gs=%d; N %% 8 == 0, gs | K)", P, E, K, N, gs);
     return QL_ERR_ARG;
   }
@@ -439,6 +439,10 @@ extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const
   if (P == 0) return QL_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const long qw_es = (long)(K / per) * N, qz_es = (long)(K / gs) * (N / per), sc_es = (long)(K / gs) * N;
+  if (glu && tile_rows == 128 && grouped_uses_gemm(P, E, K, gs)) {
+    set_error("ql_moe_grouped_matmul_swiglu: the tensor-core path takes activations (run ql_moe_act first)");
+    return QL_ERR_UNSUPPORTED;
+  }
   if (tile_rows == 128 && grouped_uses_gemm(P, E, K, gs)) {
     if (!tiles || !n_tiles || max_tiles <= 0) {
       set_error("ql_moe_grouped_matmul: the tensor-core path needs the routing tile table");
@@ -453,9 +457,33 @@ extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const
   int trc = 0;
   if (gptq_gemv_tma_grouped(x, x_dtype, ldx, row_token, qweight, qzeros, scales, scales_dtype, E, offsets, tiles,
                             n_tiles, max_tiles, tile_rows, out, out_dtype, ldo, K, N, gs, bits, zero_offset, st,
-                            &trc))
+                            &trc, glu))
     return trc;
   return gptq_gemv_grouped(x, x_dtype, ldx, row_token, qweight, qzeros, scales, scales_dtype, qw_es, qz_es, sc_es,
                            offsets, active, n_active, max_active, max_rows_per_expert, out, out_dtype, ldo, K, N, gs,
-                           bits, zero_offset, st);
+                           bits, zero_offset, st, glu);
+}
+
+extern "C" int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int32_t* row_token, long P,
+                                     const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                     int scales_dtype, int E, const int32_t* offsets, const int32_t* active,
+                                     const int32_t* n_active, const int32_t* tiles, const int32_t* n_tiles,
+                                     int max_tiles, int tile_rows, int max_rows_per_expert, void* out, int out_dtype,
+                                     long ldo, int K, int N, int gs, int bits, float zero_offset, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  return grouped_matmul_impl(x, x_dtype, ldx, row_token, P, qweight, qzeros, scales, scales_dtype, E, offsets, active,
+                             n_active, tiles, n_tiles, max_tiles, tile_rows, max_rows_per_expert, out, out_dtype, ldo,
+                             K, N, gs, bits, zero_offset, workspace, workspace_bytes, stream, 0);
+}
+
+extern "C" int ql_moe_grouped_matmul_swiglu(const void* y, int y_dtype, long ldy, long P, const int32_t* qweight,
+                                            const int32_t* qzeros, const void* scales, int scales_dtype, int E,
+                                            const int32_t* offsets, const int32_t* active, const int32_t* n_active,
+                                            const int32_t* tiles, const int32_t* n_tiles, int max_tiles,
+                                            int tile_rows, int max_rows_per_expert, void* out, int out_dtype,
+                                            long ldo, int K, int N, int gs, int bits, float zero_offset,
+                                            void* stream) {
+  return grouped_matmul_impl(y, y_dtype, ldy, nullptr, P, qweight, qzeros, scales, scales_dtype, E, offsets, active,
+                             n_active, tiles, n_tiles, max_tiles, tile_rows, max_rows_per_expert, out, out_dtype, ldo,
+                             K, N, gs, bits, zero_offset, nullptr, 0, stream, K);
 }

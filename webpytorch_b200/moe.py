@@ -26,6 +26,9 @@ from .qlinear import QuantizedLinear, _device
 __all__ = ["MoEBlock", "StackedExperts", "moe_mlp"]
 
 TILE_ROWS = 128   # rows per tile of the grouped tensor-core GEMM
+# Largest decode tile for which the down GEMV forms silu(gate) * up itself: every column tile of
+# the down projection recomputes it for its rows, which only pays off for a few rows.
+SWIGLU_FUSE_ROWS = 8
 
 
 def _as_quantized(lin, what):
@@ -158,6 +161,19 @@ def grouped_matmul(x, row_token, r, w, out_dtype=torch.float32, stream=None):
     return y
 
 
+def down_swiglu(y, r, w, out_dtype=torch.float32, stream=None):
+    """z[P, N] = (silu(y[:, :K]) * y[:, K:]) @ W_e per expert segment, the activation formed while
+    staging (decode tile tables only)."""
+    P = r.P
+    z = torch.empty((P, w.N), dtype=out_dtype, device=y.device)
+    _ffi.call("ql_moe_grouped_matmul_swiglu", _ffi.ptr(y), _ffi.dtype_code(y.dtype), y.stride(0), P,
+              _ffi.ptr(w.qweight), _ffi.ptr(w.qzeros), _ffi.ptr(w.scales), _ffi.dtype_code(w.scales.dtype), w.E,
+              _ffi.ptr(r.offsets), _ffi.ptr(r.active), _ffi.ptr(r.n_active), _ffi.ptr(r.tiles), _ffi.ptr(r.n_tiles),
+              r.max_tiles, r.tile_rows, r.T, _ffi.ptr(z), _ffi.dtype_code(z.dtype), z.stride(0), w.K, w.N, w.gs,
+              w.bits, float(w.zoff), _ffi.stream_ptr(stream))
+    return z
+
+
 def act(y, I, out_dtype=torch.float32, stream=None):
     """a[P, I] = silu(y[:, :I]) * y[:, I:] for the fused gate|up output y [P, 2I] (fp32)."""
     P = y.shape[0]
@@ -225,6 +241,8 @@ class MoEBlock(torch.nn.Module):
     def expert_ffn(self, x, r, stream=None):
         """Routed experts' outputs for the sorted rows: z [P, H] fp32."""
         y = grouped_matmul(x, r.row_token, r, self.gate_up, stream=stream)
+        if r.tile_rows <= SWIGLU_FUSE_ROWS:   # small decode tiles: SwiGLU formed while staging
+            return down_swiglu(y, r, self.down, stream=stream)
         a = act(y, self.I, stream=stream)
         return grouped_matmul(a, None, r, self.down, stream=stream)
 
@@ -233,6 +251,8 @@ class MoEBlock(torch.nn.Module):
         T = x.shape[0]
         r1 = _single_expert_routing(T, x.device, tile_rows_for(T, 1, gu.K, gu.gs, T))
         y = grouped_matmul(x, None, r1, gu, stream=stream)
+        if r1.tile_rows <= SWIGLU_FUSE_ROWS:
+            return down_swiglu(y, r1, dn, stream=stream)
         a = act(y, self.SI, stream=stream)
         return grouped_matmul(a, None, r1, dn, stream=stream)
 
