@@ -82,8 +82,8 @@ QL_API int ql_gptq_dequant(const int32_t* qweight, const int32_t* qzeros, const 
  *   bias     NULL or fp32 [N]
  *   out      [M, N] of out_dtype, row stride ldo (elements)
  *   zero_offset 0 (reference's own packing) or 1 (AutoGPTQ "stores zero-1" convention)
- * Selects the kernel family from M: a register-unpacking tensor-core GEMV for small M and
- * a tcgen05 dequant-GEMM for large M.
+ * Selects the kernel family from M: for small M a TMA-fed GEMV on the integer MMA (u8 weights
+ * x s8 activation bytes, exact int32 group sums), for large M a tcgen05 dequant-GEMM.
  * Replaces: webtorch/_core.py:4008-4043 (_gptq_matmul), called from
  *           QuantizedLinear.forward webtorch/_core.py:4446-4456.
  */

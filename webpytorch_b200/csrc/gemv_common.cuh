@@ -188,6 +188,16 @@ __device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half*
   sync();
 }
 
+// Layout of the staged B operand: row (step, t) holds sstride slots (uint2 each). With the
+// swizzle (SWZ, kernels of more than 4 tokens) slot s of row t is stored at s ^ xb_swz(sstride,
+// t) and rows are rounded up to 8 slots: a warp's 64-bit loads of one step read rows t = 0..3,
+// 4 slots each per half-warp, and the swizzle places the 4 rows 8 banks apart. Without it
+// (up to 4 tokens) rows are 2M slots, unpadded.
+__host__ __device__ __forceinline__ int xb_slots(int slots) { return slots <= 4 ? slots : (slots + 7) & ~7; }
+__host__ __device__ __forceinline__ int xb_swz(int sstride, int t) {
+  return sstride <= 4 ? 0 : (sstride % 16 == 0 ? 4 * t : 4 * (t >> 1));
+}
+
 // Stage x[:, kbase : kbase + klen] for M <= 16 tokens as the B operand of the integer MMA
 // (mma.m16n8k32, A = u8 weights, B = s8 activations):
 //   * each token row is scaled by an exact power of two, v = rint(x * 2^-e) with |v| <= 2^14
@@ -198,16 +208,16 @@ __device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half*
 //     16 + 4t + i <- K 8r + 2i + 1), lane t of a 32-K step taking row 4s + t. An int8 packed row
 //     (K = 4r .. 4r+3) is a register as it is: rows 8s + t and 8s + 4 + t feed MMA k 4t + i and
 //     16 + 4t + i;
-//   * xb[(s * 4 + t) * 2M + slot] holds lane t's two B registers of step s for that slot;
+//   * xb[(s * 4 + t) * sstride + slot'] holds lane t's two B registers of step s for that slot
+//     (slot' = slot ^ xb_swz(sstride, t) and sstride = xb_slots(2M) with SWZ, else slot and 2M);
 //   * gsum[m * gstride + g] = sum of v over group g (exact integers), for the zero point.
 // sh_max must be zero and visible before the call; sh_exp is valid after it returns.
-template <int BITS, int GS, bool NAMED, class Args>
-__device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint2* xb, int* gsum, int* sh_exp,
-                           unsigned* sh_max, int tid, int nthr) {
+template <int BITS, int GS, bool NAMED, bool SWZ, class Args>
+__device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, int sstride, uint2* xb, int* gsum,
+                           int* sh_exp, unsigned* sh_max, int tid, int nthr) {
   constexpr int CH = 4;          // 8-value chunks a thread keeps in registers on the one-pass path
   constexpr int SEG = GS / 8;    // chunks per group (lanes reduced together)
   const int M = a.M;
-  const int slots = 2 * M;
   auto sync = [&]() {
     if constexpr (NAMED) {
       asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
@@ -236,15 +246,17 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, uint
     }
     if constexpr (BITS == 4) {
       const int s4 = kc >> 2, t = kc & 3;
-      uint2* dst = xb + (s4 * 4 + t) * slots + 2 * m;
+      uint2* dst = xb + (s4 * 4 + t) * sstride + (SWZ ? (2 * m) ^ xb_swz(sstride, t) : 2 * m);
       dst[0] = make_uint2(hi[0], hi[1]);
       dst[1] = make_uint2(lo[0], lo[1]);
     } else {
       const int r0 = 2 * kc;                // rows r0, r0 + 1 of the same half of a step
       const int s8 = r0 >> 3, j = r0 & 7;
       const int half = j >> 2, t0 = j & 3;
-      uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * slots + 2 * m) + half;
-      uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * slots + 2 * m) + half;
+      const int c0 = SWZ ? (2 * m) ^ xb_swz(sstride, t0) : 2 * m;
+      const int c1 = SWZ ? (2 * m) ^ xb_swz(sstride, t0 + 1) : 2 * m;
+      uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * sstride + c0) + half;
+      uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * sstride + c1) + half;
       d0[0] = hi[0];
       d0[2] = lo[0];
       d1[0] = hi[1];

@@ -698,13 +698,14 @@ extern "C" size_t ql_gptq_matmul_workspace(int M, int K) { return ql::gptq_gemm_
 
 namespace ql {
 int take_tma_gemv_status();
+int take_q4k_tma_status();
 }
 
 extern "C" int ql_device_status(void) {
   const cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return ql::cuda_status(e, "ql_device_status");
   const int gemm = ql::take_tc_status();
-  const int gemv = ql::take_tma_gemv_status();
+  const int gemv = ql::take_tma_gemv_status() | ql::take_q4k_tma_status();
   if (gemm || gemv) {
     ql::set_error("a tensor-core kernel gave up on a bounded wait");
     return QL_ERR_TIMEOUT;

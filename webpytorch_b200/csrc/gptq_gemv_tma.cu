@@ -62,6 +62,7 @@ struct TmaGemvArgs {
   int nstage;   // K / kStageK
   int cs;       // cluster size along K
   int sw;       // 32-column strips per CTA (8 or 4; host-side choice)
+  int nst;      // ring stages (the kernel's NST; host-side choice)
   float zoff;
   // grouped (MoE) mode when g_offsets != NULL: blockIdx.z is an entry of the device-built tile
   // table (expert e = g_tiles[2z], first row g_tiles[2z + 1] of its segment, MAXM rows at
@@ -99,7 +100,7 @@ struct TmaLayout {
   static constexpr int kZBytes = GPS * (TC / PER) * 4;
   static constexpr int kStageBytes = (kWBytes + kScBytes + kZBytes + 1023) & ~1023;
   static constexpr int kBarOff = NST * kStageBytes;
-  static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + abort flag
+  static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier, abort flag
 };
 
 template <int BITS, int GS, int NQ, int NST, int SCB, int SW>
@@ -147,13 +148,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int klen_max = nst_max * kStageK;
   const int ng_max = nst_max * GPS;
   const int N = a.N;
+  // staged activations: B rows of sstride slots (swizzled), group sums gstride ints apart (odd
+  // from two tokens on, so the 4 tokens a warp reads at once sit in distinct banks)
+  constexpr bool SWZ = NQ > 1;   // swizzled B rows (more than 4 tokens)
+  const int sstride = SWZ ? gemv::xb_slots(2 * M) : 2 * M;
+  const int gstride = M > 1 ? (ng_max | 1) : ng_max;
   uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
-  const int xs_bytes = (M * klen_max * 2 + 15) & ~15;
+  const int xs_bytes = (klen_max * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
-  const int gs_bytes = (M * ng_max * 4 + 15) & ~15;
+  const int gs_bytes = (M * gstride * 4 + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
-  // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16
-  float* kred = red + (TC + 64) * MAXM;   // K-way partials (KW == 2): [SW * 32 lanes][NQ * 4]
+  // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16 (only
+  // with cs > 1); kred: K-way partials (KW == 2), [SW * 32 lanes][NQ * 4]
+  float* kred = red + (a.cs > 1 ? (TC + 64) * MAXM : 0);
 
   // Split-K reduction over the cluster: rank q owns the column quads [qs(q), qs(q + 1)) of
   // the tile, qs(q) = ceil(q * Q / cs), Q = TC / 4; every rank sends each owner its partial
@@ -231,7 +238,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
     const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
                     a.ldx, a.x_dtype, a.x_vec, M, a.glu};
-    gemv::stage_x_i8<BITS, GS, true>(xsrc, s0 * kStageK, klen, ng_max, xb, gsum, sh_exp, sh_max, tid, kCW * 32);
+    gemv::stage_x_i8<BITS, GS, true, SWZ>(xsrc, s0 * kStageK, klen, gstride, sstride, xb, gsum, sh_exp, sh_max, tid,
+                                     kCW * 32);
 
     float acc[NQ][4];
 #pragma unroll
@@ -241,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     const uint32_t strip_off = strip * L::kStripBytes;
     const uint32_t xb_base = ptx::smem_addr(xb);
+    const int swz = SWZ ? gemv::xb_swz(sstride, t) : 0;
     for (int i = kway; i < nst; i += KW) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
@@ -290,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int slot = 8 * mq + gq;
             uint32_t b0 = 0u, b1 = 0u;
             if (slot < slots) {
-              const uint32_t xa = xb_base + ((step * 4 + t) * slots + slot) * 8;
+              const uint32_t xa = xb_base + ((step * 4 + t) * sstride + (slot ^ swz)) * 8;
               asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
             }
             mma_16832_u8s8(d[mq][0], A0[0], A0[1], A0[2], A0[3], b0, b1);
@@ -322,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int mq = 0; mq < NQ; ++mq) {
           const int tok = 4 * mq + t;
-          const int S = tok < M ? gsum[tok * ng_max + gl] : 0;
+          const int S = tok < M ? gsum[tok * gstride + gl] : 0;
           const int C[4] = {d[mq][0][0] * 256 + d[mq][0][1], d[mq][0][2] * 256 + d[mq][0][3],
                             d[mq][1][0] * 256 + d[mq][1][1], d[mq][1][2] * 256 + d[mq][1][3]};
 #pragma unroll
@@ -438,6 +447,31 @@ bool encode_2d(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const 
          CUDA_SUCCESS;
 }
 
+constexpr int kMaxSmem = 220 * 1024;
+
+// Ring depth (NST) of the kernel built for (bits, sw): the same bytes in flight for both tile
+// widths. Batches of more than 4 tokens may also take a ring of half that depth, so that two
+// CTAs with their larger activation slices still fit on one SM.
+constexpr int nst_cap(int bits, int sw) { return (bits == 4 ? 4 : 3) * (kCW / sw); }
+constexpr int nst_half(int bits, int sw) { return nst_cap(bits, sw) / 2 > 2 ? nst_cap(bits, sw) / 2 : 2; }
+
+// Dynamic shared memory of one CTA (ring of nst = NST stages), as the kernel's prologue carves
+// it up: 1 KB of alignment slack, the ring, the barriers, the staged activations and their group sums, the split-K
+// receive buffer (cs > 1) and the K-way hand-off (128-column tiles).
+size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int M, int nstage) {
+  const int per = 32 / bits, tc = 32 * sw, gps = kStageK / kgs, rows = kStageK / per;
+  const size_t stage = ((size_t)sw * rows * 128 + (size_t)gps * tc * scb + (size_t)gps * (tc / per) * 4 + 1023) & ~(size_t)1023;
+  const int nq = M <= 4 ? 1 : (M <= 8 ? 2 : 4);
+  const int sq = nstage / cs, nst_max = sq + (nstage % cs ? 1 : 0);
+  const int ng_max = nst_max * gps;
+  size_t b = 1024 + (size_t)nst * stage + 2 * nst * 8 + 16;
+  b += ((size_t)nst_max * kStageK * gemv::xb_slots(2 * M) + 15) & ~(size_t)15;
+  b += ((size_t)M * (M > 1 ? (ng_max | 1) : ng_max) * 4 + 15) & ~(size_t)15;
+  if (cs > 1) b += (size_t)(tc + 64) * 4 * nq * 4;
+  if (sw < kCW) b += (size_t)sw * 32 * nq * 4 * 4;
+  return b;
+}
+
 template <int BITS, int GS, int NQ, int NST, int SCB, int SW>
 int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qzeros, const void* scales,
                cudaStream_t st) {
@@ -466,17 +500,13 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
                  TC / L::PER, L::GPS))
     return -1;
   auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB, SW>;
-  const int sq = a.nstage / a.cs;
-  const int nst_max = sq + (a.nstage % a.cs ? 1 : 0);
-  const size_t smem = 1024 + L::kXsOff + (((size_t)a.M * nst_max * kStageK * 2 + 15) & ~(size_t)15) +
-                      (((size_t)a.M * nst_max * L::GPS * 4 + 15) & ~(size_t)15) + (size_t)(TC + 64) * 4 * NQ * 4 +
-                      (SW < kCW ? (size_t)SW * 32 * NQ * 4 * 4 : 0);
-  if (smem > 200 * 1024) return -1;  // too large an activation slice: caller falls back
+  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, a.M, a.nstage);
+  if (smem > kMaxSmem) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_dev != dev) {
-    int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024),
+    int rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
                          "cudaFuncSetAttribute(tma gemv smem)");
     if (rc) return rc;
     rc = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
@@ -505,23 +535,22 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, tw, ts, tz, a), "gptq_gemv_tma launch");
 }
 
-template <int BITS, int GS, int SW>
+template <int BITS, int GS, int SW, int SCB>
 int tma_nq(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
-  // the same bytes in flight per CTA for both tile widths
-  constexpr int NST = (BITS == 4 ? 4 : 3) * (kCW / SW);
-  if (a.sc_dtype == QL_F32) {
-    if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 4, SW>(a, qw, qz, sc, st);
-    return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 4, SW>(a, qw, qz, sc, st)
-                    : launch_tma<BITS, GS, 4, NST, 4, SW>(a, qw, qz, sc, st);
-  }
-  if (a.M <= 4) return launch_tma<BITS, GS, 1, NST, 2, SW>(a, qw, qz, sc, st);
-  return a.M <= 8 ? launch_tma<BITS, GS, 2, NST, 2, SW>(a, qw, qz, sc, st)
-                  : launch_tma<BITS, GS, 4, NST, 2, SW>(a, qw, qz, sc, st);
+  constexpr int CAP = nst_cap(BITS, SW), HALF = nst_half(BITS, SW);
+  if (a.M <= 4) return launch_tma<BITS, GS, 1, CAP, SCB, SW>(a, qw, qz, sc, st);
+  if (a.M <= 8)
+    return a.nst == CAP ? launch_tma<BITS, GS, 2, CAP, SCB, SW>(a, qw, qz, sc, st)
+                        : launch_tma<BITS, GS, 2, HALF, SCB, SW>(a, qw, qz, sc, st);
+  return a.nst == CAP ? launch_tma<BITS, GS, 4, CAP, SCB, SW>(a, qw, qz, sc, st)
+                      : launch_tma<BITS, GS, 4, HALF, SCB, SW>(a, qw, qz, sc, st);
 }
 
 template <int BITS, int GS>
 int tma_mt(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
-  return a.sw == 8 ? tma_nq<BITS, GS, 8>(a, qw, qz, sc, st) : tma_nq<BITS, GS, 4>(a, qw, qz, sc, st);
+  if (a.sc_dtype == QL_F32)
+    return a.sw == 8 ? tma_nq<BITS, GS, 8, 4>(a, qw, qz, sc, st) : tma_nq<BITS, GS, 4, 4>(a, qw, qz, sc, st);
+  return a.sw == 8 ? tma_nq<BITS, GS, 8, 2>(a, qw, qz, sc, st) : tma_nq<BITS, GS, 4, 2>(a, qw, qz, sc, st);
 }
 
 template <int BITS>
@@ -533,31 +562,44 @@ int tma_gs(const TmaGemvArgs& a, int kgs, const uint32_t* qw, const uint32_t* qz
   }
 }
 
-// Tile width (a.sw) and cluster size (a.cs, the K split): the CTA count tiles * zdim * cs should
-// fill resident waves of ctas_per_sm CTAs per SM as evenly as possible (the busiest SM sets the
-// time); the wider tile wins ties (fewer partial sums to reduce).
-void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_sm, int max_cluster) {
-  int cs = 1, sw = 8;
+// Tile width (a.sw), cluster size (a.cs, the K split) and ring depth (a.nst): the CTA count
+// tiles * zdim * cs should fill resident waves of the SMs as evenly as possible (the busiest SM
+// sets the time), two CTAs per SM where their shared memory allows (a shallower ring is
+// preferred to a single CTA per SM); the wider tile and the deeper ring win ties.
+void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_sm, int max_cluster, int bits,
+                  int kgs, int scb) {
+  int cs = 1, sw = 8, nst = nst_cap(bits, 8);
   double best = -1.0;
-  const int slots = sms * ctas_per_sm;
+  const size_t per_sm = 228 * 1024;   // shared memory per SM; each CTA also reserves 1 KB
   for (int w = 8; w >= 4; w /= 2) {
     const int tiles = (N + 32 * w - 1) / (32 * w) * zdim;
-    for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-      const int ctas = tiles * c;
-      if (ctas > slots && c > 1) break;
-      if ((size_t)M * ((a.nstage + c - 1) / c) * kStageK * 2 > 64 * 1024 && c < 16) continue;
-      const double waves = (double)ctas / slots;
-      const double busiest = (double)((ctas + slots - 1) / slots);
-      const double score = waves / busiest * (ctas < slots ? (double)ctas / slots : 1.0);
-      if (score > best + 1e-9) {
-        best = score;
-        cs = c;
-        sw = w;
+    const int cap = nst_cap(bits, w), half = nst_half(bits, w);
+    for (int ns = cap; ns >= half; ns = (ns == cap && M > 4 && half < cap) ? half : 0) {
+      for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
+        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, M, a.nstage);
+        if (sm > (size_t)kMaxSmem) continue;
+        const int fit = (int)(per_sm / (sm + 1024 + 256));
+        const int per = fit < ctas_per_sm ? fit : ctas_per_sm;
+        if (per < 1) continue;
+        const int slots = sms * per;
+        const int ctas = tiles * c;
+        if (ctas > slots && c > 1) continue;
+        const double waves = (double)ctas / slots;
+        const double busiest = (double)((ctas + slots - 1) / slots);
+        double score = waves / busiest * (ctas < slots ? (double)ctas / slots : 1.0);
+        if (per < ctas_per_sm) score *= 0.75;
+        if (score > best + 1e-9) {
+          best = score;
+          cs = c;
+          sw = w;
+          nst = ns;
+        }
       }
     }
   }
   a.sw = sw;
   a.cs = cs;
+  a.nst = nst;
 }
 
 }  // namespace
@@ -592,7 +634,7 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
-  choose_split(a, N, M, 1, sms, ctas_per_sm, max_cluster);
+  choose_split(a, N, M, 1, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
   const int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);
@@ -636,7 +678,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
   a.g_wrows = K / per;
   a.g_grows = K / gs;
   a.n_experts = E;
-  choose_split(a, N, a.M, max_tiles, sms, 2, 8);
+  choose_split(a, N, a.M, max_tiles, sms, 2, 8, bits, kgs, sc_dtype == QL_F32 ? 4 : 2);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
   const int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);

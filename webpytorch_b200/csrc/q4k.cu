@@ -6,7 +6,9 @@
 // has 6-bit scale sc_j and min m_j (get_scale_min_k4); value = (d*sc_j) * q - dmin*m_j, with q
 // the low nibbles of qs[32g .. 32g+31] for j = 2g and the high nibbles for j = 2g+1.
 //
-// GEMV design:
+// The decode GEMV / small-M GEMM runs the TMA-fed integer-MMA kernel of q4k_gemv_tma.cu; the
+// register-fed kernel below serves the calls that kernel declines (no tensor-map encoder, an
+// activation slice too large for shared memory). Its design:
 //  * A warp owns 16 output rows; lane (g = lane/4, t = lane%4) streams rows g and g+8. For
 //    each 32-byte quant group of a block, lane t reads its 8 bytes of both rows, so every
 //    warp load touches 8 rows x 32 contiguous bytes.
@@ -376,6 +378,11 @@ int q4k_gemv(const void* x, int x_dtype, long ldx, const uint8_t* raw, const flo
 }  // namespace
 }  // namespace ql
 
+namespace ql {
+bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
+                  int out_dtype, long ldo, int M, int K, int N, cudaStream_t st, int* rc);
+}
+
 using namespace ql;
 
 extern "C" int ql_q4k_dequant(const uint8_t* raw, float* W, int N, int K, void* stream) {
@@ -409,6 +416,8 @@ extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t
     return QL_ERR_ALIGN;
   }
   cudaStream_t st = (cudaStream_t)stream;
+  int rc = QL_OK;
+  if (q4k_gemv_tma(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, st, &rc)) return rc;
   for (int m0 = 0; m0 < M; m0 += 16) {
     const int mc = (M - m0) < 16 ? (M - m0) : 16;
     const char* xb = reinterpret_cast<const char*>(x) + (long)m0 * ldx * (x_dtype == QL_F32 ? 4 : 2);
