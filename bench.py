@@ -257,11 +257,12 @@ def profile_case(name):
         x = torch.randn((T, MOE_H), device=dev, generator=g).to(torch.bfloat16)
         for _ in range(2):
             blk(x)
-    elif name == "q4k":                      # q4k_gemv_kernel, config 2, M=1, 8 copies (264 MB)
+    elif name in ("q4k", "q4k_m8"):          # q4k_gemv_tma_kernel, config 2, M=1 / 8, 8 copies (264 MB)
         from webpytorch_b200.ggml import ggml_matmul
         raws = [rand_q4k(Q4K_N, Q4K_K, dev, g) for _ in range(Q4K_COPIES)]
-        x = torch.randn((1, Q4K_K), device=dev, generator=g)
-        y = torch.empty((1, Q4K_N), device=dev)
+        M = 1 if name == "q4k" else 8
+        x = torch.randn((M, Q4K_K), device=dev, generator=g)
+        y = torch.empty((M, Q4K_N), device=dev)
         for r in raws:
             ggml_matmul(x, r, "Q4_K", Q4K_K, Q4K_N, out=y)
     else:
@@ -407,7 +408,7 @@ def main():
     ap.add_argument("--skip-extra", action="store_true", help="skip the config-2 and config-4 sections")
     ap.add_argument("--profile", default=None,
                     help="run one small fixed case for ncu: gemv | gemv_narrow | gemm | moe_decode | "
-                         "moe_prefill | q4k")
+                         "moe_prefill | q4k | q4k_m8")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:
