@@ -207,11 +207,12 @@ def test_moe_step_replays_in_a_cuda_graph():
     (4, 2048, 1536, 40, 2, 4, 128),   # more rows than a chunk: several chunks per expert
 ])
 @pytest.mark.parametrize("xdtype,gather", [(torch.float16, True), (torch.float32, True), (torch.float32, False)])
-@pytest.mark.parametrize("table", ["chosen", "128"])
+@pytest.mark.parametrize("table", ["chosen", "128", "64", "32"])
 def test_grouped_matmul_vs_dense_per_expert(E, K, N, T, k, bits, gs, xdtype, gather, table):
     """Every expert's sorted rows of ql_moe_grouped_matmul equal the dense operator on its weights
     (rows gathered through row_token, or read in sorted order directly), with the tile table the
-    call asks for (tensor-core GEMM or decode GEMV) and with 128-row tiles (other paths)."""
+    call asks for (tensor-core GEMM or decode GEMV) and with 128-, 64- and 32-row tiles (the
+    tensor-core GEMM's tile heights when the call takes it, else the other paths)."""
     exps = synth.moe_experts(E, K, N, bits=bits, gs=gs, seed=E * T + K)
     experts = [{"gate": _ql(e["gate"], gs, bits), "up": _ql(e["up"], gs, bits), "down": _ql(e["down"], gs, bits)}
                for e in exps]
@@ -219,7 +220,7 @@ def test_grouped_matmul_vs_dense_per_expert(E, K, N, T, k, bits, gs, xdtype, gat
     rng = np.random.default_rng(T)
     logits = torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).to(DEV)
     x = torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32)).to(DEV).to(xdtype)
-    tr = moe.tile_rows_for(T * k, E, K, gs, T) if table == "chosen" else moe.TILE_ROWS
+    tr = moe.tile_rows_for(T * k, E, K, gs, T) if table == "chosen" else int(table)
     r = moe.route(logits, k, True, tr)
     rows = r.row_token[:r.P].long()
     if gather:

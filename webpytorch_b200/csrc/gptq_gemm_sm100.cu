@@ -286,9 +286,10 @@ __device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, ui
   out2[1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v1), u32_as_h2(zlo)), s2));
 }
 
-// BT = tokens per tile (MMA N). BT = 128 keeps two accumulators in TMEM (the epilogue drains one
-// while the next tile's MMAs fill the other); BT = 256 halves the dequant work per MMA flop with
-// one accumulator (the next tile waits for the drain into registers).
+// BT = tokens per tile (MMA N). Up to 128 two accumulators sit in TMEM at columns 0 and 128 (the
+// epilogue drains one while the next tile's MMAs fill the other): 128 for dense GEMMs, 32 / 64 for
+// MoE experts with few rows each (less padding, same dequant work per tile). BT = 256 halves the
+// dequant work per MMA flop with one accumulator (the next tile waits for the drain).
 template <int BITS, int NS, int BT>
 __global__ void __launch_bounds__(kThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
@@ -299,8 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int ROWS = L::ROWS;
   constexpr int HROWS = ROWS / 2;               // packed rows per dequant half
   constexpr int TCOLS_A = kSlabK / 2;           // TMEM columns per A stage (fp16 pairs)
-  constexpr int ND = BT == 128 ? 2 : 1;         // accumulator buffers
-  constexpr int A_COL = ND * BT;                // A stages start after the accumulators
+  constexpr int ND = BT <= 128 ? 2 : 1;         // accumulator buffers
+  constexpr int DCOL = BT <= 128 ? 128 : BT;    // TMEM columns between accumulator buffers
+  constexpr int A_COL = ND * DCOL;              // A stages start after the accumulators
+  constexpr int DQP = 1;                        // slabs a dequant warp converts per TMEM-store wait (2 measured slower)
   constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, BT);
   constexpr uint32_t MASK = (1u << BITS) - 1u;
   static_assert(A_COL + NS * TCOLS_A <= 512, "TMEM budget");
@@ -404,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t xs = sbase + s * L::kStageBytes;
 #pragma unroll
           for (int j = 0; j < kSlabK / 16; ++j) {
-            ptx::mma_f16_ts(tmem + b * BT, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
+            ptx::mma_f16_ts(tmem + b * DCOL, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
                             IDESC, (kb | j) != 0);
           }
           ptx::mma_commit(slab_free(s));  // frees the stage's shared memory and its TMEM A columns
@@ -421,36 +424,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lrow = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     const int gi = a.gb == 2 ? h : 0;   // scale/zero row of this half inside the slab
+    // DQP slabs per step: both TMEM stores in flight before one wait, so the store latency is
+    // paid once per DQP slabs
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      for (int kb = 0; kb < nslab; ++kb, ++it) {
-        const int s = it % NS;
-        if (!ptx::mbar_wait(full(s), (it / NS) & 1, abort_flag)) goto done;
-        const unsigned char* stp = smem + s * L::kStageBytes;
-        const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
-        uint32_t w[HROWS];
+      for (int kb = 0; kb < nslab;) {
+        const int cnt = nslab - kb < DQP ? nslab - kb : DQP;
+        uint32_t v[DQP][16];
 #pragma unroll
-        for (int r = 0; r < HROWS; ++r) w[r] = wsm[(h * HROWS + r) * kTileN + lrow];
-        const float scv = load_as_float(stp + L::kSOff, a.sc_dtype, gi * kTileN + lrow);
-        const uint32_t zw = reinterpret_cast<const uint32_t*>(stp + L::kZOff)[gi * (kTileN / PER) + lrow / PER];
-        const float zf = (float)((zw >> (BITS * (lrow % PER))) & MASK) + a.zoff;
-        const uint32_t zlo = h2_as_u32(__float2half2_rn(1024.f + zf));
-        const uint32_t zhi = h2_as_u32(__float2half2_rn(-(64.f + zf)));
-        const __half2 s2 = __float2half2_rn(scv);
-        uint32_t v[16];
+        for (int u = 0; u < DQP; ++u) {
+          if (u < cnt) {
+            const int s = (it + u) % NS;
+            if (!ptx::mbar_wait(full(s), ((it + u) / NS) & 1, abort_flag)) goto done;
+            const unsigned char* stp = smem + s * L::kStageBytes;
+            const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
+            uint32_t w[HROWS];
 #pragma unroll
-        for (int r = 0; r < HROWS; ++r) {
-          if constexpr (BITS == 4) {
-            dq_int4(w[r], zlo, zhi, s2, &v[r * 4]);
-          } else {
-            dq_int8(w[r], zlo, s2, &v[r * 2]);
+            for (int r = 0; r < HROWS; ++r) w[r] = wsm[(h * HROWS + r) * kTileN + lrow];
+            const float scv = load_as_float(stp + L::kSOff, a.sc_dtype, gi * kTileN + lrow);
+            const uint32_t zw = reinterpret_cast<const uint32_t*>(stp + L::kZOff)[gi * (kTileN / PER) + lrow / PER];
+            const float zf = (float)((zw >> (BITS * (lrow % PER))) & MASK) + a.zoff;
+            const uint32_t zlo = h2_as_u32(__float2half2_rn(1024.f + zf));
+            const uint32_t zhi = h2_as_u32(__float2half2_rn(-(64.f + zf)));
+            const __half2 s2 = __float2half2_rn(scv);
+#pragma unroll
+            for (int r = 0; r < HROWS; ++r) {
+              if constexpr (BITS == 4) {
+                dq_int4(w[r], zlo, zhi, s2, &v[u][r * 4]);
+              } else {
+                dq_int8(w[r], zlo, s2, &v[u][r * 2]);
+              }
+            }
           }
         }
-        ptx::tmem_st16(lane_addr + A_COL + s * TCOLS_A + h * (TCOLS_A / 2), v);
+#pragma unroll
+        for (int u = 0; u < DQP; ++u)
+          if (u < cnt) ptx::tmem_st16(lane_addr + A_COL + ((it + u) % NS) * TCOLS_A + h * (TCOLS_A / 2), v[u]);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(a_full(s));
+        if (lane == 0) {
+          for (int u = 0; u < cnt; ++u) ptx::mbar_arrive(a_full((it + u) % NS));
+        }
+        kb += cnt;
+        it += cnt;
       }
     }
   } else if (warp >= kEpilogueWarp0) {
@@ -477,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < BT / 32; ++c) {
         uint32_t v[32];
-        ptx::tmem_ld32(lane_addr + b * BT + c * 32, v);
+        ptx::tmem_ld32(lane_addr + b * DCOL + c * 32, v);
         ptx::tmem_wait_ld();
         if (c == BT / 32 - 1) {
           ptx::tc_fence_before();
@@ -534,7 +551,7 @@ bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const voi
 // n_experts: stacked weight matrices (grouped mode), 1 otherwise.
 template <int BITS, int BT>
 int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
-  constexpr int NS = BT == 128 ? (BITS == 4 ? 8 : 7) : 4;
+  constexpr int NS = BT <= 128 ? (BITS == 4 ? 8 : 7) : 4;
   constexpr int PER = 32 / BITS;
   using L = SmemLayout<BITS, NS, BT>;
   EncodeTiledFn enc = encode_fn();
@@ -656,8 +673,8 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
               "(int8), qzeros 16-byte aligned", K, gs, N);
     return QL_ERR_UNSUPPORTED;
   }
-  if (tile_rows_n != kBT) {
-    set_error("grouped GEMM: tile rows must be %d (got %d)", kBT, tile_rows_n);
+  if (tile_rows_n != 32 && tile_rows_n != 64 && tile_rows_n != kBT) {
+    set_error("grouped GEMM: tile rows must be 32, 64 or %d (got %d)", kBT, tile_rows_n);
     return QL_ERR_ARG;
   }
   const size_t need = gptq_gemm_workspace(P, K);
@@ -681,7 +698,11 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
   a.tiles = tiles; a.n_tiles = n_tiles; a.offsets = offsets;
   a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
   a.gb = gs == 32 ? 2 : 1;
-  return bits == 4 ? launch_gemm<4, 128>(a, x16, n_experts, st) : launch_gemm<8, 128>(a, x16, n_experts, st);
+  switch (tile_rows_n) {
+    case 32: return bits == 4 ? launch_gemm<4, 32>(a, x16, n_experts, st) : launch_gemm<8, 32>(a, x16, n_experts, st);
+    case 64: return bits == 4 ? launch_gemm<4, 64>(a, x16, n_experts, st) : launch_gemm<8, 64>(a, x16, n_experts, st);
+    default: return bits == 4 ? launch_gemm<4, 128>(a, x16, n_experts, st) : launch_gemm<8, 128>(a, x16, n_experts, st);
+  }
 }
 
 int take_tc_status() {

@@ -28,11 +28,78 @@ namespace {
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 1024;
 
-// Top-k of one token's logits by one warp: softmax statistics over all E experts, then k
-// rounds of warp argmax (ties to the lower expert index). Lane j < k returns pick j in
+// Top-k of one token's logits by one warp: softmax statistics over all E experts in float64,
+// then k rounds of warp argmax (ties to the lower expert index). Lane j < k returns pick j in
 // (*idx, *w); the weights are the softmax probabilities, renormalised over the k when norm.
-__device__ __forceinline__ void topk_token(const float* __restrict__ row, int E, int k, int norm, int lane, int* idx,
-                                           float* w) {
+//
+// Up to 32 * VPL experts every lane keeps its VPL logits and their exp(l - max) in registers: a
+// pick is struck from its lane's bitmask and its probability comes from the lane that holds it,
+// so a token costs VPL float64 exponentials per lane. Same arithmetic and order as the generic
+// form below (identical results).
+template <int VPL>
+__device__ __forceinline__ void topk_token_reg(const float* __restrict__ row, int E, int k, int norm, int lane,
+                                               int* idx, float* w) {
+  float v[VPL];
+  double ex[VPL];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? row[e] : -INFINITY;
+    if (e < E) mx = fmaxf(mx, v[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  double den = 0.0;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    ex[i] = lane + 32 * i < E ? exp((double)v[i] - (double)mx) : 0.0;
+    den += ex[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  unsigned taken = 0u;
+  double psum = 0.0, mine = 0.0;
+  int my_idx = 0;
+  for (int j = 0; j < k; ++j) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    double be = 0.0;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && !((taken >> i) & 1u) && (v[i] > best || (v[i] == best && e < bi))) {
+        best = v[i];
+        bi = e;
+        be = ex[i];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const double oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+        be = oe;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    const double p = be / den;
+    psum += p;
+    if (lane == j) {
+      my_idx = bi;
+      mine = p;
+    }
+  }
+  *idx = lane < k ? my_idx : 0;
+  *w = lane < k ? (float)(norm ? mine / psum : mine) : 0.f;
+}
+
+// Any E (up to kMaxExperts): the logits are re-read from memory each round.
+__device__ __forceinline__ void topk_token_any(const float* __restrict__ row, int E, int k, int norm, int lane,
+                                               int* idx, float* w) {
   float mx = -INFINITY;
   for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
 #pragma unroll
@@ -42,8 +109,8 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ row, int E,
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
   int chosen[kMaxTopK];
-  double pw[kMaxTopK];
-  double psum = 0.0;
+  double psum = 0.0, mine = 0.0;
+  int my_idx = 0;
   for (int j = 0; j < k; ++j) {
     float best = -INFINITY;
     int bi = 0x7fffffff;
@@ -66,16 +133,22 @@ __device__ __forceinline__ void topk_token(const float* __restrict__ row, int E,
       }
     }
     chosen[j] = bi;
-    pw[j] = exp((double)best - (double)mx) / den;
-    psum += pw[j];
-  }
-  *idx = 0;
-  *w = 0.f;
-  for (int j = 0; j < k; ++j)
-    if (j == lane) {
-      *idx = chosen[j];
-      *w = (float)(norm ? pw[j] / psum : pw[j]);
+    const double p = exp((double)best - (double)mx) / den;
+    psum += p;
+    if (lane == j) {
+      my_idx = bi;
+      mine = p;
     }
+  }
+  *idx = lane < k ? my_idx : 0;
+  *w = lane < k ? (float)(norm ? mine / psum : mine) : 0.f;
+}
+
+__device__ __forceinline__ void topk_token(const float* __restrict__ row, int E, int k, int norm, int lane, int* idx,
+                                           float* w) {
+  if (E <= 128) topk_token_reg<4>(row, E, k, norm, lane, idx, w);
+  else if (E <= 256) topk_token_reg<8>(row, E, k, norm, lane, idx, w);
+  else topk_token_any(row, E, k, norm, lane, idx, w);
 }
 
 __global__ void moe_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int norm,
@@ -176,9 +249,13 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ topk_idx, int T, 
   pair_row[i] = r;
 }
 
-// The whole route in one CTA for decode-sized batches (T * k <= kSmallPairs, E <= 1024): top-k
-// per token (one warp each), histogram in shared memory, the scans, and the scatter.
+// The whole route in one CTA for decode-sized batches (T <= kSmallTokens, T * k <= kSmallPairs,
+// E <= 1024): top-k per token (one warp each), histogram in shared memory, the scans, and the
+// scatter.
 constexpr int kSmallPairs = 4096;
+// Above this many tokens the top-k runs on many SMs (one CTA holds the route of a decode step;
+// a larger batch would queue all its tokens on one SM's warps).
+constexpr int kSmallTokens = 64;
 __global__ void __launch_bounds__(1024) moe_route_small_kernel(const float* __restrict__ logits, int T, int E, int k,
                                                                int norm, int tile_rows, int32_t* __restrict__ topk_idx,
                                                                float* __restrict__ topk_w, int32_t* __restrict__ counts,
@@ -282,7 +359,7 @@ extern "C" int ql_moe_route(const float* logits, int T, int E, int top_k, int no
     return QL_ERR_ARG;
   }
   cudaStream_t st = (cudaStream_t)stream;
-  if ((long)T * top_k <= kSmallPairs) {   // decode: one launch
+  if (T <= kSmallTokens && (long)T * top_k <= kSmallPairs) {   // decode: one launch
     moe_route_small_kernel<<<1, 1024, 0, st>>>(logits, T, E, top_k, norm_topk_prob, tile_rows, topk_idx, topk_w, counts,
                                                offsets, active, n_active, tiles, n_tiles, max_tiles, row_token,
                                                pair_row);
@@ -392,8 +469,23 @@ static bool grouped_uses_gemm(long P, int E, int K, int gs) {
   return act > 0 && P >= (long)min_avg * act && K % 64 == 0 && (gs % 64 == 0 || gs == 32);
 }
 
+// Token-tile height of the grouped tensor-core GEMM for an average of `avg` rows per active
+// expert. A tile dequantises its expert's weight tile once whatever its height, and its MMA work
+// grows with the height, so the lowest tile that holds most experts' rows wins: 32 up to 32
+// rows on average, 64 up to 80, else 128.
+static int gemm_tile_rows(long P, int E) {
+  static int forced = -1;
+  if (forced < 0) forced = env_int("QL_MOE_GEMM_TILE", 0);
+  if (forced == 32 || forced == 64 || forced == 128) return forced;
+  const long act = P < E ? P : E;
+  const long avg = act > 0 ? (P + act - 1) / act : 0;
+  return avg <= 32 ? 32 : avg <= 80 ? 64 : 128;
+}
+
+static bool is_gemm_tile(int tile_rows) { return tile_rows == 32 || tile_rows == 64 || tile_rows == 128; }
+
 extern "C" int ql_moe_tile_rows(long P, int E, int K, int gs, int max_rows_per_expert) {
-  if (grouped_uses_gemm(P, E, K, gs)) return 128;
+  if (grouped_uses_gemm(P, E, K, gs)) return gemm_tile_rows(P, E);
   return max_rows_per_expert <= 4 ? 4 : max_rows_per_expert <= 8 ? 8 : 16;
 }
 
@@ -439,11 +531,11 @@ static int grouped_matmul_impl(const void* x, int x_dtype, long ldx, const int32
   if (P == 0) return QL_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const long qw_es = (long)(K / per) * N, qz_es = (long)(K / gs) * (N / per), sc_es = (long)(K / gs) * N;
-  if (glu && tile_rows == 128 && grouped_uses_gemm(P, E, K, gs)) {
+  if (glu && is_gemm_tile(tile_rows) && grouped_uses_gemm(P, E, K, gs)) {
     set_error("ql_moe_grouped_matmul_swiglu: the tensor-core path takes activations (run ql_moe_act first)");
     return QL_ERR_UNSUPPORTED;
   }
-  if (tile_rows == 128 && grouped_uses_gemm(P, E, K, gs)) {
+  if (is_gemm_tile(tile_rows) && grouped_uses_gemm(P, E, K, gs)) {
     if (!tiles || !n_tiles || max_tiles <= 0) {
       set_error("ql_moe_grouped_matmul: the tensor-core path needs the routing tile table");
       return QL_ERR_ARG;
