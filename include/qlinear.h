@@ -207,7 +207,8 @@ QL_API int ql_moe_group(const int32_t* ids, int n, int G, int tile_rows, int32_t
 
 /* Tile height the grouped matmul expects in the routing tile table for P rows over E experts of
  * a K-input projection: 32, 64 or 128 when it takes the tensor-core GEMM (from the average rows
- * per active expert), else 4, 8 or 16 (decode GEMV tiles, from the bound on rows per expert).
+ * per active expert), else 4, 8 or 16 (decode GEMV tiles: about twice the average rows per
+ * active expert, at most the bound on rows per expert).
  * Pass it as ql_moe_route's tile_rows.
  * No counterpart in the reference. */
 QL_API int ql_moe_tile_rows(long P, int E, int K, int gs, int max_rows_per_expert);

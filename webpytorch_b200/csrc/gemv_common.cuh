@@ -193,9 +193,48 @@ __device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half*
 // t) and rows are rounded up to 8 slots: a warp's 64-bit loads of one step read rows t = 0..3,
 // 4 slots each per half-warp, and the swizzle places the 4 rows 8 banks apart. Without it
 // (up to 4 tokens) rows are 2M slots, unpadded.
-__host__ __device__ __forceinline__ int xb_slots(int slots) { return slots <= 4 ? slots : (slots + 7) & ~7; }
+__host__ __device__ constexpr int xb_slots(int slots) { return slots <= 4 ? slots : (slots + 7) & ~7; }
 __host__ __device__ __forceinline__ int xb_swz(int sstride, int t) {
   return sstride <= 4 ? 0 : (sstride % 16 == 0 ? 4 * t : 4 * (t >> 1));
+}
+
+// Stage one 8-value chunk (chunk kc of a token's slice, scaled by s) of token m into the B
+// operand layout described below; returns the chunk's sum of staged integers.
+template <int BITS, bool SWZ>
+__device__ __forceinline__ int put_chunk_i8(const float (&v)[8], float s, int m, int kc, int sstride, uint2* xb) {
+  uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
+  int sum = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int q = __float2int_rn(v[j] * s);
+    const int l = (int)(int8_t)(q & 0xff);
+    const int h = (q - l) >> 8;
+    sum += q;
+    // int4: even offsets -> register 0, odd -> register 1; int8: first row -> 0, second -> 1
+    const int reg = BITS == 4 ? (j & 1) : (j >> 2);
+    const int byte = BITS == 4 ? (j >> 1) : (j & 3);
+    hi[reg] |= (uint32_t)(h & 0xff) << (8 * byte);
+    lo[reg] |= (uint32_t)(l & 0xff) << (8 * byte);
+  }
+  if constexpr (BITS == 4) {
+    const int s4 = kc >> 2, t = kc & 3;
+    uint2* dst = xb + (s4 * 4 + t) * sstride + (SWZ ? (2 * m) ^ xb_swz(sstride, t) : 2 * m);
+    dst[0] = make_uint2(hi[0], hi[1]);
+    dst[1] = make_uint2(lo[0], lo[1]);
+  } else {
+    const int r0 = 2 * kc;                // rows r0, r0 + 1 of the same half of a step
+    const int s8 = r0 >> 3, j = r0 & 7;
+    const int half = j >> 2, t0 = j & 3;
+    const int c0 = SWZ ? (2 * m) ^ xb_swz(sstride, t0) : 2 * m;
+    const int c1 = SWZ ? (2 * m) ^ xb_swz(sstride, t0 + 1) : 2 * m;
+    uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * sstride + c0) + half;
+    uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * sstride + c1) + half;
+    d0[0] = hi[0];
+    d0[2] = lo[0];
+    d1[0] = hi[1];
+    d1[2] = lo[1];
+  }
+  return sum;
 }
 
 // Stage x[:, kbase : kbase + klen] for M <= 16 tokens as the B operand of the integer MMA
@@ -230,38 +269,7 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, int 
   auto store_chunk = [&](int idx, const float (&v)[8]) {
     const int m = M == 1 ? 0 : idx / cpr, kc = idx - m * cpr;
     const float s = exp2i(-stage_exponent_i15(__uint_as_float(sh_max[m])));
-    uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
-    int sum = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int q = __float2int_rn(v[j] * s);
-      const int l = (int)(int8_t)(q & 0xff);
-      const int h = (q - l) >> 8;
-      sum += q;
-      // int4: even offsets -> register 0, odd -> register 1; int8: first row -> 0, second -> 1
-      const int reg = BITS == 4 ? (j & 1) : (j >> 2);
-      const int byte = BITS == 4 ? (j >> 1) : (j & 3);
-      hi[reg] |= (uint32_t)(h & 0xff) << (8 * byte);
-      lo[reg] |= (uint32_t)(l & 0xff) << (8 * byte);
-    }
-    if constexpr (BITS == 4) {
-      const int s4 = kc >> 2, t = kc & 3;
-      uint2* dst = xb + (s4 * 4 + t) * sstride + (SWZ ? (2 * m) ^ xb_swz(sstride, t) : 2 * m);
-      dst[0] = make_uint2(hi[0], hi[1]);
-      dst[1] = make_uint2(lo[0], lo[1]);
-    } else {
-      const int r0 = 2 * kc;                // rows r0, r0 + 1 of the same half of a step
-      const int s8 = r0 >> 3, j = r0 & 7;
-      const int half = j >> 2, t0 = j & 3;
-      const int c0 = SWZ ? (2 * m) ^ xb_swz(sstride, t0) : 2 * m;
-      const int c1 = SWZ ? (2 * m) ^ xb_swz(sstride, t0 + 1) : 2 * m;
-      uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * sstride + c0) + half;
-      uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * sstride + c1) + half;
-      d0[0] = hi[0];
-      d0[2] = lo[0];
-      d1[0] = hi[1];
-      d1[2] = lo[1];
-    }
+    int sum = put_chunk_i8<BITS, SWZ>(v, s, m, kc, sstride, xb);
     // the SEG chunks of one group sit in SEG consecutive lanes
 #pragma unroll
     for (int o = SEG / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -351,5 +359,60 @@ __device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, int 
   sync();
 }
 
+// Activations staged once in global memory for the TMA-fed GEMVs of more than 4 tokens, so no
+// CTA stages them itself: tokens in chunks of MAXM, chunk c at xg + c * chunk_bytes holding the
+// B operand of all K (rows of xb_slots(2 MAXM) slots, swizzled, as stage_x_i8 with SWZ) and, at
+// sum_off, the group sums as [group][MAXM]. xe[m] = the token's exponent e (x = v * 2^e), or
+// kNonFinite for a row with inf / nan.
+constexpr int kNonFinite = (int)0x80000000;
+
 }  // namespace gemv
+
+namespace {
+// One CTA per token row (256 threads): the row's absolute maximum, then its 8-value chunks.
+template <int BITS, int GS, int MAXM, class Args>
+__global__ void __launch_bounds__(256) prestage_x_kernel(const Args a, int K, uint8_t* __restrict__ xg, long chunk_bytes,
+                                                         long sum_off, int* __restrict__ xe) {
+  constexpr int SEG = GS / 8;
+  constexpr int SS = gemv::xb_slots(2 * MAXM);
+  __shared__ float s_max[8];
+  const int m = blockIdx.x, c = m / MAXM, mm = m - c * MAXM;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int cpr = K / 8;
+  float mx = 0.f;
+  for (int kc = tid; kc < cpr; kc += 256) {
+    float v[8];
+    gemv::load_x8(a, m, kc * 8, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
+    if (mx != mx) mx = __int_as_float(0x7f800000);   // NaN counts as non-finite
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_max[warp] = mx;
+  __syncthreads();
+  mx = s_max[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_max[w]);
+  const int e = stage_exponent_i15(mx);
+  if (tid == 0) xe[m] = mx < 3.0e38f ? e : gemv::kNonFinite;
+  const float s = exp2i(-e);
+  uint2* xb = reinterpret_cast<uint2*>(xg + (long)c * chunk_bytes);
+  int* gsum = reinterpret_cast<int*>(xg + (long)c * chunk_bytes + sum_off);
+  for (int base = 0; base < cpr; base += 256) {   // warp-uniform trip count (group shuffles)
+    const int kc = base + tid;
+    float v[8];
+    if (kc < cpr) {
+      gemv::load_x8(a, m, kc * 8, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+    int sum = kc < cpr ? gemv::put_chunk_i8<BITS, true>(v, s, mm, kc, SS, xb) : 0;
+#pragma unroll
+    for (int o = SEG / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (kc < cpr && kc % SEG == 0) gsum[(kc / SEG) * MAXM + mm] = sum;
+  }
+}
+}  // namespace
 }  // namespace ql

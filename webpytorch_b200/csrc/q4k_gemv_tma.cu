@@ -66,6 +66,11 @@ struct Q4kTmaArgs {
   int cs;       // cluster size along K
   int mchunk;   // tokens per z-slice
   int nst;      // ring stages (the kernel's NST)
+  // activations staged in global memory (more than 4 tokens): chunk of z-slice c at
+  // xg + c * chunk_bytes (B operand of all K, then the sub-block sums at sum_off), exponents xe
+  const uint8_t* xg;
+  long chunk_bytes, sum_off;
+  const int* xe;
 };
 
 // activation source in the form gemv::load_x8 reads
@@ -80,9 +85,15 @@ struct XSrc {
   int glu;
 };
 
-template <int NST>
+// Ring stage: the weights' TMA box, then with XP (activations staged in global memory) the
+// stage's B operand (8 steps x 4 lanes x kXSlots slots x 8 bytes) and sub-block sums [8][MAXM].
+template <int NST, int MAXM, bool XP>
 struct Layout {
-  static constexpr int kBarOff = NST * kStageBytes;
+  static constexpr int kXSlots = gemv::xb_slots(2 * MAXM);
+  static constexpr int kXBytes = XP ? kBlkVals * kXSlots : 0;
+  static constexpr int kSBytes = XP ? 8 * MAXM * 4 : 0;
+  static constexpr int kStage = kStageBytes + kXBytes + kSBytes;   // a multiple of 128
+  static constexpr int kBarOff = NST * kStage;
   static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier + abort flag
 };
 
@@ -94,11 +105,12 @@ __device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t r
 
 // Two CTAs per SM: registers are allocated per pair of warps, so the 9 warps count as 10 and the
 // limit is 96 registers per thread.
-template <int NQ, int NST>
+template <int NQ, int NST, bool XP>
 __global__ void __launch_bounds__(kThreads, 2)
     q4k_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const Q4kTmaArgs a) {
-  using L = Layout<NST>;
   constexpr int MAXM = 4 * NQ;
+  using L = Layout<NST, MAXM, XP>;
+  static_assert(L::kStage % 128 == 0, "stage alignment");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ int sh_exp[16];
@@ -121,12 +133,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // staged activations: B rows of sstride slots (swizzled), sub-block sums gstride ints apart
   // (2 mod 8: the 4 tokens' pairs of sums a warp reads at once sit in distinct banks)
   constexpr bool SWZ = NQ > 1;   // swizzled B rows (more than 4 tokens)
-  const int sstride = SWZ ? gemv::xb_slots(2 * M) : 2 * M;
+  const int sstride = XP ? L::kXSlots : (SWZ ? gemv::xb_slots(2 * M) : 2 * M);
   const int gstride = nbl_max * 8 + 2;
   uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
-  const int xs_bytes = (nbl_max * kBlkVals * sstride + 15) & ~15;
+  const int xs_bytes = XP ? 0 : (nbl_max * kBlkVals * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
-  const int gs_bytes = (M * gstride * 4 + 15) & ~15;
+  const int gs_bytes = XP ? 0 : (M * gstride * 4 + 15) & ~15;
   // split-K partials received by this rank: [cs ranks][MAXM tokens][rows_max rows]; rank q
   // owns the CTA rows [orow(q), orow(q + 1)), orow(q) = ceil(q * kRows / cs)
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
@@ -152,6 +164,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       ptx::tma_prefetch(&tmap);
       const int row0 = blockIdx.y * kRows;
+      const uint8_t* xgc = XP ? a.xg + (long)blockIdx.z * a.chunk_bytes : nullptr;
+      if (XP) pdl_wait();   // the staged activations are the previous kernel's output
       int i = 0;
       bool ok = true;
       for (; i < nbl; ++i) {
@@ -162,8 +176,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         const uint32_t fb = bar_full + 8 * s;
-        ptx::mbar_arrive_expect_tx(fb, kStageBytes);
-        ptx::tma_load_2d(sbase + s * kStageBytes, &tmap, fb, (b0 + i) * kBlkBytes, row0);
+        const uint32_t st = sbase + s * L::kStage;
+        ptx::mbar_arrive_expect_tx(fb, L::kStage);
+        ptx::tma_load_2d(st, &tmap, fb, (b0 + i) * kBlkBytes, row0);
+        if constexpr (XP) {
+          ptx::bulk_load(st + kStageBytes, xgc + (long)(b0 + i) * L::kXBytes, L::kXBytes, fb);
+          ptx::bulk_load(st + kStageBytes + L::kXBytes, xgc + a.sum_off + (long)(b0 + i) * L::kSBytes, L::kSBytes, fb);
+        }
       }
       if (nbl <= NST) pdl_trigger();
       if (!ok) {
@@ -179,12 +198,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int g = lane >> 2, t = lane & 3;
     const int slots = 2 * M;
     pdl_wait();   // x may be the previous kernel's output
-    const XSrc xsrc{reinterpret_cast<const char*>(a.x) + (size_t)tok0 * a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u),
-                    nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, M, 0};
-    // int8 staging order = natural K order: a 32-K step's B fragment (t) holds K 4t .. 4t + 3
-    // and 16 + 4t .. 16 + 4t + 3; the sums are per 32 values, one Q4_K sub-block
-    gemv::stage_x_i8<8, 32, true, SWZ>(xsrc, b0 * kBlkVals, nbl * kBlkVals, gstride, sstride, xb, gsum, sh_exp, sh_max,
-                                  tid, kCW * 32);
+    if constexpr (!XP) {
+      const XSrc xsrc{reinterpret_cast<const char*>(a.x) + (size_t)tok0 * a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u),
+                      nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, M, 0};
+      // int8 staging order = natural K order: a 32-K step's B fragment (t) holds K 4t .. 4t + 3
+      // and 16 + 4t .. 16 + 4t + 3; the sums are per 32 values, one Q4_K sub-block
+      gemv::stage_x_i8<8, 32, true, SWZ>(xsrc, b0 * kBlkVals, nbl * kBlkVals, gstride, sstride, xb, gsum, sh_exp,
+                                         sh_max, tid, kCW * 32);
+    }
 
     float acc[NQ][2];
 #pragma unroll
@@ -195,7 +216,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = 0; i < nbl; ++i) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
-      const unsigned char* p0 = smem + s * kStageBytes + r0 * kBlkBytes;
+      const unsigned char* p0 = smem + s * L::kStage + r0 * kBlkBytes;
+      // B operand and sums of this stage: staged in the ring (XP) or once for the CTA's slice
+      const uint32_t xstage = XP ? sbase + s * L::kStage + kStageBytes : xb_base + i * 8 * 4 * sstride * 8;
+      const int* sstage = XP ? reinterpret_cast<const int*>(smem + s * L::kStage + kStageBytes + L::kXBytes) : nullptr;
       const unsigned char* p1 = p0 + 8 * kBlkBytes;
       const uint4 h0 = *reinterpret_cast<const uint4*>(p0);
       const uint4 h1 = *reinterpret_cast<const uint4*>(p1);
@@ -222,7 +246,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int mq = 0; mq < NQ; ++mq) {
           const int tok = 4 * mq + t;
-          S2[mq] = tok < M ? *reinterpret_cast<const int2*>(gsum + tok * gstride + i * 8 + 2 * G) : make_int2(0, 0);
+          if constexpr (XP)
+            S2[mq] = tok < M ? make_int2(sstage[(2 * G) * MAXM + tok], sstage[(2 * G + 1) * MAXM + tok]) : make_int2(0, 0);
+          else
+            S2[mq] = tok < M ? *reinterpret_cast<const int2*>(gsum + tok * gstride + i * 8 + 2 * G) : make_int2(0, 0);
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -234,13 +261,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int s1 = (int)__byte_perm(sc1[j >> 2], 0u, 0x4440u + (j & 3)) << (u ? 0 : 4);
           const int m0 = (int)__byte_perm(mn0[j >> 2], 0u, 0x4440u + (j & 3));
           const int m1 = (int)__byte_perm(mn1[j >> 2], 0u, 0x4440u + (j & 3));
-          const int step = i * 8 + j;   // 32-K step inside this rank's slice
 #pragma unroll
           for (int mq = 0; mq < NQ; ++mq) {
             const int slot = 8 * mq + g;
             uint32_t b0 = 0u, b1 = 0u;
             if (slot < slots) {
-              const uint32_t xa = xb_base + ((step * 4 + t) * sstride + (slot ^ swz)) * 8;
+              const uint32_t xa = xstage + ((j * 4 + t) * sstride + (slot ^ swz)) * 8;
               asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
             }
             int d[4] = {0, 0, 0, 0};
@@ -270,8 +296,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     // non-finite activation rows give NaN (the integer staging cannot carry inf / nan)
     auto finish = [&](int tok, float v) {
-      const float mx = __uint_as_float(sh_max[tok]);
-      return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+      if constexpr (XP) {
+        const int e = a.xe[tok0 + tok];
+        return e != gemv::kNonFinite ? v * exp2i(e) : __int_as_float(0x7fc00000);
+      } else {
+        const float mx = __uint_as_float(sh_max[tok]);
+        return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+      }
     };
     if (cs == 1) {
 #pragma unroll
@@ -346,16 +377,21 @@ EncodeTiledFn encode_fn() {
 
 constexpr int kNST = 4;
 
-// dynamic shared memory of one CTA with an nst-stage ring, as the kernel carves it up
-size_t smem_bytes(int mchunk, int nb, int cs, int nq, int nst) {
+// dynamic shared memory of one CTA with an nst-stage ring, as the kernel carves it up (xp:
+// activations staged in global memory and carried by the ring)
+size_t smem_bytes(int mchunk, int nb, int cs, int nq, int nst, bool xp) {
   const int nbl_max = (nb + cs - 1) / cs;
+  const size_t red = cs > 1 ? (size_t)cs * 4 * nq * ((kRows + cs - 1) / cs) * 4 : 0;
+  if (xp) {
+    const size_t stage = kStageBytes + (size_t)kBlkVals * gemv::xb_slots(8 * nq) + 8 * 4 * nq * 4;
+    return 1024 + (size_t)nst * stage + 2 * nst * 8 + 16 + red;
+  }
   const size_t xs = ((size_t)nbl_max * kBlkVals * gemv::xb_slots(2 * mchunk) + 15) & ~(size_t)15;
   const size_t gsb = ((size_t)mchunk * (nbl_max * 8 + 2) * 4 + 15) & ~(size_t)15;
-  const size_t red = cs > 1 ? (size_t)cs * 4 * nq * ((kRows + cs - 1) / cs) * 4 : 0;
   return 1024 + (size_t)nst * kStageBytes + 2 * nst * 8 + 16 + xs + gsb + red;
 }
 
-template <int NQ, int NST>
+template <int NQ, int NST, bool XP>
 int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
@@ -369,7 +405,7 @@ int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return -1;
-  auto kern = q4k_gemv_tma_kernel<NQ, NST>;
+  auto kern = q4k_gemv_tma_kernel<NQ, NST, XP>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -384,6 +420,14 @@ int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.cs, (a.N + kRows - 1) / kRows, (a.M + a.mchunk - 1) / a.mchunk);
+  if constexpr (XP) {
+    // stage the activations once: one CTA per token row, chunks of 4 NQ tokens
+    const XSrc xsrc{a.x, nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, a.M, 0};
+    prestage_x_kernel<8, 32, 4 * NQ><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg), a.chunk_bytes,
+                                                         a.sum_off, const_cast<int*>(a.xe));
+    const int rc = cuda_status(cudaGetLastError(), "q4k prestage launch");
+    if (rc) return rc;
+  }
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -428,9 +472,14 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   a.bias = bias; a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N;
   a.nb = K / kBlkVals;
+  // up to 4 tokens: one z-slice that stages its own activations; more: activations staged
+  // once in global memory (prestage_x_kernel), z-slices of 4 NQ tokens
+  static int prestage = -1;
+  if (prestage < 0) prestage = env_int("QL_Q4K_PRESTAGE", 1);
+  const bool xp = M > 4 && prestage;
   int mchunk = M <= 4 ? 4 : (M <= 8 || chunk_max == 8 ? 8 : (chunk_max == 4 ? 4 : 16));
   if (M > 8 && chunk_max == 4) mchunk = 4;
-  if (mchunk > M) mchunk = M;
+  if (mchunk > M && !xp) mchunk = M;
   a.mchunk = mchunk;
   const int nq = (mchunk + 3) / 4;
   const int zdim = (M + mchunk - 1) / mchunk;
@@ -440,7 +489,7 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   double best = -1.0;
   for (int ns = kNST; ns >= 2; ns -= 2) {   // ring depths built: 4 and 2
     for (int c = 1; c <= 8 && c <= a.nb; ++c) {
-      const size_t sm = smem_bytes(mchunk, a.nb, c, nq, ns);
+      const size_t sm = smem_bytes(mchunk, a.nb, c, nq, ns, xp);
       if (sm > 220 * 1024) continue;
       const int fit = (int)(per_sm / (sm + 1024 + 256));
       const int per = fit >= 2 ? 2 : fit;
@@ -462,12 +511,39 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   if (best_cs == 0) return false;
   a.cs = best_cs;
   a.nst = best_nst;
-  const size_t smem = smem_bytes(mchunk, a.nb, a.cs, nq, a.nst);
+  const size_t smem = smem_bytes(mchunk, a.nb, a.cs, nq, a.nst, xp);
+  void* ws = nullptr;
+  if (xp) {
+    // per chunk: B operand of all K (K * slots bytes), then [K / 32][4 NQ] sums; then exponents
+    a.sum_off = (long)K * gemv::xb_slots(8 * nq);
+    a.chunk_bytes = (a.sum_off + (long)(K / 32) * 4 * nq * 4 + 255) & ~255L;
+    const size_t need = (size_t)zdim * a.chunk_bytes + (size_t)M * 4;
+    const int arc = cuda_status(cudaMallocAsync(&ws, need, st), "cudaMallocAsync(q4k staging)");
+    if (arc) {
+      *rc = arc;
+      return true;
+    }
+    a.xg = reinterpret_cast<const uint8_t*>(ws);
+    a.xe = reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(ws) + (size_t)zdim * a.chunk_bytes);
+  }
   int r;
-  switch (nq) {
-    case 1: r = a.nst == kNST ? launch<1, kNST>(a, raw, smem, st) : launch<1, 2>(a, raw, smem, st); break;
-    case 2: r = a.nst == kNST ? launch<2, kNST>(a, raw, smem, st) : launch<2, 2>(a, raw, smem, st); break;
-    default: r = a.nst == kNST ? launch<4, kNST>(a, raw, smem, st) : launch<4, 2>(a, raw, smem, st); break;
+  if (xp) {
+    switch (nq) {
+      case 2: r = a.nst == kNST ? launch<2, kNST, true>(a, raw, smem, st) : launch<2, 2, true>(a, raw, smem, st); break;
+      default: r = a.nst == kNST ? launch<4, kNST, true>(a, raw, smem, st) : launch<4, 2, true>(a, raw, smem, st); break;
+    }
+    const int frc = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(q4k staging)");
+    if (r == 0) r = frc;
+    if (r < 0) {   // declined after the staging ran: report, the register kernel would redo it
+      set_error("ql_q4k_matmul: tensor-map encoding failed");
+      r = QL_ERR_CUDA;
+    }
+  } else {
+    switch (nq) {
+      case 1: r = a.nst == kNST ? launch<1, kNST, false>(a, raw, smem, st) : launch<1, 2, false>(a, raw, smem, st); break;
+      case 2: r = a.nst == kNST ? launch<2, kNST, false>(a, raw, smem, st) : launch<2, 2, false>(a, raw, smem, st); break;
+      default: r = a.nst == kNST ? launch<4, kNST, false>(a, raw, smem, st) : launch<4, 2, false>(a, raw, smem, st); break;
+    }
   }
   if (r < 0) return false;
   *rc = r;
