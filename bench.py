@@ -551,6 +551,36 @@ def main():
                                        "GB/s": round(gemv_bytes(K, N) / res["plain"] / 1e3, 1),
                                        "GB/s_pdl": round(gemv_bytes(K, N) / res["pdl"] / 1e3, 1)}
 
+    # ---- the whole config-1 sweep: bits in {4, 8} x M in {1, 4, 16}, one graph over COPIES
+    # copies of the five shapes per point (weights from HBM), GB/s of algorithmic bytes
+    sweep = {}
+    if world == 1 and not args.skip_extra:
+        for bits in (4, 8):
+            ws = [(L[0], L[1], L[2], L[3], L[4]) for L in lay] if bits == 4 else \
+                 [(K, N) + tuple(rand_gptq(K, N, dev, g, bits=bits)) for _ in range(COPIES) for (K, N) in SHAPES]
+            for M in (1, 4, 16):
+                xs = {K: torch.randn((M, K), device=dev, generator=g).half() for K, _ in SHAPES}
+                ys = {N: torch.empty((M, N), device=dev) for _, N in SHAPES}
+
+                def one_pass():
+                    for (K, N, qw, qz, sc) in ws:
+                        _gptq_matmul(xs[K], qw, qz, sc, K, N, GS, bits, 1.0, out=ys[N])
+                one_pass()
+                torch.cuda.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    one_pass()
+                for _ in range(3):
+                    gr.replay()
+                us = event_time(gr.replay, 20) * 1e3
+                nbytes = sum(gemv_bytes(K, N, M=M, bits=bits) for (K, N, _, _, _) in ws)
+                sweep["int%d_M%d" % (bits, M)] = {"us_per_pass": round(us, 2),
+                                                   "GB/s": round(nbytes / us / 1e3, 1),
+                                                   "frac_of_hbm": round(nbytes / us / 1e3 / peaks()[0], 4)}
+                del gr, xs, ys
+            del ws
+        torch.cuda.empty_cache()
+
     # ---- e2e: public operator path with pinned host buffers, copies inside the timed region
     hx = [torch.empty(L[5].shape, dtype=L[5].dtype, pin_memory=True).copy_(L[5].cpu()) for L in lay]
     hy = [torch.empty(L[6].shape, dtype=L[6].dtype, pin_memory=True) for L in lay]
@@ -633,6 +663,9 @@ def main():
                      "avg_launch_us": round(avg_launch_us, 3)},
         "value_with_pdl": round(value_pdl, 2),
         "per_shape": per_shape,
+        "config1_sweep": {"basis": "one pass = %d GEMVs (%d copies of the 5 shapes, weights from HBM), fp16 x, "
+                                   "fp32 out; algorithmic bytes / pass time" % (COPIES * len(SHAPES), COPIES),
+                          "points": sweep},
         "gemm": {"workload": "config3: int4 g128 desc_act dequant-GEMM, bf16 x/out, M in %s (act-order gather "
                              "+ fp16 staging + tcgen05 GEMM per call)" % (GEMM_MS,),
                  "bound": "tensor", "peak_TFLOP/s": peaks()[1], "shapes": gemm},

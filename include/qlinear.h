@@ -93,8 +93,9 @@ QL_API int ql_gptq_matmul(const void* x, int x_dtype, long ldx, const int32_t* x
                    int M, int K, int N, int gs, int bits, float zero_offset, void* stream);
 
 /*
- * Bytes of device workspace ql_gptq_matmul_ws needs for an M x K activation on the
- * tensor-core (large-M) path: the fp16 staging of x plus one int per row.
+ * Bytes of device workspace ql_gptq_matmul_ws needs for an M x K activation: on the tensor-core
+ * (large-M) path the fp16 staging of x plus one int per row, on the decode path (more than 4
+ * tokens) the activations staged once as the integer MMA's operand.
  * No counterpart in the reference (its WebGPU buffers are allocated per call, _core.py:4022).
  */
 QL_API size_t ql_gptq_matmul_workspace(int M, int K);
@@ -121,7 +122,8 @@ QL_API int ql_gptq_matmul_ws(const void* x, int x_dtype, long ldx, const int32_t
  * whose M x K needs more than that fail with QL_ERR_UNSUPPORTED. The first call on a device
  * resolves the array's device address, so make one call per device before any stream capture.
  * All calls share the array: calls that can overlap on the GPU (different streams) race and
- * must be serialised by the caller. Small-M calls use no scratch at all.
+ * must be serialised by the caller. Calls of up to 4 tokens use no scratch at all (decode calls
+ * of 5 to 63 tokens stage their activations there).
  * No counterpart in the reference.
  */
 QL_API int ql_gptq_matmul_noalloc(const void* x, int x_dtype, long ldx, const int32_t* x_perm,

@@ -162,6 +162,25 @@ def test_large_activation_range_is_staged_exactly():
         assert max_rel_err(y[m], ref[m]) < TOL, m
 
 
+@pytest.mark.parametrize("M", [8, 12])
+def test_staged_activations_extreme_and_nonfinite_rows(M):
+    """Decode calls of more than 4 tokens stage the activations once in global memory: rows far
+    outside fp16 range are scaled exactly, a row holding inf / nan gives a NaN output row."""
+    K, N = 1024, 256
+    w = synth.gptq_weights(K, N, 4, 128, seed=6)
+    x = synth.activations(M, K, np.float32, seed=M)
+    x[0] *= 1e6
+    x[1] *= 1e-6
+    x[2, 5] = 3e5
+    x[3, 7] = np.inf
+    ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4)
+    y = ql(_t(x)).cpu().numpy()
+    ref = og.gptq_matmul(np.nan_to_num(x, posinf=0.0), w["qweight"], w["qzeros"], w["scales"], K, N, 128, 4, 1.0)
+    assert np.isnan(y[3]).all()
+    for m in [r for r in range(M) if r != 3]:
+        assert max_rel_err(y[m], ref[m]) < TOL, m
+
+
 def test_empty_batch():
     w = synth.gptq_weights(256, 64, 4, 128, seed=1)
     ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4)

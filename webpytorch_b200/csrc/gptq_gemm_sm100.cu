@@ -715,7 +715,18 @@ int take_tc_status() {
 
 }  // namespace ql
 
-extern "C" size_t ql_gptq_matmul_workspace(int M, int K) { return ql::gptq_gemm_workspace(M, K); }
+namespace ql {
+size_t gemv_stage_workspace(int M, int K, int kgs);
+}
+
+// The larger of the two paths' needs: the tensor-core path's fp16 staging, and the decode path's
+// staged activations for up to 16 tokens a launch (counted for 32-value groups, the most sums).
+extern "C" size_t ql_gptq_matmul_workspace(int M, int K) {
+  if (M <= 0 || K <= 0) return 0;
+  const size_t gemm = ql::gptq_gemm_workspace(M, K);
+  const size_t gemv = ql::gemv_stage_workspace(M < 16 ? M : 16, K, 32);
+  return gemm > gemv ? gemm : gemv;
+}
 
 namespace ql {
 int take_tma_gemv_status();
@@ -789,8 +800,9 @@ extern "C" int ql_gptq_matmul_noalloc(const void* x, int x_dtype, long ldx, cons
                                       int M, int K, int N, int gs, int bits, float zero_offset, void* stream) {
   void* ws = nullptr;
   size_t ws_bytes = 0;
-  if (M > 0 && K > 0 && gs > 0 && ql::gemm_path_taken(M, K, gs)) {
-    const size_t need = ql::gptq_gemm_workspace(M, K);
+  const bool gemm = M > 0 && K > 0 && gs > 0 && ql::gemm_path_taken(M, K, gs);
+  if (gemm || (M > 4 && K > 0 && gs > 0)) {   // tensor-core path, or staged decode activations
+    const size_t need = gemm ? ql::gptq_gemm_workspace(M, K) : ql::gemv_stage_workspace(M < 16 ? M : 16, K, 32);
     if (need > ql::kNoAllocScratchBytes) {
       ql::set_error("ql_gptq_matmul_noalloc: M=%d x K=%d needs %zu bytes of scratch; this entry point has %zu "
                     "(use ql_gptq_matmul_ws with a workspace, or split M)",

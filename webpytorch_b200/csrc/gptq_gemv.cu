@@ -479,15 +479,17 @@ inline int pow2_floor(int v) {
 bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
-                   int* rc);
+                   int* rc, void* workspace, size_t ws_bytes);
 
-// Picks the K split (cluster size) so the grid holds ~16 warps per SM, then launches.
+// The TMA-fed GEMV when it takes the shape; else the register-fed kernel below, with the K split
+// (cluster size) picked so the grid holds ~16 warps per SM.
 int gptq_gemv(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
               const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
-              int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st) {
+              int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
+              void* workspace, size_t ws_bytes) {
   int trc = 0;
   if (gptq_gemv_tma(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, sc_dtype, bias, out, out_dtype, ldo, M, K, N,
-                    gs, bits, zoff, st, &trc))
+                    gs, bits, zoff, st, &trc, workspace, ws_bytes))
     return trc;
   // kernel group: the largest of {128, 64, 32} dividing the checkpoint's group size
   const int kgs = (gs % 128 == 0) ? 128 : (gs % 64 == 0) ? 64 : 32;
@@ -718,7 +720,7 @@ int ql::gptq_matmul_impl(const void* x, int x_dtype, long ldx, const int32_t* x_
     const char* xb = reinterpret_cast<const char*>(x) + (long)m0 * ldx * (x_dtype == QL_F32 ? 4 : 2);
     char* ob = reinterpret_cast<char*>(out) + (long)m0 * ldo * (out_dtype == QL_F32 ? 4 : 2);
     rc = gptq_gemv(xb, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, ob, out_dtype, ldo,
-                   mc, K, N, gs, bits, zero_offset, st);
+                   mc, K, N, gs, bits, zero_offset, st, workspace, ws_bytes);
     if (rc) return rc;
   }
   return QL_OK;

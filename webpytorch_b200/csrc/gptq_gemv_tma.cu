@@ -74,6 +74,11 @@ struct TmaGemvArgs {
   int g_max_tiles;  // host: table capacity (grid z)
   int n_experts;    // host: stacked weight matrices (1 when dense)
   int glu;          // > 0: x rows are [gate | up] glu elements apart (SwiGLU applied when staging)
+  // dense calls of more than 4 tokens: activations staged once in global memory (one chunk:
+  // the B operand of all K, then the group sums at xg_sum_off) and exponents xe
+  const uint8_t* xg;
+  long xg_sum_off;
+  const int* xe;
 };
 
 // Activation source of one CTA (its rows of x, possibly gathered).
@@ -88,7 +93,9 @@ struct XSrc {
   int glu;   // > 0: rows are [gate | up] glu elements apart; the activation is silu(gate) * up
 };
 
-template <int BITS, int GS, int NST, int SCB, int SW>
+// Ring stage: weights, scales, zeros; with XP also the stage's B operand (4 steps x 4 lanes x
+// kXSlots slots x 8 bytes) and its group sums [GPS][MAXM].
+template <int BITS, int GS, int NST, int SCB, int SW, int MAXM = 4, bool XP = false>
 struct TmaLayout {
   static constexpr int PER = 32 / BITS;
   static constexpr int TC = 32 * SW;                       // columns per CTA tile
@@ -98,16 +105,20 @@ struct TmaLayout {
   static constexpr int kWBytes = SW * kStripBytes;         // 2 KB per strip (int4) / 4 KB (int8)
   static constexpr int kScBytes = GPS * TC * SCB;          // scales of the stage
   static constexpr int kZBytes = GPS * (TC / PER) * 4;
-  static constexpr int kStageBytes = (kWBytes + kScBytes + kZBytes + 1023) & ~1023;
+  static constexpr int kWSZBytes = (kWBytes + kScBytes + kZBytes + 15) & ~15;
+  static constexpr int kXSlots = gemv::xb_slots(2 * MAXM);
+  static constexpr int kXBytes = XP ? kStageK * kXSlots : 0;
+  static constexpr int kGBytes = XP ? GPS * MAXM * 4 : 0;
+  static constexpr int kStageBytes = (kWSZBytes + kXBytes + kGBytes + 1023) & ~1023;
   static constexpr int kBarOff = NST * kStageBytes;
   static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier, abort flag
 };
 
-template <int BITS, int GS, int NQ, int NST, int SCB, int SW>
+template <int BITS, int GS, int NQ, int NST, int SCB, int SW, bool XP>
 __global__ void __launch_bounds__(kThreads, 2)
     gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                          const __grid_constant__ CUtensorMap tmap_z, const TmaGemvArgs a) {
-  using L = TmaLayout<BITS, GS, NST, SCB, SW>;
+  using L = TmaLayout<BITS, GS, NST, SCB, SW, 4 * NQ, XP>;
   constexpr int TC = L::TC;
   constexpr int KW = kCW / SW;
   constexpr int PER = L::PER;
@@ -151,12 +162,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // staged activations: B rows of sstride slots (swizzled), group sums gstride ints apart (odd
   // from two tokens on, so the 4 tokens a warp reads at once sit in distinct banks)
   constexpr bool SWZ = NQ > 1;   // swizzled B rows (more than 4 tokens)
-  const int sstride = SWZ ? gemv::xb_slots(2 * M) : 2 * M;
+  const int sstride = XP ? L::kXSlots : (SWZ ? gemv::xb_slots(2 * M) : 2 * M);
   const int gstride = M > 1 ? (ng_max | 1) : ng_max;
   uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
-  const int xs_bytes = (klen_max * sstride + 15) & ~15;
+  const int xs_bytes = XP ? 0 : (klen_max * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
-  const int gs_bytes = (M * gstride * 4 + 15) & ~15;
+  const int gs_bytes = XP ? 0 : (M * gstride * 4 + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
   // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16 (only
   // with cs > 1); kred: K-way partials (KW == 2), [SW * 32 lanes][NQ * 4]
@@ -192,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::tma_prefetch(&tmap_z);
       const int strip0 = blockIdx.y * SW;
       const int wrow0 = e * a.g_wrows, grow0 = e * a.g_grows;   // expert's first rows (0 when dense)
+      if (XP) pdl_wait();   // the staged activations are the previous kernel's output
       int i = 0;
       bool ok = true;
       for (; i < nst; ++i) {
@@ -204,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t st = sbase + s * L::kStageBytes;
         const uint32_t fb = bar_full + 8 * s;
         const int srow = grow0 + ((s0 + i) * kStageK) / a.gs;   // first scale/zero row of the stage
-        ptx::mbar_arrive_expect_tx(fb, L::kWBytes + L::kScBytes + L::kZBytes);
+        ptx::mbar_arrive_expect_tx(fb, L::kWBytes + L::kScBytes + L::kZBytes + L::kXBytes + L::kGBytes);
         asm volatile(
             "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
             "[%2];" ::"r"(st),
@@ -212,6 +224,11 @@ __global__ void __launch_bounds__(kThreads, 2)
             : "memory");
         ptx::tma_load_2d(st + L::kWBytes, &tmap_s, fb, blockIdx.y * TC, srow);
         ptx::tma_load_2d(st + L::kWBytes + L::kScBytes, &tmap_z, fb, blockIdx.y * (TC / PER), srow);
+        if constexpr (XP) {
+          ptx::bulk_load(st + L::kWSZBytes, a.xg + (long)(s0 + i) * L::kXBytes, L::kXBytes, fb);
+          ptx::bulk_load(st + L::kWSZBytes + L::kXBytes, a.xg + a.xg_sum_off + (long)(s0 + i) * L::kGBytes, L::kGBytes,
+                         fb);
+        }
       }
       if (nst <= NST) pdl_trigger();
       if (!ok) {
@@ -238,8 +255,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
     const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
                     a.ldx, a.x_dtype, a.x_vec, M, a.glu};
-    gemv::stage_x_i8<BITS, GS, true, SWZ>(xsrc, s0 * kStageK, klen, gstride, sstride, xb, gsum, sh_exp, sh_max, tid,
-                                     kCW * 32);
+    if constexpr (!XP)
+      gemv::stage_x_i8<BITS, GS, true, SWZ>(xsrc, s0 * kStageK, klen, gstride, sstride, xb, gsum, sh_exp, sh_max,
+                                            tid, kCW * 32);
 
     float acc[NQ][4];
 #pragma unroll
@@ -299,7 +317,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int slot = 8 * mq + gq;
             uint32_t b0 = 0u, b1 = 0u;
             if (slot < slots) {
-              const uint32_t xa = xb_base + ((step * 4 + t) * sstride + (slot ^ swz)) * 8;
+              const uint32_t xa = XP ? st + L::kWSZBytes + (((u * SPG + sp) * 4 + t) * sstride + (slot ^ swz)) * 8
+                                     : xb_base + ((step * 4 + t) * sstride + (slot ^ swz)) * 8;
               asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
             }
             mma_16832_u8s8(d[mq][0], A0[0], A0[1], A0[2], A0[3], b0, b1);
@@ -331,7 +350,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int mq = 0; mq < NQ; ++mq) {
           const int tok = 4 * mq + t;
-          const int S = tok < M ? gsum[tok * gstride + gl] : 0;
+          const int S = tok >= M ? 0
+                        : XP ? *reinterpret_cast<const int*>(stp + L::kWSZBytes + L::kXBytes + (u * MAXM + tok) * 4)
+                             : gsum[tok * gstride + gl];
           const int C[4] = {d[mq][0][0] * 256 + d[mq][0][1], d[mq][0][2] * 256 + d[mq][0][3],
                             d[mq][1][0] * 256 + d[mq][1][1], d[mq][1][2] * 256 + d[mq][1][3]};
 #pragma unroll
@@ -362,8 +383,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool writer = kway == 0;
     // non-finite activation rows give NaN (the integer staging cannot carry inf / nan)
     auto finish = [&](int tok, float v) {
-      const float mx = __uint_as_float(sh_max[tok]);
-      return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+      if constexpr (XP) {
+        const int ex = a.xe[tok];
+        return ex != gemv::kNonFinite ? v * exp2i(ex) : __int_as_float(0x7fc00000);
+      } else {
+        const float mx = __uint_as_float(sh_max[tok]);
+        return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+      }
     };
     if (cs == 1) {
 #pragma unroll
@@ -456,26 +482,31 @@ constexpr int nst_cap(int bits, int sw) { return (bits == 4 ? 4 : 3) * (kCW / sw
 constexpr int nst_half(int bits, int sw) { return nst_cap(bits, sw) / 2 > 2 ? nst_cap(bits, sw) / 2 : 2; }
 
 // Dynamic shared memory of one CTA (ring of nst = NST stages), as the kernel's prologue carves
-// it up: 1 KB of alignment slack, the ring, the barriers, the staged activations and their group sums, the split-K
-// receive buffer (cs > 1) and the K-way hand-off (128-column tiles).
-size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int M, int nstage) {
+// it up: 1 KB of alignment slack, the ring, the barriers, the staged activations and their group
+// sums (unless xp: then each stage carries its own), the split-K receive buffer (cs > 1) and the
+// K-way hand-off (128-column tiles).
+size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int M, int nstage, bool xp) {
   const int per = 32 / bits, tc = 32 * sw, gps = kStageK / kgs, rows = kStageK / per;
-  const size_t stage = ((size_t)sw * rows * 128 + (size_t)gps * tc * scb + (size_t)gps * (tc / per) * 4 + 1023) & ~(size_t)1023;
   const int nq = M <= 4 ? 1 : (M <= 8 ? 2 : 4);
+  const size_t wsz = ((size_t)sw * rows * 128 + (size_t)gps * tc * scb + (size_t)gps * (tc / per) * 4 + 15) & ~(size_t)15;
+  const size_t xpart = xp ? (size_t)kStageK * gemv::xb_slots(8 * nq) + (size_t)gps * 4 * nq * 4 : 0;
+  const size_t stage = (wsz + xpart + 1023) & ~(size_t)1023;
   const int sq = nstage / cs, nst_max = sq + (nstage % cs ? 1 : 0);
   const int ng_max = nst_max * gps;
   size_t b = 1024 + (size_t)nst * stage + 2 * nst * 8 + 16;
-  b += ((size_t)nst_max * kStageK * gemv::xb_slots(2 * M) + 15) & ~(size_t)15;
-  b += ((size_t)M * (M > 1 ? (ng_max | 1) : ng_max) * 4 + 15) & ~(size_t)15;
+  if (!xp) {
+    b += ((size_t)nst_max * kStageK * gemv::xb_slots(2 * M) + 15) & ~(size_t)15;
+    b += ((size_t)M * (M > 1 ? (ng_max | 1) : ng_max) * 4 + 15) & ~(size_t)15;
+  }
   if (cs > 1) b += (size_t)(tc + 64) * 4 * nq * 4;
   if (sw < kCW) b += (size_t)sw * 32 * nq * 4 * 4;
   return b;
 }
 
-template <int BITS, int GS, int NQ, int NST, int SCB, int SW>
+template <int BITS, int GS, int NQ, int NST, int SCB, int SW, bool XP>
 int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qzeros, const void* scales,
                cudaStream_t st) {
-  using L = TmaLayout<BITS, GS, NST, SCB, SW>;
+  using L = TmaLayout<BITS, GS, NST, SCB, SW, 4 * NQ, XP>;
   constexpr int TC = L::TC;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
@@ -499,8 +530,8 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
                  (uint64_t)(a.N / L::PER) * 4,
                  TC / L::PER, L::GPS))
     return -1;
-  auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB, SW>;
-  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, a.M, a.nstage);
+  auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB, SW, XP>;
+  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, a.M, a.nstage, XP);
   if (smem > kMaxSmem) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -532,18 +563,29 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   }
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
+  if constexpr (XP) {
+    // stage the activations once (one CTA per token row) for every CTA of the GEMV
+    const XSrc xsrc{a.x, nullptr, a.x_perm, a.ldx, a.x_dtype, a.x_vec, a.M, 0};
+    prestage_x_kernel<BITS, GS, 4 * NQ><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg), 0, a.xg_sum_off,
+                                                            const_cast<int*>(a.xe));
+    const int rc = cuda_status(cudaGetLastError(), "gptq prestage launch");
+    if (rc) return rc;
+  }
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, tw, ts, tz, a), "gptq_gemv_tma launch");
 }
 
 template <int BITS, int GS, int SW, int SCB>
 int tma_nq(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
   constexpr int CAP = nst_cap(BITS, SW), HALF = nst_half(BITS, SW);
-  if (a.M <= 4) return launch_tma<BITS, GS, 1, CAP, SCB, SW>(a, qw, qz, sc, st);
+  if (a.M <= 4) return launch_tma<BITS, GS, 1, CAP, SCB, SW, false>(a, qw, qz, sc, st);
+  if (a.xg)   // activations staged in global memory: full ring, no staging area
+    return a.M <= 8 ? launch_tma<BITS, GS, 2, CAP, SCB, SW, true>(a, qw, qz, sc, st)
+                    : launch_tma<BITS, GS, 4, CAP, SCB, SW, true>(a, qw, qz, sc, st);
   if (a.M <= 8)
-    return a.nst == CAP ? launch_tma<BITS, GS, 2, CAP, SCB, SW>(a, qw, qz, sc, st)
-                        : launch_tma<BITS, GS, 2, HALF, SCB, SW>(a, qw, qz, sc, st);
-  return a.nst == CAP ? launch_tma<BITS, GS, 4, CAP, SCB, SW>(a, qw, qz, sc, st)
-                      : launch_tma<BITS, GS, 4, HALF, SCB, SW>(a, qw, qz, sc, st);
+    return a.nst == CAP ? launch_tma<BITS, GS, 2, CAP, SCB, SW, false>(a, qw, qz, sc, st)
+                        : launch_tma<BITS, GS, 2, HALF, SCB, SW, false>(a, qw, qz, sc, st);
+  return a.nst == CAP ? launch_tma<BITS, GS, 4, CAP, SCB, SW, false>(a, qw, qz, sc, st)
+                      : launch_tma<BITS, GS, 4, HALF, SCB, SW, false>(a, qw, qz, sc, st);
 }
 
 template <int BITS, int GS>
@@ -567,16 +609,16 @@ int tma_gs(const TmaGemvArgs& a, int kgs, const uint32_t* qw, const uint32_t* qz
 // sets the time), two CTAs per SM where their shared memory allows (a shallower ring is
 // preferred to a single CTA per SM); the wider tile and the deeper ring win ties.
 void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_sm, int max_cluster, int bits,
-                  int kgs, int scb) {
+                  int kgs, int scb, bool xp) {
   int cs = 1, sw = 8, nst = nst_cap(bits, 8);
   double best = -1.0;
   const size_t per_sm = 228 * 1024;   // shared memory per SM; each CTA also reserves 1 KB
   for (int w = 8; w >= 4; w /= 2) {
     const int tiles = (N + 32 * w - 1) / (32 * w) * zdim;
     const int cap = nst_cap(bits, w), half = nst_half(bits, w);
-    for (int ns = cap; ns >= half; ns = (ns == cap && M > 4 && half < cap) ? half : 0) {
+    for (int ns = cap; ns >= half; ns = (ns == cap && M > 4 && half < cap && !xp) ? half : 0) {
       for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, M, a.nstage);
+        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, M, a.nstage, xp);
         if (sm > (size_t)kMaxSmem) continue;
         const int fit = (int)(per_sm / (sm + 1024 + 256));
         const int per = fit < ctas_per_sm ? fit : ctas_per_sm;
@@ -605,10 +647,21 @@ void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_
 }  // namespace
 
 // Returns true (and the launch status in *rc) when the TMA-fed GEMV handles this shape.
+// Bytes of global staging a dense call of M tokens needs (0 when it stages in shared memory): one
+// chunk of 8 or 16 tokens, B operand of all K plus group sums, then one exponent per token.
+size_t gemv_stage_workspace(int M, int K, int kgs) {
+  if (M <= 4 || M > 16) return 0;
+  const int maxm = M <= 8 ? 8 : 16;
+  const size_t body = (size_t)K * gemv::xb_slots(2 * maxm) + (size_t)(K / kgs) * maxm * 4;
+  return ((body + 255) & ~(size_t)255) + (size_t)maxm * 4;
+}
+
+// Dense GEMV of M <= 16 tokens. More than 4 tokens: the activations are staged once in global
+// memory (the caller's workspace when it is large enough, else the stream-ordered allocator).
 bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
-                   int* rc) {
+                   int* rc, void* workspace, size_t ws_bytes) {
   static int enabled = -1, sms = 0, ctas_per_sm = 0, max_cluster = 8;
   if (enabled < 0) {
     enabled = env_int("QL_GEMV_TMA", 1);
@@ -634,11 +687,40 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
-  choose_split(a, N, M, 1, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2);
+  static int prestage = -1;
+  if (prestage < 0) prestage = env_int("QL_GEMV_PRESTAGE", 1);
+  const size_t need = prestage ? gemv_stage_workspace(M, K, kgs) : 0;
+  void* ws = nullptr;
+  bool owned = false;
+  if (need) {
+    if (workspace && ws_bytes >= need) {
+      ws = workspace;
+    } else {
+      const int arc = cuda_status(cudaMallocAsync(&ws, need, st), "cudaMallocAsync(gemv staging)");
+      if (arc) {
+        *rc = arc;
+        return true;
+      }
+      owned = true;
+    }
+    const int maxm = M <= 8 ? 8 : 16;
+    a.xg = reinterpret_cast<const uint8_t*>(ws);
+    a.xg_sum_off = (long)K * gemv::xb_slots(2 * maxm);
+    a.xe = reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(ws) + need - (size_t)maxm * 4);
+  }
+  choose_split(a, N, M, 1, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2, need != 0);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
-  const int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);
-  if (r < 0) return false;
+  int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);
+  if (owned) {
+    const int frc = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(gemv staging)");
+    if (r == 0) r = frc;
+  }
+  if (r < 0) {
+    if (!need) return false;
+    set_error("ql_gptq_matmul: tensor-map encoding failed");   // after the staging ran
+    r = QL_ERR_CUDA;
+  }
   *rc = r;
   return true;
 }
@@ -678,7 +760,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
   a.g_wrows = K / per;
   a.g_grows = K / gs;
   a.n_experts = E;
-  choose_split(a, N, a.M, max_tiles, sms, 2, 8, bits, kgs, sc_dtype == QL_F32 ? 4 : 2);
+  choose_split(a, N, a.M, max_tiles, sms, 2, 8, bits, kgs, sc_dtype == QL_F32 ? 4 : 2, false);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
   const int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);
