@@ -110,11 +110,26 @@ def dtype_code(t):
 
 
 def ptr(t):
-    """Device address of a torch tensor, or None for None."""
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+    """Device address of a torch tensor (an int, which ctypes passes as void*), or None for None."""
+    return None if t is None else t.data_ptr()
 
 
-def stream_ptr(stream=None):
+_raw_stream = None
+
+
+def stream_ptr(stream=None, device=None):
+    """The CUDA stream to launch on: `stream`, else torch's current stream on `device` (an index
+    or torch.device; the current device when None). Read through torch's raw-stream query when it
+    has one (no Stream object per call)."""
+    global _raw_stream
+    if stream is not None:
+        return stream.cuda_stream
     import torch
-    s = stream if stream is not None else torch.cuda.current_stream()
-    return ctypes.c_void_p(s.cuda_stream)
+    if _raw_stream is None:
+        _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", False)
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None:
+        idx = torch.cuda.current_device()
+    if _raw_stream:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream

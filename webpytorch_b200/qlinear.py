@@ -78,13 +78,14 @@ def _gptq_matmul(xf, qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, *, x_per
     M = xf.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=xf.device)
-    # the tensor-core (large-M) path stages x in a workspace; take it from torch's allocator
-    ws_bytes = _ffi.load().ql_gptq_matmul_workspace(M, K) if M >= 16 else 0
+    # calls of more than 4 tokens stage x in a workspace (the tensor-core path's fp16 copy or the
+    # decode path's MMA operand); take it from torch's allocator
+    ws_bytes = _ffi.load().ql_gptq_matmul_workspace(M, K) if M > 4 else 0
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xf.device) if ws_bytes else None
-    _ffi.call("ql_gptq_matmul_ws", _ffi.ptr(xf), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(x_perm),
-              _ffi.ptr(qweight), _ffi.ptr(qzeros), _ffi.ptr(scales), _ffi.dtype_code(scales.dtype),
-              _ffi.ptr(bias), _ffi.ptr(out), _ffi.dtype_code(out.dtype), out.stride(0), M, K, N, gs, bits,
-              float(zoff), _ffi.ptr(ws), ws_bytes, _ffi.stream_ptr(stream))
+    _ffi.call("ql_gptq_matmul_ws", xf.data_ptr(), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(x_perm),
+              qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), _ffi.dtype_code(scales.dtype),
+              _ffi.ptr(bias), out.data_ptr(), _ffi.dtype_code(out.dtype), out.stride(0), M, K, N, gs, bits,
+              float(zoff), _ffi.ptr(ws), ws_bytes, _ffi.stream_ptr(stream, xf.device))
     return out
 
 
