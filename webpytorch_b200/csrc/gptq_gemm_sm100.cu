@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int wrow0 = tr.e * (a.K / PER), grow0 = tr.e * G;
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
-          if (!ptx::mbar_wait(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) {
+          if (!ptx::mbar_wait_sleep(slab_free(s), ((it / NS) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -394,12 +394,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++tcount) {
         const int b = ND == 2 ? (tcount & 1) : 0;
         const int use = ND == 2 ? (tcount >> 1) : tcount;   // earlier uses of this buffer
-        if (!ptx::mbar_wait(d_empty(b), (use & 1) ^ 1, abort_flag)) break;
+        if (!ptx::mbar_wait_sleep(d_empty(b), (use & 1) ^ 1, abort_flag)) break;
         ptx::tc_fence_after();
         for (int kb = 0; kb < nslab; ++kb, ++it) {
           const int s = it % NS;
           const uint32_t par = (it / NS) & 1;
-          if (!ptx::mbar_wait(full(s), par, abort_flag) || !ptx::mbar_wait(a_full(s), par, abort_flag)) {
+          if (!ptx::mbar_wait_sleep(full(s), par, abort_flag) || !ptx::mbar_wait_sleep(a_full(s), par, abort_flag)) {
             ok = false;
             break;
           }
@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = 0; u < DQP; ++u) {
           if (u < cnt) {
             const int s = (it + u) % NS;
-            if (!ptx::mbar_wait(full(s), ((it + u) / NS) & 1, abort_flag)) goto done;
+            if (!ptx::mbar_wait_sleep(full(s), ((it + u) / NS) & 1, abort_flag)) goto done;
             const unsigned char* stp = smem + s * L::kStageBytes;
             const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
             uint32_t w[HROWS];
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tok = tr.row0 + c * 32 + lane;
         rexp[c] = tok < tr.row_end ? a.row_exp[tok] : 0;
       }
-      if (!ptx::mbar_wait(d_full(b), use & 1, abort_flag)) goto done;
+      if (!ptx::mbar_wait_sleep(d_full(b), use & 1, abort_flag)) goto done;
       ptx::tc_fence_after();
 #pragma unroll
       for (int c = 0; c < BT / 32; ++c) {

@@ -37,18 +37,18 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// The suspend-time hint lets a waiting thread sleep in hardware until the phase completes (up
-// to the hint, in ns) instead of re-polling, so idle roles do not take issue slots from the
-// warps that compute.
-constexpr uint32_t kSuspendHintNs = 200000;
+// try_wait without a suspend-time hint: the thread may still sleep in hardware for a
+// system-defined window while the phase is pending. Measured on B200, a try_wait that carries a
+// hint costs hundreds of cycles even when the phase has already completed; in a loop that waits
+// once per K-slab before issuing its MMAs that halved the tensor-core rate.
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -60,6 +60,37 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// The same with a suspend-time hint: a waiting thread sleeps in hardware until the phase
+// completes (up to the hint, in ns) instead of re-polling, so waiting roles leave the issue slots
+// to the warps that compute. Each hinted try pays a fixed cost even on a completed phase (about
+// half the tensor-core rate in a loop that only waits and issues MMAs), yet in the dequant-bound
+// prefill GEMM every wait measured fastest hinted from the first try (6 % over an unhinted first
+// try); the decode GEMVs, whose consumers wait once per stage, measured fastest unhinted (4 %).
+constexpr uint32_t kSuspendHintNs = 200000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if (mbar_try_wait_sleep(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > kWaitLimitNs) {
       *abort = 1;
