@@ -245,11 +245,14 @@ __device__ __forceinline__ TileRows tile_rows(const GemmArgs& a, int tt, int BT)
   return r;
 }
 
-template <int BITS, int NS, int BT>
+// A stage covers SK values of K (64 or 128): SK / 64 activation boxes of [BT rows][64 K] fp16
+// (128-byte swizzled rows, one box after the other), the packed weights of those K, one or two
+// scale / zero rows.
+template <int BITS, int NS, int BT, int SK = kSlabK>
 struct SmemLayout {
   static constexpr int PER = 32 / BITS;
-  static constexpr int ROWS = kSlabK / PER;                // packed rows per slab (8 int4 / 16 int8)
-  static constexpr int kXBytes = BT * kSlabK * 2;          // activation tile, 128-byte swizzled rows
+  static constexpr int ROWS = SK / PER;                    // packed rows per stage (8 / 16 int4)
+  static constexpr int kXBytes = BT * SK * 2;              // activation boxes, 128-byte swizzled rows
   static constexpr int kWOff = kXBytes;
   static constexpr int kWBytes = ROWS * kTileN * 4;        // packed weights [ROWS][128]
   static constexpr int kSOff = kWOff + kWBytes;
@@ -290,16 +293,19 @@ __device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, ui
 // epilogue drains one while the next tile's MMAs fill the other): 128 for dense GEMMs, 32 / 64 for
 // MoE experts with few rows each (less padding, same dequant work per tile). BT = 256 halves the
 // dequant work per MMA flop with one accumulator (the next tile waits for the drain).
-template <int BITS, int NS, int BT>
+// SK = K per pipeline stage (64, or 128 for dense GEMMs with whole 128-value groups): a larger
+// stage halves every role's per-stage handshakes (barrier waits, TMEM-store waits, commits).
+template <int BITS, int NS, int BT, int SK>
 __global__ void __launch_bounds__(kThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const GemmArgs a) {
-  using L = SmemLayout<BITS, NS, BT>;
+  using L = SmemLayout<BITS, NS, BT, SK>;
   constexpr int PER = L::PER;
   constexpr int ROWS = L::ROWS;
   constexpr int HROWS = ROWS / 2;               // packed rows per dequant half
-  constexpr int TCOLS_A = kSlabK / 2;           // TMEM columns per A stage (fp16 pairs)
+  constexpr int TCOLS_A = SK / 2;               // TMEM columns per A stage (fp16 pairs)
+  static_assert(SK == kSlabK || SK == 2 * kSlabK, "stage K");
   constexpr int ND = BT <= 128 ? 2 : 1;         // accumulator buffers
   constexpr int DCOL = BT <= 128 ? 128 : BT;    // TMEM columns between accumulator buffers
   constexpr int A_COL = ND * DCOL;              // A stages start after the accumulators
@@ -352,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  const int nslab = a.K / kSlabK;
+  const int nslab = a.K / SK;
   const int ntiles = a.n_wtiles * (a.tiles ? *a.n_tiles : a.n_ttiles);
   const int G = a.K / a.gs;
   const int sc_bytes = a.sc_dtype == QL_F32 ? 4 : 2;
@@ -374,9 +380,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t st = sbase + s * L::kStageBytes;
-          const int g0 = (kb * kSlabK) / a.gs;
+          const int g0 = (kb * SK) / a.gs;
           ptx::mbar_arrive_expect_tx(full(s), stage_tx);
-          ptx::tma_load_2d(st, &tmap_x, full(s), kb * kSlabK, tr.row0);
+#pragma unroll
+          for (int xb = 0; xb < SK / kSlabK; ++xb)
+            ptx::tma_load_2d(st + xb * BT * 128, &tmap_x, full(s), kb * SK + xb * kSlabK, tr.row0);
           ptx::tma_load_2d(st + L::kWOff, &tmap_w, full(s), wt * kTileN, wrow0 + kb * ROWS);
           ptx::tma_load_2d(st + L::kSOff, &tmap_s, full(s), wt * kTileN, grow0 + g0);
           ptx::tma_load_2d(st + L::kZOff, &tmap_z, full(s), wt * (kTileN / PER), grow0 + g0);
@@ -406,9 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
           const uint32_t xs = sbase + s * L::kStageBytes;
 #pragma unroll
-          for (int j = 0; j < kSlabK / 16; ++j) {
-            ptx::mma_f16_ts(tmem + b * DCOL, tmem + A_COL + s * TCOLS_A + j * 8, ptx::smem_desc_sw128(xs + j * 32),
-                            IDESC, (kb | j) != 0);
+          for (int j = 0; j < SK / 16; ++j) {
+            // K step j: activation box j / 4, 32-byte column (j % 4) of its swizzled rows
+            ptx::mma_f16_ts(tmem + b * DCOL, tmem + A_COL + s * TCOLS_A + j * 8,
+                            ptx::smem_desc_sw128(xs + (j >> 2) * BT * 128 + (j & 3) * 32), IDESC, (kb | j) != 0);
           }
           ptx::mma_commit(slab_free(s));  // frees the stage's shared memory and its TMEM A columns
         }
@@ -430,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       for (int kb = 0; kb < nslab;) {
         const int cnt = nslab - kb < DQP ? nslab - kb : DQP;
-        uint32_t v[DQP][16];
+        uint32_t v[DQP][TCOLS_A / 2];   // this half's TMEM columns: 16 (SK = 64) or 32 (SK = 128)
 #pragma unroll
         for (int u = 0; u < DQP; ++u) {
           if (u < cnt) {
@@ -458,8 +467,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
 #pragma unroll
-        for (int u = 0; u < DQP; ++u)
-          if (u < cnt) ptx::tmem_st16(lane_addr + A_COL + ((it + u) % NS) * TCOLS_A + h * (TCOLS_A / 2), v[u]);
+        for (int u = 0; u < DQP; ++u) {
+          if (u < cnt) {
+            const uint32_t ta = lane_addr + A_COL + ((it + u) % NS) * TCOLS_A + h * (TCOLS_A / 2);
+            if constexpr (TCOLS_A / 2 == 16) ptx::tmem_st16(ta, v[u]);
+            else ptx::tmem_st32(ta, v[u]);
+          }
+        }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
@@ -549,11 +563,12 @@ bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const voi
 }
 
 // n_experts: stacked weight matrices (grouped mode), 1 otherwise.
-template <int BITS, int BT>
+template <int BITS, int BT, int SK = kSlabK>
 int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
-  constexpr int NS = BT <= 128 ? (BITS == 4 ? 8 : 7) : 4;
+  // ring depth: the TMEM A stages (NS * SK / 2 columns) fit beside the accumulators
+  constexpr int NS = SK == kSlabK ? (BT <= 128 ? (BITS == 4 ? 8 : 7) : 4) : 4;
   constexpr int PER = 32 / BITS;
-  using L = SmemLayout<BITS, NS, BT>;
+  using L = SmemLayout<BITS, NS, BT, SK>;
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled is unavailable");
@@ -576,7 +591,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed");
     return QL_ERR_CUDA;
   }
-  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT>;
+  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT, SK>;
   const int smem = L::kBytes;
   static int configured_dev = -1;
   static int sms = 0;
@@ -649,8 +664,14 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
       a.n_ttiles = (M + 255) / 256;
       rc = bits == 4 ? launch_gemm<4, 256>(a, x16, 1, st) : launch_gemm<8, 256>(a, x16, 1, st);
     } else {
+      // 128-value stages when the groups hold whole stages (one scale row per stage)
+      static int sk128 = -1;
+      if (sk128 < 0) sk128 = env_int("QL_GEMM_SK128", 1);
       a.n_ttiles = (M + 127) / 128;
-      rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
+      if (sk128 && K % 128 == 0 && gs % 128 == 0)
+        rc = bits == 4 ? launch_gemm<4, 128, 128>(a, x16, 1, st) : launch_gemm<8, 128, 128>(a, x16, 1, st);
+      else
+        rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
     }
   }
   if (owned) {
