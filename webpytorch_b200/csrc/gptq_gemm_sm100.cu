@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int ROWS = L::ROWS;
   constexpr int HROWS = ROWS / 2;               // packed rows per dequant half
   constexpr int TCOLS_A = SK / 2;               // TMEM columns per A stage (fp16 pairs)
-  static_assert(SK == kSlabK || SK == 2 * kSlabK, "stage K");
+  static_assert(SK == kSlabK || SK == 2 * kSlabK || SK == 4 * kSlabK, "stage K");
   constexpr int ND = BT <= 128 ? 2 : 1;         // accumulator buffers
   constexpr int DCOL = BT <= 128 ? 128 : BT;    // TMEM columns between accumulator buffers
   constexpr int A_COL = ND * DCOL;              // A stages start after the accumulators
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       for (int kb = 0; kb < nslab;) {
         const int cnt = nslab - kb < DQP ? nslab - kb : DQP;
-        uint32_t v[DQP][TCOLS_A / 2];   // this half's TMEM columns: 16 (SK = 64) or 32 (SK = 128)
+        uint32_t v[DQP][TCOLS_A / 2];   // this half's TMEM columns: SK / 4
 #pragma unroll
         for (int u = 0; u < DQP; ++u) {
           if (u < cnt) {
@@ -470,8 +470,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = 0; u < DQP; ++u) {
           if (u < cnt) {
             const uint32_t ta = lane_addr + A_COL + ((it + u) % NS) * TCOLS_A + h * (TCOLS_A / 2);
-            if constexpr (TCOLS_A / 2 == 16) ptx::tmem_st16(ta, v[u]);
-            else ptx::tmem_st32(ta, v[u]);
+            if constexpr (TCOLS_A / 2 == 16) {
+              ptx::tmem_st16(ta, v[u]);
+            } else {
+#pragma unroll
+              for (int c = 0; c < TCOLS_A / 2; c += 32)
+                ptx::tmem_st32(ta + c, *reinterpret_cast<const uint32_t(*)[32]>(&v[u][c]));
+            }
           }
         }
         ptx::tmem_wait_st();
@@ -566,7 +571,7 @@ bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const voi
 template <int BITS, int BT, int SK = kSlabK>
 int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
   // ring depth: the TMEM A stages (NS * SK / 2 columns) fit beside the accumulators
-  constexpr int NS = SK == kSlabK ? (BT <= 128 ? (BITS == 4 ? 8 : 7) : 4) : 4;
+  constexpr int NS = SK == kSlabK ? (BT <= 128 ? (BITS == 4 ? 8 : 7) : 4) : (SK == 2 * kSlabK ? 4 : 2);
   constexpr int PER = 32 / BITS;
   using L = SmemLayout<BITS, NS, BT, SK>;
   EncodeTiledFn enc = encode_fn();
@@ -665,10 +670,13 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
       rc = bits == 4 ? launch_gemm<4, 256>(a, x16, 1, st) : launch_gemm<8, 256>(a, x16, 1, st);
     } else {
       // 128-value stages when the groups hold whole stages (one scale row per stage)
-      static int sk128 = -1;
-      if (sk128 < 0) sk128 = env_int("QL_GEMM_SK128", 1);
+      static int sk = -1;
+      if (sk < 0) sk = env_int("QL_GEMM_SK", 128);
       a.n_ttiles = (M + 127) / 128;
-      if (sk128 && K % 128 == 0 && gs % 128 == 0)
+      if (sk == 256 && K % 256 == 0 && (gs == 128 || gs % 256 == 0)) {
+        a.gb = gs == 128 ? 2 : 1;   // scale / zero rows per 256-value stage
+        rc = bits == 4 ? launch_gemm<4, 128, 256>(a, x16, 1, st) : launch_gemm<8, 128, 256>(a, x16, 1, st);
+      } else if (sk >= 128 && K % 128 == 0 && gs % 128 == 0)
         rc = bits == 4 ? launch_gemm<4, 128, 128>(a, x16, 1, st) : launch_gemm<8, 128, 128>(a, x16, 1, st);
       else
         rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
@@ -719,6 +727,13 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
   a.tiles = tiles; a.n_tiles = n_tiles; a.offsets = offsets;
   a.qw_estride = qw_estride; a.qz_estride = qz_estride; a.sc_estride = sc_estride;
   a.gb = gs == 32 ? 2 : 1;
+  if (K % 128 == 0 && gs % 128 == 0) {   // 128-value stages (one scale row each)
+    switch (tile_rows_n) {
+      case 32: return bits == 4 ? launch_gemm<4, 32, 128>(a, x16, n_experts, st) : launch_gemm<8, 32, 128>(a, x16, n_experts, st);
+      case 64: return bits == 4 ? launch_gemm<4, 64, 128>(a, x16, n_experts, st) : launch_gemm<8, 64, 128>(a, x16, n_experts, st);
+      default: return bits == 4 ? launch_gemm<4, 128, 128>(a, x16, n_experts, st) : launch_gemm<8, 128, 128>(a, x16, n_experts, st);
+    }
+  }
   switch (tile_rows_n) {
     case 32: return bits == 4 ? launch_gemm<4, 32>(a, x16, n_experts, st) : launch_gemm<8, 32>(a, x16, n_experts, st);
     case 64: return bits == 4 ? launch_gemm<4, 64>(a, x16, n_experts, st) : launch_gemm<8, 64>(a, x16, n_experts, st);
