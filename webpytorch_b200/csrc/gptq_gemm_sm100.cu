@@ -295,7 +295,7 @@ __device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, ui
 // dequant work per MMA flop with one accumulator (the next tile waits for the drain).
 // SK = K per pipeline stage (64, or 128 for dense GEMMs with whole 128-value groups): a larger
 // stage halves every role's per-stage handshakes (barrier waits, TMEM-store waits, commits).
-template <int BITS, int NS, int BT, int SK>
+template <int BITS, int NS, int BT, int SK, bool DQ_ALT_T>
 __global__ void __launch_bounds__(kThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int ND = BT <= 128 ? 2 : 1;         // accumulator buffers
   constexpr int DCOL = BT <= 128 ? 128 : BT;    // TMEM columns between accumulator buffers
   constexpr int A_COL = ND * DCOL;              // A stages start after the accumulators
-  constexpr int DQP = 1;                        // slabs a dequant warp converts per TMEM-store wait (2 measured slower)
+  constexpr bool DQ_ALT = DQ_ALT_T;               // dequant groups on alternate stages
   constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, BT);
   constexpr uint32_t MASK = (1u << BITS) - 1u;
   static_assert(A_COL + NS * TCOLS_A <= 512, "TMEM budget");
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       ptx::mbar_init(full(s), 1);
-      ptx::mbar_init(a_full(s), kDequantWarps);
+      ptx::mbar_init(a_full(s), DQ_ALT ? kDequantWarps / 2 : kDequantWarps);
       ptx::mbar_init(slab_free(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -428,65 +428,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_wait_drain(fin_bar, 0);
     }
   } else if (warp >= kDequantWarp0 && warp < kDequantWarp0 + kDequantWarps) {
-    // ---------------- dequant: lane = TMEM lane = output column; half h of each slab's K
-    const int q = warp & 3, h = (warp - kDequantWarp0) >> 2;
+    // ---------------- dequant: lane = TMEM lane = output column. With DQ_ALT the two groups of
+    // four warps take alternate stages and a warp converts both halves of its stage's K (one
+    // ring wait and one TMEM-store wait per twice the work); otherwise warp group h converts
+    // half h of every stage.
+    const int q = warp & 3, grp = (warp - kDequantWarp0) >> 2;
     const int lrow = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    const int gi = a.gb == 2 ? h : 0;   // scale/zero row of this half inside the slab
-    // DQP slabs per step: both TMEM stores in flight before one wait, so the store latency is
-    // paid once per DQP slabs
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      for (int kb = 0; kb < nslab;) {
-        const int cnt = nslab - kb < DQP ? nslab - kb : DQP;
-        uint32_t v[DQP][TCOLS_A / 2];   // this half's TMEM columns: SK / 4
+      for (int kb = 0; kb < nslab; ++kb, ++it) {
+        if (DQ_ALT && (it & 1) != grp) continue;
+        const int s = it % NS;
+        if (!ptx::mbar_wait_sleep(full(s), (it / NS) & 1, abort_flag)) goto done;
+        const unsigned char* stp = smem + s * L::kStageBytes;
+        const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
 #pragma unroll
-        for (int u = 0; u < DQP; ++u) {
-          if (u < cnt) {
-            const int s = (it + u) % NS;
-            if (!ptx::mbar_wait_sleep(full(s), ((it + u) / NS) & 1, abort_flag)) goto done;
-            const unsigned char* stp = smem + s * L::kStageBytes;
-            const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
-            uint32_t w[HROWS];
+        for (int hh = 0; hh < (DQ_ALT ? 2 : 1); ++hh) {
+          const int h = DQ_ALT ? hh : grp;
+          const int gi = a.gb == 2 ? h : 0;   // scale/zero row of this half inside the stage
+          uint32_t w[HROWS];
 #pragma unroll
-            for (int r = 0; r < HROWS; ++r) w[r] = wsm[(h * HROWS + r) * kTileN + lrow];
-            const float scv = load_as_float(stp + L::kSOff, a.sc_dtype, gi * kTileN + lrow);
-            const uint32_t zw = reinterpret_cast<const uint32_t*>(stp + L::kZOff)[gi * (kTileN / PER) + lrow / PER];
-            const float zf = (float)((zw >> (BITS * (lrow % PER))) & MASK) + a.zoff;
-            const uint32_t zlo = h2_as_u32(__float2half2_rn(1024.f + zf));
-            const uint32_t zhi = h2_as_u32(__float2half2_rn(-(64.f + zf)));
-            const __half2 s2 = __float2half2_rn(scv);
+          for (int r = 0; r < HROWS; ++r) w[r] = wsm[(h * HROWS + r) * kTileN + lrow];
+          const float scv = load_as_float(stp + L::kSOff, a.sc_dtype, gi * kTileN + lrow);
+          const uint32_t zw = reinterpret_cast<const uint32_t*>(stp + L::kZOff)[gi * (kTileN / PER) + lrow / PER];
+          const float zf = (float)((zw >> (BITS * (lrow % PER))) & MASK) + a.zoff;
+          const uint32_t zlo = h2_as_u32(__float2half2_rn(1024.f + zf));
+          const uint32_t zhi = h2_as_u32(__float2half2_rn(-(64.f + zf)));
+          const __half2 s2 = __float2half2_rn(scv);
+          uint32_t v[TCOLS_A / 2];   // this half's TMEM columns: SK / 4
 #pragma unroll
-            for (int r = 0; r < HROWS; ++r) {
-              if constexpr (BITS == 4) {
-                dq_int4(w[r], zlo, zhi, s2, &v[u][r * 4]);
-              } else {
-                dq_int8(w[r], zlo, s2, &v[u][r * 2]);
-              }
+          for (int r = 0; r < HROWS; ++r) {
+            if constexpr (BITS == 4) {
+              dq_int4(w[r], zlo, zhi, s2, &v[r * 4]);
+            } else {
+              dq_int8(w[r], zlo, s2, &v[r * 2]);
             }
           }
-        }
+          const uint32_t ta = lane_addr + A_COL + s * TCOLS_A + h * (TCOLS_A / 2);
+          if constexpr (TCOLS_A / 2 == 16) {
+            ptx::tmem_st16(ta, v);
+          } else {
 #pragma unroll
-        for (int u = 0; u < DQP; ++u) {
-          if (u < cnt) {
-            const uint32_t ta = lane_addr + A_COL + ((it + u) % NS) * TCOLS_A + h * (TCOLS_A / 2);
-            if constexpr (TCOLS_A / 2 == 16) {
-              ptx::tmem_st16(ta, v[u]);
-            } else {
-#pragma unroll
-              for (int c = 0; c < TCOLS_A / 2; c += 32)
-                ptx::tmem_st32(ta + c, *reinterpret_cast<const uint32_t(*)[32]>(&v[u][c]));
-            }
+            for (int c = 0; c < TCOLS_A / 2; c += 32)
+              ptx::tmem_st32(ta + c, *reinterpret_cast<const uint32_t(*)[32]>(&v[c]));
           }
         }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          for (int u = 0; u < cnt; ++u) ptx::mbar_arrive(a_full((it + u) % NS));
-        }
-        kb += cnt;
-        it += cnt;
+        if (lane == 0) ptx::mbar_arrive(a_full(s));
       }
     }
   } else if (warp >= kEpilogueWarp0) {
@@ -568,7 +559,7 @@ bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const voi
 }
 
 // n_experts: stacked weight matrices (grouped mode), 1 otherwise.
-template <int BITS, int BT, int SK = kSlabK>
+template <int BITS, int BT, int SK = kSlabK, bool DQ_ALT = false>
 int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
   // ring depth: the TMEM A stages (NS * SK / 2 columns) fit beside the accumulators
   constexpr int NS = SK == kSlabK ? (BT <= 128 ? (BITS == 4 ? 8 : 7) : 4) : (SK == 2 * kSlabK ? 4 : 2);
@@ -596,7 +587,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed");
     return QL_ERR_CUDA;
   }
-  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT, SK>;
+  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT, SK, DQ_ALT>;
   const int smem = L::kBytes;
   static int configured_dev = -1;
   static int sms = 0;
@@ -676,8 +667,14 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
       if (sk == 256 && K % 256 == 0 && (gs == 128 || gs % 256 == 0)) {
         a.gb = gs == 128 ? 2 : 1;   // scale / zero rows per 256-value stage
         rc = bits == 4 ? launch_gemm<4, 128, 256>(a, x16, 1, st) : launch_gemm<8, 128, 256>(a, x16, 1, st);
-      } else if (sk >= 128 && K % 128 == 0 && gs % 128 == 0)
-        rc = bits == 4 ? launch_gemm<4, 128, 128>(a, x16, 1, st) : launch_gemm<8, 128, 128>(a, x16, 1, st);
+      } else if (sk >= 128 && K % 128 == 0 && gs % 128 == 0) {
+        static int alt = -1;
+        if (alt < 0) alt = env_int("QL_GEMM_DQ_ALT", 1);
+        if (alt)
+          rc = bits == 4 ? launch_gemm<4, 128, 128, true>(a, x16, 1, st) : launch_gemm<8, 128, 128, true>(a, x16, 1, st);
+        else
+          rc = bits == 4 ? launch_gemm<4, 128, 128>(a, x16, 1, st) : launch_gemm<8, 128, 128>(a, x16, 1, st);
+      }
       else
         rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
     }
