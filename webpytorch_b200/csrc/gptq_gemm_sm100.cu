@@ -728,7 +728,9 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
     switch (tile_rows_n) {
       case 32: return bits == 4 ? launch_gemm<4, 32, 128>(a, x16, n_experts, st) : launch_gemm<8, 32, 128>(a, x16, n_experts, st);
       case 64: return bits == 4 ? launch_gemm<4, 64, 128>(a, x16, n_experts, st) : launch_gemm<8, 64, 128>(a, x16, n_experts, st);
-      default: return bits == 4 ? launch_gemm<4, 128, 128>(a, x16, n_experts, st) : launch_gemm<8, 128, 128>(a, x16, n_experts, st);
+      default:
+        return bits == 4 ? launch_gemm<4, 128, 128, true>(a, x16, n_experts, st)
+                         : launch_gemm<8, 128, 128, true>(a, x16, n_experts, st);
     }
   }
   switch (tile_rows_n) {
