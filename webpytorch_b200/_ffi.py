@@ -36,6 +36,9 @@ SIGNATURES = {
     "ql_gptq_matmul_noalloc_max_scratch": (ctypes.c_size_t, []),
     "ql_q4k_dequant": (_c_int, [_vp, _vp, _c_int, _c_int, _vp]),
     "ql_q4k_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp]),
+    "ql_q4k_matmul_workspace": (ctypes.c_size_t, [_c_int, _c_int]),
+    "ql_q4k_matmul_ws": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp,
+                                  ctypes.c_size_t, _vp]),
     "ql_moe_route": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _vp, _vp, _c_int, _vp, _vp, _vp]),
     "ql_moe_group": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int, _vp, _vp,
@@ -78,7 +81,7 @@ def load(build_if_missing=True):
     global _lib
     if _lib is not None:
         return _lib
-    path = os.environ.get("QL_LIBRARY", _build.LIB)   # a library built elsewhere (same ABI)
+    path = _build.LIB
     if not os.path.exists(path):
         if not build_if_missing:
             raise RuntimeError("libqlinear.so is not built (run webpytorch_b200._build.build())")
@@ -92,11 +95,21 @@ def load(build_if_missing=True):
     return lib
 
 
+_fns = {}
+
+
+def fn(name):
+    """The bound ctypes function `name` (looked up once)."""
+    f = _fns.get(name)
+    if f is None:
+        f = _fns[name] = getattr(load(), name)
+    return f
+
+
 def call(name, *args):
-    lib = load()
-    rc = getattr(lib, name)(*args)
+    rc = (_fns.get(name) or fn(name))(*args)
     if rc != 0:
-        msg = lib.ql_last_error()
+        msg = _lib.ql_last_error()
         raise QLError(name, rc, msg.decode(errors="replace") if msg else "")
     return rc
 

@@ -188,230 +188,212 @@ __device__ void stage_x(const Args& a, int kbase, int klen, int gstride, __half*
   sync();
 }
 
-// Layout of the staged B operand: row (step, t) holds sstride slots (uint2 each). With the
-// swizzle (SWZ, kernels of more than 4 tokens) slot s of row t is stored at s ^ xb_swz(sstride,
-// t) and rows are rounded up to 8 slots: a warp's 64-bit loads of one step read rows t = 0..3,
-// 4 slots each per half-warp, and the swizzle places the 4 rows 8 banks apart. Without it
-// (up to 4 tokens) rows are 2M slots, unpadded.
-__host__ __device__ constexpr int xb_slots(int slots) { return slots <= 4 ? slots : (slots + 7) & ~7; }
-__host__ __device__ __forceinline__ int xb_swz(int sstride, int t) {
-  return sstride <= 4 ? 0 : (sstride % 16 == 0 ? 4 * t : 4 * (t >> 1));
+// ---------------------------------------------------------------------------------------
+// Integer staging of activations for the integer-MMA GEMVs (u8 weights x s8 activation bytes)
+// ---------------------------------------------------------------------------------------
+// Every exponent group of EG consecutive values of one token (the quantisation group, or the
+// Q4_K super-block) gets its own power of two: e such that max|x| * 2^-e lies in [2^21, 2^22),
+// and each value becomes the integer v = rint(x * 2^-e), |v| <= 2^22 (23 bits: an element 1000x
+// below its group's maximum still keeps 13 significant bits). v is split into three signed
+// bytes, v = 2^16 b2 + 2^8 b1 + b0, which take MMA columns 4u, 4u + 1 and 4u + 3 of the token
+// (u = its place in the n8 tile); column 4u + 2 is zero. With v1 = 2^8 b2 + b1 (|v1| <= 2^14)
+// the MMA lane that owns the column pair (b2, b1) forms the exact int32 dot product with v1 as
+// 256 D[4u] + D[4u + 1], and the lane that owns (0, b0) the one with b0 the same way; both
+// lanes fold their group into fp32 with the factor 2^e (times 2^8 for the v1 lane, applied once
+// at the end), and the two lanes' sums are added when the kernel finishes.
+//
+// B operand layout: the MMA n8 tile holds two tokens (columns 4u .. 4u + 3 for token u of the
+// tile); in memory only the three used slots are stored, slot 3m + P (P = 0, 1, 2 for b2, b1, b0)
+// of row (step, t), rows xb3_slots(M) slots apart.
+// Slots per B row for m tokens: 3m rounded up to 4 (mod 8), which makes consecutive rows start 8
+// or 24 banks apart, so the 8-byte loads of one half-warp (one token's three slots, four rows)
+// are conflict-free.
+__host__ __device__ constexpr int xb3_slots(int m) { return ((3 * m + 3) & ~7) + 4; }
+
+// |bits| of the largest |x| of a chunk, compared as integers: NaN patterns sort above inf.
+__device__ __forceinline__ uint32_t abs_bits_max(const float (&v)[8]) {
+  uint32_t mb = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mb = max(mb, __float_as_uint(v[j]) & 0x7fffffffu);
+  return mb;
 }
 
-// Stage one 8-value chunk (chunk kc of a token's slice, scaled by s) of token m into the B
-// operand layout described below; returns the chunk's sum of staged integers.
-template <int BITS, bool SWZ>
-__device__ __forceinline__ int put_chunk_i8(const float (&v)[8], float s, int m, int kc, int sstride, uint2* xb) {
-  uint32_t hi[2] = {0u, 0u}, lo[2] = {0u, 0u};
-  int sum = 0;
+// Exponent of a group whose largest |x| has bit pattern mb (finite): max|x| * 2^-e < 2^22,
+// clamped below so that 2^-e stays a normal float (groups of values below 2^-105 keep fewer bits).
+__device__ __forceinline__ int stage_exponent_i23(uint32_t mb) {
+  if (mb == 0u) return 0;
+  const int e = (int)(mb >> 23) - 127 - 21;
+  return e < -126 ? -126 : e;
+}
+
+// Split 8 values (scaled by s) into the three byte planes, packed in MMA register order (BITS 4:
+// even K offsets -> register 0, odd -> register 1, byte j / 2; BITS 8: values 0-3 -> register 0,
+// 4-7 -> register 1, byte j % 4), and the chunk's sums of v1 and b0.
+template <int BITS>
+__device__ __forceinline__ void split3(const float (&v)[8], float s, uint32_t (&pl)[3][2], int& s1, int& s0) {
+#pragma unroll
+  for (int P = 0; P < 3; ++P) pl[P][0] = pl[P][1] = 0u;
+  s1 = s0 = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int q = __float2int_rn(v[j] * s);
-    const int l = (int)(int8_t)(q & 0xff);
-    const int h = (q - l) >> 8;
-    sum += q;
-    // int4: even offsets -> register 0, odd -> register 1; int8: first row -> 0, second -> 1
+    const int b0 = (q << 24) >> 24;          // signed low byte
+    const int q1 = (q - b0) >> 8;            // exact
+    const int b1 = (q1 << 24) >> 24;
+    const int b2 = (q1 - b1) >> 8;
+    s1 += q1;
+    s0 += b0;
     const int reg = BITS == 4 ? (j & 1) : (j >> 2);
-    const int byte = BITS == 4 ? (j >> 1) : (j & 3);
-    hi[reg] |= (uint32_t)(h & 0xff) << (8 * byte);
-    lo[reg] |= (uint32_t)(l & 0xff) << (8 * byte);
+    const int sh = 8 * (BITS == 4 ? (j >> 1) : (j & 3));
+    pl[0][reg] |= (uint32_t)(b2 & 0xff) << sh;
+    pl[1][reg] |= (uint32_t)(b1 & 0xff) << sh;
+    pl[2][reg] |= (uint32_t)(b0 & 0xff) << sh;
   }
-  if constexpr (BITS == 4) {
-    const int s4 = kc >> 2, t = kc & 3;
-    uint2* dst = xb + (s4 * 4 + t) * sstride + (SWZ ? (2 * m) ^ xb_swz(sstride, t) : 2 * m);
-    dst[0] = make_uint2(hi[0], hi[1]);
-    dst[1] = make_uint2(lo[0], lo[1]);
-  } else {
-    const int r0 = 2 * kc;                // rows r0, r0 + 1 of the same half of a step
-    const int s8 = r0 >> 3, j = r0 & 7;
-    const int half = j >> 2, t0 = j & 3;
-    const int c0 = SWZ ? (2 * m) ^ xb_swz(sstride, t0) : 2 * m;
-    const int c1 = SWZ ? (2 * m) ^ xb_swz(sstride, t0 + 1) : 2 * m;
-    uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * sstride + c0) + half;
-    uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * sstride + c1) + half;
-    d0[0] = hi[0];
-    d0[2] = lo[0];
-    d1[0] = hi[1];
-    d1[2] = lo[1];
-  }
-  return sum;
 }
 
-// Stage x[:, kbase : kbase + klen] for M <= 16 tokens as the B operand of the integer MMA
-// (mma.m16n8k32, A = u8 weights, B = s8 activations):
-//   * each token row is scaled by an exact power of two, v = rint(x * 2^-e) with |v| <= 2^14
-//     (sh_exp[m] = e), and split into two signed bytes v = 256 * hi + lo, which become two
-//     MMA columns ("slots" 2m and 2m + 1) so that one MMA yields both partial dot products;
-//   * the MMA K order follows the weight unpack. An int4 packed row r (K = 8r .. 8r+7) is
-//     unpacked into bytes of even offsets (MMA k 4t + i <- K 8r + 2i) and odd offsets (MMA k
-//     16 + 4t + i <- K 8r + 2i + 1), lane t of a 32-K step taking row 4s + t. An int8 packed row
-//     (K = 4r .. 4r+3) is a register as it is: rows 8s + t and 8s + 4 + t feed MMA k 4t + i and
-//     16 + 4t + i;
-//   * xb[(s * 4 + t) * sstride + slot'] holds lane t's two B registers of step s for that slot
-//     (slot' = slot ^ xb_swz(sstride, t) and sstride = xb_slots(2M) with SWZ, else slot and 2M);
-//   * gsum[m * gstride + g] = sum of v over group g (exact integers), for the zero point.
-// sh_max must be zero and visible before the call; sh_exp is valid after it returns.
-template <int BITS, int GS, bool NAMED, bool SWZ, class Args>
-__device__ void stage_x_i8(const Args& a, int kbase, int klen, int gstride, int sstride, uint2* xb, int* gsum,
-                           int* sh_exp, unsigned* sh_max, int tid, int nthr) {
-  constexpr int CH = 4;          // 8-value chunks a thread keeps in registers on the one-pass path
-  constexpr int SEG = GS / 8;    // chunks per group (lanes reduced together)
-  const int M = a.M;
-  auto sync = [&]() {
-    if constexpr (NAMED) {
-      asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
-    } else {
-      __syncthreads();
+// Store the planes of chunk kc (8 values) of token m into the B layout. BITS 4: an int4 packed
+// row r (K 8r .. 8r+7) is lane (r % 4)'s B registers of step r / 4 (even offsets -> MMA k 4t + i,
+// odd -> 16 + 4t + i). BITS 8 (int8 weights, Q4_K bytes): packed rows 8s + t and 8s + 4 + t are
+// lane t's two registers of step s; a chunk is rows 2kc and 2kc + 1.
+template <int BITS>
+__device__ __forceinline__ void put3(const uint32_t (&pl)[3][2], int m, int kc, int sstride, uint2* xb) {
+  if constexpr (BITS == 4) {
+    uint2* dst = xb + ((kc >> 2) * 4 + (kc & 3)) * sstride + 3 * m;
+#pragma unroll
+    for (int P = 0; P < 3; ++P) dst[P] = make_uint2(pl[P][0], pl[P][1]);
+  } else {
+    const int r0 = 2 * kc, s8 = r0 >> 3, j = r0 & 7, half = j >> 2, t0 = j & 3;
+    uint32_t* d0 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0) * sstride + 3 * m) + half;
+    uint32_t* d1 = reinterpret_cast<uint32_t*>(xb + (s8 * 4 + t0 + 1) * sstride + 3 * m) + half;
+#pragma unroll
+    for (int P = 0; P < 3; ++P) {
+      d0[2 * P] = pl[P][0];
+      d1[2 * P] = pl[P][1];
     }
-  };
+  }
+}
+
+// One chunk (8 values of token m at chunk kc of the slice) of a warp that covers whole exponent
+// groups: the group's exponent from a shuffle maximum over its EG / 8 lanes, the planes, and
+// the group sums over SG / 8 lanes. `live` lanes store (put3, then sums(m, kc / (SG / 8), S1,
+// S0) and expo(m, kc / (EG / 8), fe) from the first lane of each group); the others only take
+// part in the shuffles. fe = 2^e, or NaN for a group holding inf / nan.
+template <int BITS, int SG, int EG, class SumFn, class ExpFn>
+__device__ __forceinline__ void stage_chunk3(const float (&v)[8], bool live, int m, int kc, int sstride, uint2* xb,
+                                             SumFn& sums, ExpFn& expo) {
+  constexpr int SSEG = SG / 8, ESEG = EG / 8;
+  static_assert(ESEG >= SSEG && ESEG <= 32 && (ESEG & (ESEG - 1)) == 0, "exponent groups of 8 to 256 values");
+  uint32_t mb = abs_bits_max(v);
+#pragma unroll
+  for (int o = ESEG / 2; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+  const bool finite = mb < 0x7f800000u;
+  const int e = finite ? stage_exponent_i23(mb) : 0;
+  uint32_t pl[3][2];
+  int s1, s0;
+  split3<BITS>(v, finite ? exp2i(-e) : 0.f, pl, s1, s0);
+#pragma unroll
+  for (int o = SSEG / 2; o > 0; o >>= 1) {
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+  }
+  if (live) {
+    put3<BITS>(pl, m, kc, sstride, xb);
+    if (kc % SSEG == 0) sums(m, kc / SSEG, s1, s0);
+    if (kc % ESEG == 0) expo(m, kc / ESEG, finite ? exp2i(e) : __int_as_float(0x7fc00000));
+  }
+}
+
+// Stage x[:, kbase : kbase + klen] for M tokens (rows of `a`) into the three-plane B layout in
+// shared memory, rows sstride slots apart (klen a multiple of EG). Every warp takes 32
+// consecutive chunks of one token, so groups never straddle warps.
+// NAMED: synchronise only the nthr participating threads with named barrier 1 (the TMA-fed
+// kernels keep their producer warp out of the staging); otherwise __syncthreads.
+template <int BITS, int SG, int EG, bool NAMED, class Args, class SumFn, class ExpFn>
+__device__ void stage_x3(const Args& a, int kbase, int klen, int sstride, uint2* xb, SumFn sums, ExpFn expo, int tid,
+                         int nthr) {
+  constexpr int CH = 4;   // chunks a thread loads before converting (memory-level parallelism)
+  const int M = a.M;
   const int cpr = klen / 8;
   const int nchunk = M * cpr;
-  auto store_chunk = [&](int idx, const float (&v)[8]) {
-    const int m = M == 1 ? 0 : idx / cpr, kc = idx - m * cpr;
-    const float s = exp2i(-stage_exponent_i15(__uint_as_float(sh_max[m])));
-    int sum = put_chunk_i8<BITS, SWZ>(v, s, m, kc, sstride, xb);
-    // the SEG chunks of one group sit in SEG consecutive lanes
-#pragma unroll
-    for (int o = SEG / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if ((kc % SEG) == 0) gsum[m * gstride + kc / SEG] = sum;
-  };
-  auto row_max = [&](int m, float mx) { atomicMax(&sh_max[m], __float_as_uint(mx)); };
-  if (nchunk <= nthr * CH) {
+  for (int base = 0; base < nchunk; base += CH * nthr) {
     float v[CH][8];
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const int idx = tid + c * nthr;
+      const int idx = base + c * nthr + tid;
       if (idx < nchunk) {
         const int m = M == 1 ? 0 : idx / cpr;
         load_x8(a, m, kbase + (idx - m * cpr) * 8, v[c]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[c][j] = 0.f;
       }
     }
 #pragma unroll
     for (int c = 0; c < CH; ++c) {
-      const int idx = tid + c * nthr;
-      float mx = 0.f;
-      if (idx < nchunk) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[c][j]));
-        if (mx != mx) mx = __int_as_float(0x7f800000);   // NaN counts as non-finite
-      }
-      const int base_idx = tid - (tid & 31) + c * nthr;
-      const bool uniform = (cpr % 32 == 0) && base_idx < nchunk;
-      if (uniform) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if ((tid & 31) == 0) row_max(base_idx / cpr, mx);
-      } else if (idx < nchunk) {
-        row_max(idx / cpr, mx);
-      }
-    }
-    sync();
-    // every thread derives its row's exponent from the maxima; sh_exp is read only after the
-    // final barrier
-    if (tid < M) sh_exp[tid] = stage_exponent_i15(__uint_as_float(sh_max[tid]));
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const int idx = tid + c * nthr;
-      if (tid - (tid & 31) + c * nthr < nchunk) {   // warp-uniform: whole groups per warp
-        float w[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = idx < nchunk ? v[c][j] : 0.f;
-        if (idx < nchunk) store_chunk(idx, w);
-        else {
-          int z = 0;   // keep the group-sum shuffles converged
-#pragma unroll
-          for (int o = SEG / 2; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-        }
-      }
-    }
-  } else {
-    for (int m = 0; m < M; ++m) {
-      float mx = 0.f;
-      for (int kc = tid; kc < cpr; kc += nthr) {
-        float v[8];
-        load_x8(a, m, kbase + kc * 8, v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
-        if (mx != mx) mx = __int_as_float(0x7f800000);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      if ((tid & 31) == 0) row_max(m, mx);
-    }
-    sync();
-    if (tid < M) sh_exp[tid] = stage_exponent_i15(__uint_as_float(sh_max[tid]));
-    for (int base = 0; base < nchunk; base += nthr) {
-      const int idx = base + tid;
-      if (base + (tid - (tid & 31)) < nchunk) {      // warp-uniform
-        float v[8];
-        if (idx < nchunk) {
-          const int m = idx / cpr;
-          load_x8(a, m, kbase + (idx - m * cpr) * 8, v);
-          store_chunk(idx, v);
-        } else {
-          int z = 0;
-#pragma unroll
-          for (int o = SEG / 2; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-        }
+      const int idx = base + c * nthr + tid;
+      if (base + c * nthr + (tid & ~31) < nchunk) {   // warp-uniform: the warp's groups
+        const int m = M == 1 ? 0 : idx / cpr;
+        stage_chunk3<BITS, SG, EG>(v[c], idx < nchunk, m, idx - m * cpr, sstride, xb, sums, expo);
       }
     }
   }
-  sync();
+  if constexpr (NAMED) {
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+  } else {
+    __syncthreads();
+  }
 }
-
-// Activations staged once in global memory for the TMA-fed GEMVs of more than 4 tokens, so no
-// CTA stages them itself: tokens in chunks of MAXM, chunk c at xg + c * chunk_bytes holding the
-// B operand of all K (rows of xb_slots(2 MAXM) slots, swizzled, as stage_x_i8 with SWZ) and, at
-// sum_off, the group sums as [group][MAXM]. xe[m] = the token's exponent e (x = v * 2^e), or
-// kNonFinite for a row with inf / nan.
-constexpr int kNonFinite = (int)0x80000000;
 
 }  // namespace gemv
 
 namespace {
-// One CTA per token row (256 threads): the row's absolute maximum, then its 8-value chunks.
-template <int BITS, int GS, int MAXM, class Args>
-__global__ void __launch_bounds__(256) prestage_x_kernel(const Args a, int K, uint8_t* __restrict__ xg, long chunk_bytes,
-                                                         long sum_off, int* __restrict__ xe) {
-  constexpr int SEG = GS / 8;
-  constexpr int SS = gemv::xb_slots(2 * MAXM);
-  __shared__ float s_max[8];
+// Activations staged once in global memory for the TMA-fed GEMVs of more than 4 tokens, so no
+// CTA stages them itself. Tokens go in chunks of MAXM; chunk c at xg + c * chunk_bytes holds the
+// B operand of all K (rows of xb3_slots(MAXM) slots) and, at sum_off, per stage-contiguous sums:
+//   LAYOUT 0 (GPTQ, SG = EG = the group): group g at ints g * 3 * MAXM: [S1 | S0 | fe bits][MAXM]
+//   LAYOUT 1 (Q4_K, SG = 32, EG = 256): super-block b at ints b * q4k_sum_ints(MAXM): sub-block
+//            j's [S1 | S0][MAXM] at (2 j) * MAXM, then fe bits [MAXM] at 16 * MAXM (each
+//            super-block's record padded to 128 bytes, so ring stages stay 128-byte aligned)
+// One CTA of 256 threads per token row.
+__host__ __device__ constexpr int q4k_sum_ints(int maxm) { return (17 * maxm + 31) & ~31; }
+
+template <int BITS, int SG, int EG, int MAXM, int LAYOUT, class Args>
+__global__ void __launch_bounds__(256) prestage_x3_kernel(const Args a, int K, uint8_t* __restrict__ xg,
+                                                          long chunk_bytes, long sum_off) {
+  constexpr int SS = gemv::xb3_slots(MAXM);
   const int m = blockIdx.x, c = m / MAXM, mm = m - c * MAXM;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int cpr = K / 8;
-  float mx = 0.f;
-  for (int kc = tid; kc < cpr; kc += 256) {
-    float v[8];
-    gemv::load_x8(a, m, kc * 8, v);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, fabsf(v[j]));
-    if (mx != mx) mx = __int_as_float(0x7f800000);   // NaN counts as non-finite
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) s_max[warp] = mx;
-  __syncthreads();
-  mx = s_max[0];
-#pragma unroll
-  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, s_max[w]);
-  const int e = stage_exponent_i15(mx);
-  if (tid == 0) xe[m] = mx < 3.0e38f ? e : gemv::kNonFinite;
-  const float s = exp2i(-e);
   uint2* xb = reinterpret_cast<uint2*>(xg + (long)c * chunk_bytes);
-  int* gsum = reinterpret_cast<int*>(xg + (long)c * chunk_bytes + sum_off);
-  for (int base = 0; base < cpr; base += 256) {   // warp-uniform trip count (group shuffles)
-    const int kc = base + tid;
-    float v[8];
-    if (kc < cpr) {
-      gemv::load_x8(a, m, kc * 8, v);
+  int* sm = reinterpret_cast<int*>(xg + (long)c * chunk_bytes + sum_off);
+  auto sums = [&](int, int g, int s1, int s0) {
+    if constexpr (LAYOUT == 0) {
+      sm[(g * 3 + 0) * MAXM + mm] = s1;
+      sm[(g * 3 + 1) * MAXM + mm] = s0;
     } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      const int b = g >> 3, j = g & 7;
+      sm[b * q4k_sum_ints(MAXM) + (2 * j) * MAXM + mm] = s1;
+      sm[b * q4k_sum_ints(MAXM) + (2 * j + 1) * MAXM + mm] = s0;
     }
-    int sum = kc < cpr ? gemv::put_chunk_i8<BITS, true>(v, s, mm, kc, SS, xb) : 0;
+  };
+  auto expo = [&](int, int g, float fe) {
+    if constexpr (LAYOUT == 0)
+      sm[(g * 3 + 2) * MAXM + mm] = __float_as_int(fe);
+    else
+      sm[g * q4k_sum_ints(MAXM) + 16 * MAXM + mm] = __float_as_int(fe);
+  };
+  for (int base = 0; base < cpr; base += 256) {   // cpr is a multiple of 16 (32 for Q4_K)
+    const int kc = base + tid;
+    if (base + (tid & ~31) < cpr) {
+      float v[8];
+      if (kc < cpr) {
+        gemv::load_x8(a, m, kc * 8, v);
+      } else {
 #pragma unroll
-    for (int o = SEG / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (kc < cpr && kc % SEG == 0) gsum[(kc / SEG) * MAXM + mm] = sum;
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      }
+      gemv::stage_chunk3<BITS, SG, EG>(v, kc < cpr, mm, kc, SS, xb, sums, expo);
+    }
   }
 }
 }  // namespace

@@ -30,7 +30,6 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include <mutex>
 
 #include "ql_common.cuh"
 #include "sm100_ptx.cuh"
@@ -637,7 +636,7 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
       set_error("ql_gptq_matmul: workspace of %zu bytes is smaller than the %zu needed", ws_bytes, need);
       return QL_ERR_ARG;
     }
-    int rc = cuda_status(cudaMallocAsync(&ws, need, st), "cudaMallocAsync(workspace)");
+    int rc = stream_alloc(&ws, need, st, "ql_gptq_matmul: workspace");
     if (rc) return rc;
     owned = true;
   }
@@ -653,31 +652,11 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
     a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
     a.n_wtiles = (N + kTileN - 1) / kTileN;
     a.gb = gs == 32 ? 2 : 1;
-    // 256-token tiles once they still give every SM a tile; 128 below (small M)
-    static int min_m256 = -1;
-    if (min_m256 < 0) min_m256 = env_int("QL_GEMM_BT256_MIN_M", 1 << 30);   // measured slower so far
-    if (M >= min_m256) {
-      a.n_ttiles = (M + 255) / 256;
-      rc = bits == 4 ? launch_gemm<4, 256>(a, x16, 1, st) : launch_gemm<8, 256>(a, x16, 1, st);
-    } else {
-      // 128-value stages when the groups hold whole stages (one scale row per stage)
-      static int sk = -1;
-      if (sk < 0) sk = env_int("QL_GEMM_SK", 128);
-      a.n_ttiles = (M + 127) / 128;
-      if (sk == 256 && K % 256 == 0 && (gs == 128 || gs % 256 == 0)) {
-        a.gb = gs == 128 ? 2 : 1;   // scale / zero rows per 256-value stage
-        rc = bits == 4 ? launch_gemm<4, 128, 256>(a, x16, 1, st) : launch_gemm<8, 128, 256>(a, x16, 1, st);
-      } else if (sk >= 128 && K % 128 == 0 && gs % 128 == 0) {
-        static int alt = -1;
-        if (alt < 0) alt = env_int("QL_GEMM_DQ_ALT", 1);
-        if (alt)
-          rc = bits == 4 ? launch_gemm<4, 128, 128, true>(a, x16, 1, st) : launch_gemm<8, 128, 128, true>(a, x16, 1, st);
-        else
-          rc = bits == 4 ? launch_gemm<4, 128, 128>(a, x16, 1, st) : launch_gemm<8, 128, 128>(a, x16, 1, st);
-      }
-      else
-        rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
-    }
+    a.n_ttiles = (M + 127) / 128;
+    if (K % 128 == 0 && gs % 128 == 0)   // 128-value stages (one scale row each), dequant groups alternating
+      rc = bits == 4 ? launch_gemm<4, 128, 128, true>(a, x16, 1, st) : launch_gemm<8, 128, 128, true>(a, x16, 1, st);
+    else
+      rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
   }
   if (owned) {
     const int rc2 = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(workspace)");
@@ -795,27 +774,14 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 24ull << 20;  // 24 MiB: M * K up to ~12.5 M activations
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64];
-
-// Device address of the scratch array on the current device, resolved once per device (the
-// host-side symbol is only a stand-in; a kernel must be given this address).
+// Device address of the scratch array in the current device's context. The host-side symbol is
+// only a stand-in; a kernel must be given this address. It is looked up on every call (the
+// lookup allocates nothing), so a context torn down and created again never leaves a stale one.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  int rc = cuda_status(cudaGetDevice(&dev), "ql_gptq_matmul_noalloc: cudaGetDevice");
+  void* p = nullptr;
+  const int rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "ql_gptq_matmul_noalloc: cudaGetSymbolAddress");
   if (rc) return rc;
-  if (dev < 0 || dev >= 64) {
-    set_error("ql_gptq_matmul_noalloc: device ordinal %d out of range", dev);
-    return QL_ERR_UNSUPPORTED;
-  }
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    rc = cuda_status(cudaGetSymbolAddress(&p, g_noalloc_scratch), "ql_gptq_matmul_noalloc: cudaGetSymbolAddress");
-    if (rc) return rc;
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
+  *out = p;
   return QL_OK;
 }
 
@@ -848,6 +814,8 @@ extern "C" int ql_gptq_matmul_noalloc(const void* x, int x_dtype, long ldx, cons
     if (rc) return rc;
     ws_bytes = ql::kNoAllocScratchBytes;
   }
+  // no path below may fall back to the stream-ordered allocator: it fails instead
+  const ql::AllocGuard no_alloc;
   return ql::gptq_matmul_impl(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype,
                               ldo, M, K, N, gs, bits, zero_offset, stream, ws, ws_bytes);
 }

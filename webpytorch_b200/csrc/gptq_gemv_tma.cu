@@ -3,19 +3,24 @@
 // so each CTA keeps its whole ring in flight however long the consumer warps take per stage;
 // consumer warps touch only shared memory.
 //
-// Arithmetic (shared with the register-fed kernel, gptq_gemv.cu): nibbles become fp16
-// "1024 + q" / "1024 + 16 q" with one LOP3 each, mma.sync (register operands) forms the dot
-// products and the 4-lane K reduction, and the magic offsets and the zero point are folded
-// into per-group activation sums: acc += scale * (C - 1024 A - (z + off) S).
+// Arithmetic: integer tensor-core MMA (mma.sync m16n8k32, u8 weights x s8 activation bytes).
+// An int4 word (8 consecutive K of one column) becomes two A-fragment registers with three ALU
+// ops; an int8 word is an A register as it is. Activations are staged as 23-bit integers with one
+// power-of-two exponent per group (gemv_common.cuh, stage_x3), split into three signed byte
+// planes that occupy three MMA columns per token. Per group the MMA yields exact int32 dot
+// products, and the zero point folds into the group sums S of the staged integers:
+//   acc += scale * 2^e * (C - (z + off) * S),   C = 256 * C_hi + C_lo (exact)
+// for the lane that owns the (b2, b1) plane pair and for the lane that owns (b0, 0); the two
+// lanes' sums are added (the first times 2^8) when the kernel finishes.
 //
-// Ring stage = 128 values of K for the CTA's 256 columns:
+// Ring stage = 128 values of K for the CTA's 256 (or 128) columns:
 //   weights  3-D TMA box over the packed weight viewed as [N/32 strips][K/per rows][32 columns]:
 //            per 32-column strip a [rows][128 B] block with the 128-byte swizzle (16-byte chunk
-//            c of row r at chunk c ^ (r % 8)); consumer warp w reads strip w, lane (g, t) of
+//            c of row r at chunk c ^ (r % 8)); consumer warp w reads strip w % SW, lane (g, t) of
 //            step s the 16 bytes of row 4s + t, chunk g (at most 2-way bank conflicts)
-//   scales   2-D box [groups of the stage][256 columns]
-//   zeros    2-D box [groups of the stage][256 / per words]
-// Split-K runs over a thread-block cluster reduced through distributed shared memory.
+//   scales   2-D box [groups of the stage][tile columns]
+//   zeros    2-D box [groups of the stage][tile columns / per words]
+// Split-K runs over a thread-block cluster; partial sums go to the owning rank's shared memory.
 #include <cooperative_groups.h>
 #include <cuda.h>
 
@@ -74,11 +79,11 @@ struct TmaGemvArgs {
   int g_max_tiles;  // host: table capacity (grid z)
   int n_experts;    // host: stacked weight matrices (1 when dense)
   int glu;          // > 0: x rows are [gate | up] glu elements apart (SwiGLU applied when staging)
-  // dense calls of more than 4 tokens: activations staged once in global memory (one chunk:
-  // the B operand of all K, then the group sums at xg_sum_off) and exponents xe
+  // dense calls of more than 4 tokens: activations staged once in global memory, blockIdx.z
+  // taking tokens [z * MAXM, z * MAXM + MAXM) from chunk z at xg + z * xg_chunk (the B operand
+  // of all K, then per group [S1 | S0 | fe][MAXM] at xg_sum_off)
   const uint8_t* xg;
-  long xg_sum_off;
-  const int* xe;
+  long xg_chunk, xg_sum_off;
 };
 
 // Activation source of one CTA (its rows of x, possibly gathered).
@@ -94,8 +99,8 @@ struct XSrc {
 };
 
 // Ring stage: weights, scales, zeros; with XP also the stage's B operand (4 steps x 4 lanes x
-// kXSlots slots x 8 bytes) and its group sums [GPS][MAXM].
-template <int BITS, int GS, int NST, int SCB, int SW, int MAXM = 4, bool XP = false>
+// kXSlots slots x 8 bytes) and its group sums [GPS][3][MAXM]. MAXM = 2 NP tokens (NP MMA tiles).
+template <int BITS, int GS, int NST, int SCB, int SW, int MAXM = 2, bool XP = false>
 struct TmaLayout {
   static constexpr int PER = 32 / BITS;
   static constexpr int TC = 32 * SW;                       // columns per CTA tile
@@ -106,39 +111,40 @@ struct TmaLayout {
   static constexpr int kScBytes = GPS * TC * SCB;          // scales of the stage
   static constexpr int kZBytes = GPS * (TC / PER) * 4;
   static constexpr int kWSZBytes = (kWBytes + kScBytes + kZBytes + 15) & ~15;
-  static constexpr int kXSlots = gemv::xb_slots(2 * MAXM);
+  static constexpr int kXSlots = gemv::xb3_slots(MAXM);
   static constexpr int kXBytes = XP ? kStageK * kXSlots : 0;
-  static constexpr int kGBytes = XP ? GPS * MAXM * 4 : 0;
+  static constexpr int kGBytes = XP ? GPS * 3 * MAXM * 4 : 0;
   static constexpr int kStageBytes = (kWSZBytes + kXBytes + kGBytes + 1023) & ~1023;
   static constexpr int kBarOff = NST * kStageBytes;
   static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier, abort flag
 };
 
-template <int BITS, int GS, int NQ, int NST, int SCB, int SW, bool XP>
+// NP MMA tiles of two tokens each (MAXM = 2 NP tokens per CTA).
+template <int BITS, int GS, int NP, int NST, int SCB, int SW, bool XP>
 __global__ void __launch_bounds__(kThreads, 2)
     gptq_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_s,
                          const __grid_constant__ CUtensorMap tmap_z, const TmaGemvArgs a) {
-  using L = TmaLayout<BITS, GS, NST, SCB, SW, 4 * NQ, XP>;
+  constexpr int MAXM = 2 * NP;
+  using L = TmaLayout<BITS, GS, NST, SCB, SW, MAXM, XP>;
   constexpr int TC = L::TC;
   constexpr int KW = kCW / SW;
   constexpr int PER = L::PER;
   constexpr int GPS = L::GPS;
   constexpr int SPG = GS / 32;                             // 32-K MMA steps per group
-  constexpr int MAXM = 4 * NQ;
   constexpr uint32_t MASK = (1u << BITS) - 1u;
+  static_assert(KW == 1 || NST % 2 == 0, "two K-ways need an even ring depth (each slot stays with one way)");
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ int sh_exp[16];
-  __shared__ unsigned sh_max[16];
   const uint32_t sbase = ptx::smem_addr(smem);
   const uint32_t bar_full = sbase + L::kBarOff;
   const uint32_t bar_empty = bar_full + 8 * NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kBarOff + 16 * NST);
   const uint32_t bar_red = bar_full + 16 * NST + 8;   // partial sums received from the cluster
 
-  // grouped mode: which expert and rows this cluster takes (uniform over the cluster, which
-  // shares blockIdx.z); slots and chunks without rows leave before any barrier
+  // which rows this CTA takes: grouped mode reads the tile table (uniform over the cluster,
+  // which shares blockIdx.z; slots without rows leave before any barrier), dense calls of more
+  // than MAXM tokens take token chunk z
   int M = a.M, e = 0;
   long row0 = 0;
   if (a.g_offsets) {
@@ -147,7 +153,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     e = a.g_tiles[2 * tz];
     row0 = a.g_offsets[e] + a.g_tiles[2 * tz + 1];
     M = min(MAXM, a.g_offsets[e + 1] - (int)row0);
+  } else if (XP) {
+    row0 = (long)blockIdx.z * MAXM;
+    M = min(MAXM, a.M - (int)row0);
   }
+  const uint8_t* xgc = XP ? a.xg + (long)blockIdx.z * a.xg_chunk : nullptr;
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int rank = blockIdx.x;
@@ -159,18 +169,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int klen_max = nst_max * kStageK;
   const int ng_max = nst_max * GPS;
   const int N = a.N;
-  // staged activations: B rows of sstride slots (swizzled), group sums gstride ints apart (odd
-  // from two tokens on, so the 4 tokens a warp reads at once sit in distinct banks)
-  constexpr bool SWZ = NQ > 1;   // swizzled B rows (more than 4 tokens)
-  const int sstride = XP ? L::kXSlots : (SWZ ? gemv::xb_slots(2 * M) : 2 * M);
-  const int gstride = M > 1 ? (ng_max | 1) : ng_max;
+  // staged activations (without XP): B rows of sstride slots, then [3 M rows][gstride] ints of
+  // group sums and factors (row 3m: S of v1, 3m + 1: S of b0, 3m + 2: fe bits)
+  const int sstride = XP ? L::kXSlots : gemv::xb3_slots(M);
+  const int gstride = ng_max | 1;
   uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
   const int xs_bytes = XP ? 0 : (klen_max * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
-  const int gs_bytes = XP ? 0 : (M * gstride * 4 + 15) & ~15;
+  const int gs_bytes = XP ? 0 : (3 * M * gstride * 4 + 15) & ~15;
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
   // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16 (only
-  // with cs > 1); kred: K-way partials (KW == 2), [SW * 32 lanes][NQ * 4]
+  // with cs > 1); kred: K-way partials (KW == 2), [SW * 32 lanes][NP * 4]
   float* kred = red + (a.cs > 1 ? (TC + 64) * MAXM : 0);
 
   // Split-K reduction over the cluster: rank q owns the column quads [qs(q), qs(q + 1)) of
@@ -191,7 +200,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     ptx::fence_mbar_init();
     if (cs > 1) ptx::mbar_arrive_expect_tx(bar_red, (uint32_t)(cs * M * (oq1 - oq0) * 16));
   }
-  if (tid < 16) sh_max[tid] = 0u;
   __syncthreads();
   if (cs > 1) cluster_arrive_relaxed();   // waited for before the first remote store
 
@@ -225,8 +233,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         ptx::tma_load_2d(st + L::kWBytes, &tmap_s, fb, blockIdx.y * TC, srow);
         ptx::tma_load_2d(st + L::kWBytes + L::kScBytes, &tmap_z, fb, blockIdx.y * (TC / PER), srow);
         if constexpr (XP) {
-          ptx::bulk_load(st + L::kWSZBytes, a.xg + (long)(s0 + i) * L::kXBytes, L::kXBytes, fb);
-          ptx::bulk_load(st + L::kWSZBytes + L::kXBytes, a.xg + a.xg_sum_off + (long)(s0 + i) * L::kGBytes, L::kGBytes,
+          ptx::bulk_load(st + L::kWSZBytes, xgc + (long)(s0 + i) * L::kXBytes, L::kXBytes, fb);
+          ptx::bulk_load(st + L::kWSZBytes + L::kXBytes, xgc + a.xg_sum_off + (long)(s0 + i) * L::kGBytes, L::kGBytes,
                          fb);
         }
       }
@@ -239,35 +247,44 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (cs > 1) cluster_wait_acquire();   // pairs with the arrive above (every thread once)
   } else {
     // ------------------------------------------------------------ consumer warps
-    // Lane (g, t) owns columns 4g .. 4g+3 of its warp's 32-column strip and, per token quad
-    // mq, token 4 mq + t. Integer MMA m16n8k32: rows g / g + 8 of tile 0 are columns 4g /
-    // 4g + 1, of tile 1 columns 4g + 2 / 4g + 3; MMA columns 2t / 2t + 1 are the high / low
-    // activation bytes of token t.
+    // Lane (g, t) owns columns 4g .. 4g+3 of its warp's 32-column strip. MMA m16n8k32: rows
+    // g / g + 8 of tile 0 are columns 4g / 4g + 1, of tile 1 columns 4g + 2 / 4g + 3. In MMA
+    // tile mq, B columns 4u .. 4u + 3 hold b2, b1, 0, b0 of token 2 mq + u, so the lane's D
+    // columns 2t, 2t + 1 are the plane pair t % 2 ((b2, b1) or (0, b0)) of token 2 mq + t / 2
+    // and C = 256 * D[2t] + D[2t + 1] is the exact dot product with v1 or with b0.
     const int gq = lane >> 2, t = lane & 3;
     const int strip = warp % SW, kway = warp / SW;
     const int lcol = strip * 32 + gq * 4;                   // first of this lane's 4 columns
     const int c0 = blockIdx.y * TC + lcol;
     const bool col_ok = c0 < N;
-    const int slots = 2 * M;
     const int zoff = (int)a.zoff;
+    const int ptok = t >> 1, pp = t & 1;                     // D side: token in tile, plane pair
+    // B side: token in tile, and the stored plane of column gq (columns 4u .. 4u + 3 of token
+    // u are b2, b1, zero, b0, so that the lane pairs read (b2, b1) and (0, b0))
+    const int btok = gq >> 2, bpl = (gq & 3) == 3 ? 2 : (gq & 3);
+    const bool bld = (gq & 3) != 2;
     pdl_wait();   // x may be the previous kernel's output
-    // this CTA's rows: gathered through x_rows, else x itself from row row0 on
-    const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
-    const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
-                    a.ldx, a.x_dtype, a.x_vec, M, a.glu};
-    if constexpr (!XP)
-      gemv::stage_x_i8<BITS, GS, true, SWZ>(xsrc, s0 * kStageK, klen, gstride, sstride, xb, gsum, sh_exp, sh_max,
-                                            tid, kCW * 32);
+    if constexpr (!XP) {
+      // this CTA's rows: gathered through x_rows, else x itself from row row0 on
+      const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
+      const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
+                      a.ldx, a.x_dtype, a.x_vec, M, a.glu};
+      auto sums = [&](int m, int g, int s1, int s0v) {
+        gsum[(3 * m) * gstride + g] = s1;
+        gsum[(3 * m + 1) * gstride + g] = s0v;
+      };
+      auto expo = [&](int m, int g, float fe) { gsum[(3 * m + 2) * gstride + g] = __float_as_int(fe); };
+      gemv::stage_x3<BITS, GS, GS, true>(xsrc, s0 * kStageK, klen, sstride, xb, sums, expo, tid, kCW * 32);
+    }
 
-    float acc[NQ][4];
+    float acc[NP][4];
 #pragma unroll
-    for (int mq = 0; mq < NQ; ++mq)
+    for (int mq = 0; mq < NP; ++mq)
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[mq][c] = 0.f;
 
     const uint32_t strip_off = strip * L::kStripBytes;
     const uint32_t xb_base = ptx::smem_addr(xb);
-    const int swz = SWZ ? gemv::xb_swz(sstride, t) : 0;
     for (int i = kway; i < nst; i += KW) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
@@ -275,9 +292,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const unsigned char* stp = smem + s * L::kStageBytes;
 #pragma unroll
       for (int u = 0; u < GPS; ++u) {
-        int d[NQ][2][4];
+        int d[NP][2][4];
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq)
+        for (int mq = 0; mq < NP; ++mq)
 #pragma unroll
           for (int p = 0; p < 2; ++p)
 #pragma unroll
@@ -313,19 +330,19 @@ __global__ void __launch_bounds__(kThreads, 2)
             A1[0] = w.z; A1[1] = w.w; A1[2] = v.z; A1[3] = v.w;
           }
 #pragma unroll
-          for (int mq = 0; mq < NQ; ++mq) {
-            const int slot = 8 * mq + gq;
+          for (int mq = 0; mq < NP; ++mq) {
+            const int tok = 2 * mq + btok;
             uint32_t b0 = 0u, b1 = 0u;
-            if (slot < slots) {
-              const uint32_t xa = XP ? st + L::kWSZBytes + (((u * SPG + sp) * 4 + t) * sstride + (slot ^ swz)) * 8
-                                     : xb_base + ((step * 4 + t) * sstride + (slot ^ swz)) * 8;
+            if (bld && tok < M) {
+              const uint32_t xa = XP ? st + L::kWSZBytes + (((u * SPG + sp) * 4 + t) * sstride + 3 * tok + bpl) * 8
+                                     : xb_base + ((step * 4 + t) * sstride + 3 * tok + bpl) * 8;
               asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
             }
             mma_16832_u8s8(d[mq][0], A0[0], A0[1], A0[2], A0[3], b0, b1);
             mma_16832_u8s8(d[mq][1], A1[0], A1[1], A1[2], A1[3], b0, b1);
           }
         }
-        // fold the group: acc += scale * (C - (z + off) * S), C = 256 * hi + lo (exact)
+        // fold the group: acc += scale * 2^e * (C - (z + off) * S), C = 256 * C_hi + C_lo (exact)
         const int gl = i * GPS + u;
         float scv[4];
         if constexpr (SCB == 2) {
@@ -348,15 +365,24 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < 4; ++c) zo[c] = (int)((zw >> (BITS * c)) & MASK) + zoff;
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq) {
-          const int tok = 4 * mq + t;
-          const int S = tok >= M ? 0
-                        : XP ? *reinterpret_cast<const int*>(stp + L::kWSZBytes + L::kXBytes + (u * MAXM + tok) * 4)
-                             : gsum[tok * gstride + gl];
+        for (int mq = 0; mq < NP; ++mq) {
+          const int tok = 2 * mq + ptok;
+          int S = 0;
+          float fe = 0.f;
+          if (tok < M) {
+            if constexpr (XP) {
+              const int* gsr = reinterpret_cast<const int*>(stp + L::kWSZBytes + L::kXBytes) + u * 3 * MAXM;
+              S = gsr[pp * MAXM + tok];
+              fe = __int_as_float(gsr[2 * MAXM + tok]);
+            } else {
+              S = gsum[(3 * tok + pp) * gstride + gl];
+              fe = __int_as_float(gsum[(3 * tok + 2) * gstride + gl]);
+            }
+          }
           const int C[4] = {d[mq][0][0] * 256 + d[mq][0][1], d[mq][0][2] * 256 + d[mq][0][3],
                             d[mq][1][0] * 256 + d[mq][1][1], d[mq][1][2] * 256 + d[mq][1][3]};
 #pragma unroll
-          for (int c = 0; c < 4; ++c) acc[mq][c] = fmaf(scv[c], (float)(C[c] - zo[c] * S), acc[mq][c]);
+          for (int c = 0; c < 4; ++c) acc[mq][c] = fmaf(scv[c] * fe, (float)(C[c] - zo[c] * S), acc[mq][c]);
         }
       }
       __syncwarp();
@@ -365,40 +391,38 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     if constexpr (KW == 2) {
       // the second K-way hands its partial sums to the first through shared memory
-      float* kr = kred + (strip * 32 + lane) * (NQ * 4);
+      float* kr = kred + (strip * 32 + lane) * (NP * 4);
       if (kway == 1) {
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq)
+        for (int mq = 0; mq < NP; ++mq)
 #pragma unroll
           for (int c = 0; c < 4; ++c) kr[mq * 4 + c] = acc[mq][c];
       }
       asm volatile("bar.sync 2, %0;" ::"r"(kCW * 32) : "memory");
       if (kway == 0) {
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq)
+        for (int mq = 0; mq < NP; ++mq)
 #pragma unroll
           for (int c = 0; c < 4; ++c) acc[mq][c] += kr[mq * 4 + c];
       }
     }
-    const bool writer = kway == 0;
-    // non-finite activation rows give NaN (the integer staging cannot carry inf / nan)
-    auto finish = [&](int tok, float v) {
-      if constexpr (XP) {
-        const int ex = a.xe[tok];
-        return ex != gemv::kNonFinite ? v * exp2i(ex) : __int_as_float(0x7fc00000);
-      } else {
-        const float mx = __uint_as_float(sh_max[tok]);
-        return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+    // the (b2, b1) lane's sums count 2^8 times the (b0, 0) lane's; add the pair (exact scaling)
+#pragma unroll
+    for (int mq = 0; mq < NP; ++mq)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float v = pp ? acc[mq][c] : 256.f * acc[mq][c];
+        acc[mq][c] = v + __shfl_xor_sync(0xffffffffu, v, 1);
       }
-    };
+    const bool writer = kway == 0 && pp == 0;
     if (cs == 1) {
 #pragma unroll
-      for (int mq = 0; mq < NQ; ++mq) {
-        const int tok = 4 * mq + t;
+      for (int mq = 0; mq < NP; ++mq) {
+        const int tok = 2 * mq + ptok;
         if (writer && tok < M && col_ok) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            float v = finish(tok, acc[mq][c]);
+            float v = acc[mq][c];
             if (a.bias) v += a.bias[c0 + c];
             store_from_float(a.out, a.out_dtype, (row0 + tok) * a.ldo + c0 + c, v);
           }
@@ -414,12 +438,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t rbase = ptx::mapa(ptx::smem_addr(red), owner);
         const uint32_t rbar = ptx::mapa(bar_red, owner);
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq) {
-          const int tok = 4 * mq + t;
+        for (int mq = 0; mq < NP; ++mq) {
+          const int tok = 2 * mq + ptok;
           if (tok < M) {
             const uint32_t dst = rbase + (((rank * MAXM + tok) * cq_max + (lq - oq)) * 4) * 4;
-            ptx::st_async_v4(dst, finish(tok, acc[mq][0]), finish(tok, acc[mq][1]), finish(tok, acc[mq][2]),
-                             finish(tok, acc[mq][3]), rbar);
+            ptx::st_async_v4(dst, acc[mq][0], acc[mq][1], acc[mq][2], acc[mq][3], rbar);
           }
         }
       }
@@ -476,37 +499,48 @@ bool encode_2d(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const 
 constexpr int kMaxSmem = 220 * 1024;
 
 // Ring depth (NST) of the kernel built for (bits, sw): the same bytes in flight for both tile
-// widths. Batches of more than 4 tokens may also take a ring of half that depth, so that two
-// CTAs with their larger activation slices still fit on one SM.
+// widths. Batches of more than 2 tokens that stage their activations per CTA may also take a ring
+// of half that depth, so that two CTAs with their larger activation slices still fit on one SM.
+// With two K-ways (sw < kCW) the ring depth must be even: way j consumes the stages i with
+// i % 2 == j, and an even depth keeps every ring slot with one way. With an odd depth the two ways
+// alternate on a slot, so a way that runs ahead can wait on a slot two phases early, find the
+// barrier parity it waits for already set, and read a stage that has not been refilled.
 constexpr int nst_cap(int bits, int sw) { return (bits == 4 ? 4 : 3) * (kCW / sw); }
-constexpr int nst_half(int bits, int sw) { return nst_cap(bits, sw) / 2 > 2 ? nst_cap(bits, sw) / 2 : 2; }
+constexpr int nst_half(int bits, int sw) {
+  return sw < kCW ? (nst_cap(bits, sw) / 2 >= 4 ? (nst_cap(bits, sw) / 2) & ~1 : 2)
+                  : (nst_cap(bits, sw) / 2 > 2 ? nst_cap(bits, sw) / 2 : 2);
+}
 
-// Dynamic shared memory of one CTA (ring of nst = NST stages), as the kernel's prologue carves
-// it up: 1 KB of alignment slack, the ring, the barriers, the staged activations and their group
-// sums (unless xp: then each stage carries its own), the split-K receive buffer (cs > 1) and the
-// K-way hand-off (128-column tiles).
-size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int M, int nstage, bool xp) {
+// MMA tiles (two tokens each) of a CTA that takes m tokens.
+constexpr int np_of(int m) { return m <= 2 ? 1 : (m <= 4 ? 2 : 4); }
+constexpr int kXpTokens = 8;   // tokens per CTA when the activations are staged in global memory
+
+// Dynamic shared memory of one CTA (ring of nst = NST stages) that takes m tokens, as the
+// kernel's prologue carves it up: 1 KB of alignment slack, the ring, the barriers, the staged
+// activations and their group sums / factors (unless xp: then each stage carries its own), the
+// split-K receive buffer (cs > 1) and the K-way hand-off (128-column tiles).
+size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int nstage, bool xp) {
   const int per = 32 / bits, tc = 32 * sw, gps = kStageK / kgs, rows = kStageK / per;
-  const int nq = M <= 4 ? 1 : (M <= 8 ? 2 : 4);
+  const int np = xp ? kXpTokens / 2 : np_of(m), maxm = 2 * np;
   const size_t wsz = ((size_t)sw * rows * 128 + (size_t)gps * tc * scb + (size_t)gps * (tc / per) * 4 + 15) & ~(size_t)15;
-  const size_t xpart = xp ? (size_t)kStageK * gemv::xb_slots(8 * nq) + (size_t)gps * 4 * nq * 4 : 0;
+  const size_t xpart = xp ? (size_t)kStageK * gemv::xb3_slots(maxm) + (size_t)gps * 3 * maxm * 4 : 0;
   const size_t stage = (wsz + xpart + 1023) & ~(size_t)1023;
   const int sq = nstage / cs, nst_max = sq + (nstage % cs ? 1 : 0);
   const int ng_max = nst_max * gps;
   size_t b = 1024 + (size_t)nst * stage + 2 * nst * 8 + 16;
   if (!xp) {
-    b += ((size_t)nst_max * kStageK * gemv::xb_slots(2 * M) + 15) & ~(size_t)15;
-    b += ((size_t)M * (M > 1 ? (ng_max | 1) : ng_max) * 4 + 15) & ~(size_t)15;
+    b += ((size_t)nst_max * kStageK * gemv::xb3_slots(m) + 15) & ~(size_t)15;
+    b += ((size_t)3 * m * (ng_max | 1) * 4 + 15) & ~(size_t)15;
   }
-  if (cs > 1) b += (size_t)(tc + 64) * 4 * nq * 4;
-  if (sw < kCW) b += (size_t)sw * 32 * nq * 4 * 4;
+  if (cs > 1) b += (size_t)(tc + 64) * maxm * 4;
+  if (sw < kCW) b += (size_t)sw * 32 * np * 4 * 4;
   return b;
 }
 
-template <int BITS, int GS, int NQ, int NST, int SCB, int SW, bool XP>
+template <int BITS, int GS, int NP, int NST, int SCB, int SW, bool XP>
 int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qzeros, const void* scales,
                cudaStream_t st) {
-  using L = TmaLayout<BITS, GS, NST, SCB, SW, 4 * NQ, XP>;
+  using L = TmaLayout<BITS, GS, NST, SCB, SW, 2 * NP, XP>;
   constexpr int TC = L::TC;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
@@ -530,8 +564,8 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
                  (uint64_t)(a.N / L::PER) * 4,
                  TC / L::PER, L::GPS))
     return -1;
-  auto kern = gptq_gemv_tma_kernel<BITS, GS, NQ, NST, SCB, SW, XP>;
-  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, a.M, a.nstage, XP);
+  auto kern = gptq_gemv_tma_kernel<BITS, GS, NP, NST, SCB, SW, XP>;
+  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, XP ? kXpTokens : a.M, a.nstage, XP);
   if (smem > kMaxSmem) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -546,7 +580,8 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
     configured_dev = dev;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.cs, (a.N + TC - 1) / TC, a.g_offsets ? a.g_max_tiles : 1);
+  const int zdim = a.g_offsets ? a.g_max_tiles : (XP ? (a.M + kXpTokens - 1) / kXpTokens : 1);
+  cfg.gridDim = dim3(a.cs, (a.N + TC - 1) / TC, zdim);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -566,8 +601,8 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   if constexpr (XP) {
     // stage the activations once (one CTA per token row) for every CTA of the GEMV
     const XSrc xsrc{a.x, nullptr, a.x_perm, a.ldx, a.x_dtype, a.x_vec, a.M, 0};
-    prestage_x_kernel<BITS, GS, 4 * NQ><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg), 0, a.xg_sum_off,
-                                                            const_cast<int*>(a.xe));
+    prestage_x3_kernel<BITS, GS, GS, kXpTokens, 0><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg),
+                                                                       a.xg_chunk, a.xg_sum_off);
     const int rc = cuda_status(cudaGetLastError(), "gptq prestage launch");
     if (rc) return rc;
   }
@@ -575,13 +610,12 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
 }
 
 template <int BITS, int GS, int SW, int SCB>
-int tma_nq(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
+int tma_np(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
   constexpr int CAP = nst_cap(BITS, SW), HALF = nst_half(BITS, SW);
-  if (a.M <= 4) return launch_tma<BITS, GS, 1, CAP, SCB, SW, false>(a, qw, qz, sc, st);
   if (a.xg)   // activations staged in global memory: full ring, no staging area
-    return a.M <= 8 ? launch_tma<BITS, GS, 2, CAP, SCB, SW, true>(a, qw, qz, sc, st)
-                    : launch_tma<BITS, GS, 4, CAP, SCB, SW, true>(a, qw, qz, sc, st);
-  if (a.M <= 8)
+    return launch_tma<BITS, GS, 4, CAP, SCB, SW, true>(a, qw, qz, sc, st);
+  if (a.M <= 2) return launch_tma<BITS, GS, 1, CAP, SCB, SW, false>(a, qw, qz, sc, st);
+  if (a.M <= 4)
     return a.nst == CAP ? launch_tma<BITS, GS, 2, CAP, SCB, SW, false>(a, qw, qz, sc, st)
                         : launch_tma<BITS, GS, 2, HALF, SCB, SW, false>(a, qw, qz, sc, st);
   return a.nst == CAP ? launch_tma<BITS, GS, 4, CAP, SCB, SW, false>(a, qw, qz, sc, st)
@@ -591,8 +625,8 @@ int tma_nq(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const v
 template <int BITS, int GS>
 int tma_mt(const TmaGemvArgs& a, const uint32_t* qw, const uint32_t* qz, const void* sc, cudaStream_t st) {
   if (a.sc_dtype == QL_F32)
-    return a.sw == 8 ? tma_nq<BITS, GS, 8, 4>(a, qw, qz, sc, st) : tma_nq<BITS, GS, 4, 4>(a, qw, qz, sc, st);
-  return a.sw == 8 ? tma_nq<BITS, GS, 8, 2>(a, qw, qz, sc, st) : tma_nq<BITS, GS, 4, 2>(a, qw, qz, sc, st);
+    return a.sw == 8 ? tma_np<BITS, GS, 8, 4>(a, qw, qz, sc, st) : tma_np<BITS, GS, 4, 4>(a, qw, qz, sc, st);
+  return a.sw == 8 ? tma_np<BITS, GS, 8, 2>(a, qw, qz, sc, st) : tma_np<BITS, GS, 4, 2>(a, qw, qz, sc, st);
 }
 
 template <int BITS>
@@ -604,11 +638,11 @@ int tma_gs(const TmaGemvArgs& a, int kgs, const uint32_t* qw, const uint32_t* qz
   }
 }
 
-// Tile width (a.sw), cluster size (a.cs, the K split) and ring depth (a.nst): the CTA count
-// tiles * zdim * cs should fill resident waves of the SMs as evenly as possible (the busiest SM
-// sets the time), two CTAs per SM where their shared memory allows (a shallower ring is
-// preferred to a single CTA per SM); the wider tile and the deeper ring win ties.
-void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_sm, int max_cluster, int bits,
+// Tile width (a.sw), cluster size (a.cs, the K split) and ring depth (a.nst) for CTAs of m
+// tokens: the CTA count tiles * zdim * cs should fill resident waves of the SMs as evenly as
+// possible, two CTAs per SM where their shared memory allows (a shallower ring is preferred to a
+// single CTA per SM); the wider tile and the deeper ring win ties.
+void choose_split(TmaGemvArgs& a, int N, int m, int zdim, int sms, int ctas_per_sm, int max_cluster, int bits,
                   int kgs, int scb, bool xp) {
   int cs = 1, sw = 8, nst = nst_cap(bits, 8);
   double best = -1.0;
@@ -616,9 +650,9 @@ void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_
   for (int w = 8; w >= 4; w /= 2) {
     const int tiles = (N + 32 * w - 1) / (32 * w) * zdim;
     const int cap = nst_cap(bits, w), half = nst_half(bits, w);
-    for (int ns = cap; ns >= half; ns = (ns == cap && M > 4 && half < cap && !xp) ? half : 0) {
+    for (int ns = cap; ns >= half; ns = (ns == cap && m > 2 && half < cap && !xp) ? half : 0) {
       for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, M, a.nstage, xp);
+        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, m, a.nstage, xp);
         if (sm > (size_t)kMaxSmem) continue;
         const int fit = (int)(per_sm / (sm + 1024 + 256));
         const int per = fit < ctas_per_sm ? fit : ctas_per_sm;
@@ -644,18 +678,23 @@ void choose_split(TmaGemvArgs& a, int N, int M, int zdim, int sms, int ctas_per_
   a.nst = nst;
 }
 
-}  // namespace
-
-// Returns true (and the launch status in *rc) when the TMA-fed GEMV handles this shape.
-// Bytes of global staging a dense call of M tokens needs (0 when it stages in shared memory): one
-// chunk of 8 or 16 tokens, B operand of all K plus group sums, then one exponent per token.
-size_t gemv_stage_workspace(int M, int K, int kgs) {
-  if (M <= 4 || M > 16) return 0;
-  const int maxm = M <= 8 ? 8 : 16;
-  const size_t body = (size_t)K * gemv::xb_slots(2 * maxm) + (size_t)(K / kgs) * maxm * 4;
-  return ((body + 255) & ~(size_t)255) + (size_t)maxm * 4;
+// Bytes of one token chunk of the global staging (B operand of all K, then the group sums and
+// factors), 256-byte aligned.
+size_t stage_chunk_bytes(int K, int kgs) {
+  const size_t body = (size_t)K * gemv::xb3_slots(kXpTokens) + (size_t)(K / kgs) * 3 * kXpTokens * 4;
+  return (body + 255) & ~(size_t)255;
 }
 
+}  // namespace
+
+// Bytes of global staging a dense call of M tokens needs (0 when it stages in shared memory):
+// one chunk per kXpTokens tokens.
+size_t gemv_stage_workspace(int M, int K, int kgs) {
+  if (M <= 4 || M > 16) return 0;
+  return (size_t)((M + kXpTokens - 1) / kXpTokens) * stage_chunk_bytes(K, kgs);
+}
+
+// Returns true (and the launch status in *rc) when the TMA-fed GEMV handles this shape.
 // Dense GEMV of M <= 16 tokens. More than 4 tokens: the activations are staged once in global
 // memory (the caller's workspace when it is large enough, else the stream-ordered allocator).
 bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
@@ -673,7 +712,7 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
-  if (!enabled || N % 32 != 0 || K % kStageK != 0 || (gs % 128 != 0 && gs != 32 && gs != 64)) return false;
+  if (!enabled || M > 16 || N % 32 != 0 || K % kStageK != 0 || (gs % 128 != 0 && gs != 32 && gs != 64)) return false;
   if ((reinterpret_cast<uintptr_t>(qweight) & 15) || (reinterpret_cast<uintptr_t>(qzeros) & 15) ||
       (reinterpret_cast<uintptr_t>(scales) & 15))
     return false;
@@ -687,28 +726,27 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
-  static int prestage = -1;
-  if (prestage < 0) prestage = env_int("QL_GEMV_PRESTAGE", 1);
-  const size_t need = prestage ? gemv_stage_workspace(M, K, kgs) : 0;
+  const size_t need = gemv_stage_workspace(M, K, kgs);
   void* ws = nullptr;
   bool owned = false;
   if (need) {
     if (workspace && ws_bytes >= need) {
       ws = workspace;
     } else {
-      const int arc = cuda_status(cudaMallocAsync(&ws, need, st), "cudaMallocAsync(gemv staging)");
+      const int arc = stream_alloc(&ws, need, st, "ql_gptq_matmul: decode staging");
       if (arc) {
         *rc = arc;
         return true;
       }
       owned = true;
     }
-    const int maxm = M <= 8 ? 8 : 16;
     a.xg = reinterpret_cast<const uint8_t*>(ws);
-    a.xg_sum_off = (long)K * gemv::xb_slots(2 * maxm);
-    a.xe = reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(ws) + need - (size_t)maxm * 4);
+    a.xg_chunk = (long)stage_chunk_bytes(K, kgs);
+    a.xg_sum_off = (long)K * gemv::xb3_slots(kXpTokens);
   }
-  choose_split(a, N, M, 1, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2, need != 0);
+  const int zdim = need ? (M + kXpTokens - 1) / kXpTokens : 1;
+  choose_split(a, N, need ? kXpTokens : M, zdim, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2,
+               need != 0);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
   const uint32_t* qz = reinterpret_cast<const uint32_t*>(qzeros);
   int r = bits == 4 ? tma_gs<4>(a, kgs, qw, qz, scales, st) : tma_gs<8>(a, kgs, qw, qz, scales, st);
@@ -725,7 +763,7 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   return true;
 }
 
-// Grouped (MoE) form: one launch over the tiles of a device-built table (tile_rows = 4, 8 or 16
+// Grouped (MoE) form: one launch over the tiles of a device-built table (tile_rows = 4 or 8
 // rows of one expert per tile) for stacked weights (qweight [E][K/per][N], qzeros
 // [E][K/gs][N/per], scales [E][K/gs][N]); output row p of expert e's sorted rows is
 // x[x_rows[p]] (x[p] when x_rows is NULL) @ W_e.
@@ -739,7 +777,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (env_int("QL_GEMV_TMA", 1) == 0 || N % 32 != 0 || K % kStageK != 0 || (gs % 128 != 0 && gs != 32 && gs != 64))
     return false;
-  if ((tile_rows != 4 && tile_rows != 8 && tile_rows != 16) || !tiles || !n_tiles || max_tiles <= 0) return false;
+  if ((tile_rows != 4 && tile_rows != 8) || !tiles || !n_tiles || max_tiles <= 0) return false;
   if ((reinterpret_cast<uintptr_t>(qweight) & 15) || (reinterpret_cast<uintptr_t>(qzeros) & 15) ||
       (reinterpret_cast<uintptr_t>(scales) & 15))
     return false;
@@ -751,7 +789,7 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
   a.x_vec = ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % vec_elems == 0);
   a.sc_dtype = sc_dtype; a.bias = nullptr;
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
-  a.M = tile_rows;   // rows per tile (selects NQ, sizes smem)
+  a.M = tile_rows;   // rows per tile (selects NP, sizes smem)
   a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
   a.g_offsets = offsets; a.g_tiles = tiles; a.g_n_tiles = n_tiles;

@@ -488,13 +488,13 @@ extern "C" int ql_moe_tile_rows(long P, int E, int K, int gs, int max_rows_per_e
   if (grouped_uses_gemm(P, E, K, gs)) return gemm_tile_rows(P, E);
   static int forced = -1;
   if (forced < 0) forced = env_int("QL_MOE_GEMV_TILE", 0);
-  if (forced == 4 || forced == 8 || forced == 16) return forced;
+  if (forced == 4 || forced == 8) return forced;
   // decode GEMV: tiles of about twice the average rows per active expert (an expert with more
   // rows takes several tiles, whose weight reads mostly hit L2), at most the bound on rows
   const long act = P < E ? P : E;
   const long avg2 = act > 0 ? 2 * ((P + act - 1) / act) : 0;
   const long rows = avg2 < max_rows_per_expert ? avg2 : max_rows_per_expert;
-  return rows <= 4 ? 4 : rows <= 8 ? 8 : 16;
+  return rows <= 4 ? 4 : 8;
 }
 
 extern "C" size_t ql_moe_grouped_workspace(long P, int E, int K, int gs) {

@@ -380,7 +380,9 @@ int q4k_gemv(const void* x, int x_dtype, long ldx, const uint8_t* raw, const flo
 
 namespace ql {
 bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
-                  int out_dtype, long ldo, int M, int K, int N, cudaStream_t st, int* rc);
+                  int out_dtype, long ldo, int M, int K, int N, cudaStream_t st, int* rc, void* workspace,
+                  size_t ws_bytes);
+size_t q4k_stage_workspace(int M, int K);
 }
 
 using namespace ql;
@@ -396,8 +398,9 @@ extern "C" int ql_q4k_dequant(const uint8_t* raw, float* W, int N, int K, void* 
   return cuda_status(cudaGetLastError(), "ql_q4k_dequant launch");
 }
 
-extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
-                             int out_dtype, long ldo, int M, int K, int N, void* stream) {
+static int q4k_matmul_impl(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
+                           int out_dtype, long ldo, int M, int K, int N, void* workspace, size_t ws_bytes,
+                           void* stream) {
   if (x_dtype < QL_F32 || x_dtype > QL_BF16 || out_dtype < QL_F32 || out_dtype > QL_BF16) {
     set_error("ql_q4k_matmul: unknown dtype code");
     return QL_ERR_ARG;
@@ -417,7 +420,7 @@ extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t
   }
   cudaStream_t st = (cudaStream_t)stream;
   int rc = QL_OK;
-  if (q4k_gemv_tma(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, st, &rc)) return rc;
+  if (q4k_gemv_tma(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, st, &rc, workspace, ws_bytes)) return rc;
   for (int m0 = 0; m0 < M; m0 += 16) {
     const int mc = (M - m0) < 16 ? (M - m0) : 16;
     const char* xb = reinterpret_cast<const char*>(x) + (long)m0 * ldx * (x_dtype == QL_F32 ? 4 : 2);
@@ -426,4 +429,20 @@ extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t
     if (rc) return rc;
   }
   return QL_OK;
+}
+
+extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
+                             int out_dtype, long ldo, int M, int K, int N, void* stream) {
+  return q4k_matmul_impl(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, nullptr, 0, stream);
+}
+
+extern "C" size_t ql_q4k_matmul_workspace(int M, int K) {
+  if (M <= 0 || K <= 0 || K % kBlkVals != 0) return 0;
+  return q4k_stage_workspace(M, K);
+}
+
+extern "C" int ql_q4k_matmul_ws(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias,
+                                void* out, int out_dtype, long ldo, int M, int K, int N, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return q4k_matmul_impl(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, workspace, workspace_bytes, stream);
 }

@@ -13,18 +13,20 @@
 //
 // Arithmetic: mma.sync m16n8k32 with u8 weights x s8 activation bytes. The low (high) nibbles
 // of a lane's words at bytes 4t and 16 + 4t of quant group G are the A fragment of sub-block
-// 2G (2G + 1) with one mask each. Activations are staged per CTA as 15-bit integers
-// v = rint(x * 2^-e) split into two signed bytes (v = 256 hi + lo) that take two MMA columns,
-// with the exact per-sub-block sums S = sum v. Per row and token, sub-block j adds
+// 2G (2G + 1) with one mask each. Activations are staged as 23-bit integers with one
+// power-of-two exponent per token and super-block (gemv_common.cuh, stage_x3), three signed byte
+// planes in three MMA columns per token, with exact per-sub-block sums S of the staged integers.
+// Per row, token and plane pair ((b2, b1) or (0, b0)), sub-block j adds
 //   P += sc_j * (256 C_hi + C_lo)   (as exact int32 sums of sc_j C_hi and sc_j C_lo)
 //   Q += m_j * S_j                  (int32, exact)
-// and each super-block ends with acc += d * P - dmin * Q. The 16 six-bit scales and mins of a
-// row are unpacked four at a time with byte-parallel masks (get_scale_min_k4 on whole words).
+// and each super-block ends with acc += 2^e (d * P - dmin * Q); the two plane-pair lanes are
+// added (the first times 2^8) at the end. The 16 six-bit scales and mins of a row are unpacked
+// four at a time with byte-parallel masks (get_scale_min_k4 on whole words).
 //
 // Split-K runs over a thread-block cluster; partial sums go to the owning rank's shared memory
-// with st.async stores that count down its mbarrier. Groups of up to 4 * NQ tokens are
-// independent z-slices of the grid, so a 64-token batch is one launch whose slices read the
-// same weights (the first slice from HBM, the rest mostly from L2).
+// with st.async stores that count down its mbarrier. More than 4 tokens: activations staged once
+// in global memory, chunks of 8 tokens as independent z-slices of the grid (the first slice
+// reads the weights from HBM, the rest mostly from L2).
 #include <cuda.h>
 
 #include "gemv_common.cuh"
@@ -67,10 +69,9 @@ struct Q4kTmaArgs {
   int mchunk;   // tokens per z-slice
   int nst;      // ring stages (the kernel's NST)
   // activations staged in global memory (more than 4 tokens): chunk of z-slice c at
-  // xg + c * chunk_bytes (B operand of all K, then the sub-block sums at sum_off), exponents xe
+  // xg + c * chunk_bytes (B operand of all K, then the per-super-block sums at sum_off)
   const uint8_t* xg;
   long chunk_bytes, sum_off;
-  const int* xe;
 };
 
 // activation source in the form gemv::load_x8 reads
@@ -86,12 +87,12 @@ struct XSrc {
 };
 
 // Ring stage: the weights' TMA box, then with XP (activations staged in global memory) the
-// stage's B operand (8 steps x 4 lanes x kXSlots slots x 8 bytes) and sub-block sums [8][MAXM].
+// stage's B operand (8 steps x 4 lanes x kXSlots slots x 8 bytes) and its sums record.
 template <int NST, int MAXM, bool XP>
 struct Layout {
-  static constexpr int kXSlots = gemv::xb_slots(2 * MAXM);
+  static constexpr int kXSlots = gemv::xb3_slots(MAXM);
   static constexpr int kXBytes = XP ? kBlkVals * kXSlots : 0;
-  static constexpr int kSBytes = XP ? 8 * MAXM * 4 : 0;
+  static constexpr int kSBytes = XP ? q4k_sum_ints(MAXM) * 4 : 0;
   static constexpr int kStage = kStageBytes + kXBytes + kSBytes;   // a multiple of 128
   static constexpr int kBarOff = NST * kStage;
   static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier + abort flag
@@ -103,18 +104,16 @@ __device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t r
                : "memory");
 }
 
-// Two CTAs per SM: registers are allocated per pair of warps, so the 9 warps count as 10 and the
-// limit is 96 registers per thread.
-template <int NQ, int NST, bool XP>
+// NP MMA tiles of two tokens each. Two CTAs per SM: registers are allocated per pair of warps,
+// so the 9 warps count as 10 and the limit is 96 registers per thread.
+template <int NP, int NST, bool XP>
 __global__ void __launch_bounds__(kThreads, 2)
     q4k_gemv_tma_kernel(const __grid_constant__ CUtensorMap tmap, const Q4kTmaArgs a) {
-  constexpr int MAXM = 4 * NQ;
+  constexpr int MAXM = 2 * NP;
   using L = Layout<NST, MAXM, XP>;
   static_assert(L::kStage % 128 == 0, "stage alignment");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ int sh_exp[16];
-  __shared__ unsigned sh_max[16];
   const uint32_t sbase = ptx::smem_addr(smem);
   const uint32_t bar_full = sbase + L::kBarOff;
   const uint32_t bar_empty = bar_full + 8 * NST;
@@ -130,18 +129,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int b0 = rank * bq + min(rank, brem);
   const int nbl = bq + (rank < brem ? 1 : 0);
   const int nbl_max = bq + (brem ? 1 : 0);
-  // staged activations: B rows of sstride slots (swizzled), sub-block sums gstride ints apart
-  // (2 mod 8: the 4 tokens' pairs of sums a warp reads at once sit in distinct banks)
-  constexpr bool SWZ = NQ > 1;   // swizzled B rows (more than 4 tokens)
-  const int sstride = XP ? L::kXSlots : (SWZ ? gemv::xb_slots(2 * M) : 2 * M);
+  // staged activations (without XP): B rows of sstride slots; sub-block sums [2 M rows][gstride]
+  // (row 2m: S of v1, 2m + 1: S of b0); factors [M][nbl_max] (fe bits per super-block)
+  const int sstride = XP ? L::kXSlots : gemv::xb3_slots(M);
   const int gstride = nbl_max * 8 + 2;
   uint2* xb = reinterpret_cast<uint2*>(smem + L::kXsOff);
   const int xs_bytes = XP ? 0 : (nbl_max * kBlkVals * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
-  const int gs_bytes = XP ? 0 : (M * gstride * 4 + 15) & ~15;
+  const int gs_bytes = XP ? 0 : (2 * M * gstride * 4 + 15) & ~15;
+  int* gexp = gsum + gs_bytes / 4;
+  const int ge_bytes = XP ? 0 : (M * nbl_max * 4 + 15) & ~15;
   // split-K partials received by this rank: [cs ranks][MAXM tokens][rows_max rows]; rank q
   // owns the CTA rows [orow(q), orow(q + 1)), orow(q) = ceil(q * kRows / cs)
-  float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
+  float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes + ge_bytes);
   const int rows_max = (kRows + cs - 1) / cs;
   const int or0 = (rank * kRows + cs - 1) / cs, or1 = ((rank + 1) * kRows + cs - 1) / cs;
 
@@ -155,7 +155,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     ptx::fence_mbar_init();
     if (cs > 1) ptx::mbar_arrive_expect_tx(bar_red, (uint32_t)(cs * M * (or1 - or0) * 4));
   }
-  if (tid < 16) sh_max[tid] = 0u;
   __syncthreads();
   if (cs > 1) cluster_arrive_relaxed();   // waited for before the first remote store
 
@@ -193,26 +192,32 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (cs > 1) cluster_wait_acquire();   // pairs with the arrive above (every thread once)
   } else {
     // ------------------------------------------------------------ consumer warps
-    // Lane (g, t): MMA rows g / g + 8 are CTA rows 16 w + g / 16 w + g + 8; MMA columns 2t /
-    // 2t + 1 are the high / low activation bytes of token 4 mq + t of each token quad mq.
+    // Lane (g, t): MMA rows g / g + 8 are CTA rows 16 w + g / 16 w + g + 8. In MMA tile mq, B
+    // columns 4u .. 4u + 3 hold b2, b1, 0, b0 of token 2 mq + u; the lane's D columns 2t, 2t + 1
+    // are the plane pair t % 2 ((b2, b1) or (0, b0)) of token 2 mq + t / 2.
     const int g = lane >> 2, t = lane & 3;
-    const int slots = 2 * M;
+    const int ptok = t >> 1, pp = t & 1;
+    const int btok = g >> 2, bpl = (g & 3) == 3 ? 2 : (g & 3);
+    const bool bld = (g & 3) != 2;
     pdl_wait();   // x may be the previous kernel's output
     if constexpr (!XP) {
       const XSrc xsrc{reinterpret_cast<const char*>(a.x) + (size_t)tok0 * a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u),
                       nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, M, 0};
       // int8 staging order = natural K order: a 32-K step's B fragment (t) holds K 4t .. 4t + 3
-      // and 16 + 4t .. 16 + 4t + 3; the sums are per 32 values, one Q4_K sub-block
-      gemv::stage_x_i8<8, 32, true, SWZ>(xsrc, b0 * kBlkVals, nbl * kBlkVals, gstride, sstride, xb, gsum, sh_exp,
-                                         sh_max, tid, kCW * 32);
+      // and 16 + 4t .. 16 + 4t + 3; sums per 32 values (one sub-block), exponents per super-block
+      auto sums = [&](int m, int sb, int s1, int s0v) {
+        gsum[(2 * m) * gstride + sb] = s1;
+        gsum[(2 * m + 1) * gstride + sb] = s0v;
+      };
+      auto expo = [&](int m, int b, float fe) { gexp[m * nbl_max + b] = __float_as_int(fe); };
+      gemv::stage_x3<8, 32, 256, true>(xsrc, b0 * kBlkVals, nbl * kBlkVals, sstride, xb, sums, expo, tid, kCW * 32);
     }
 
-    float acc[NQ][2];
+    float acc[NP][2];
 #pragma unroll
-    for (int mq = 0; mq < NQ; ++mq) acc[mq][0] = acc[mq][1] = 0.f;
+    for (int mq = 0; mq < NP; ++mq) acc[mq][0] = acc[mq][1] = 0.f;
     const int r0 = warp * 16 + g;
     const uint32_t xb_base = ptx::smem_addr(xb);
-    const int swz = SWZ ? gemv::xb_swz(sstride, t) : 0;
     for (int i = 0; i < nbl; ++i) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
@@ -228,12 +233,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t mn0[2] = {h0.z & 0x3F3F3F3Fu, ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u)};
       const uint32_t sc1[2] = {h1.y & 0x3F3F3F3Fu, (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u)};
       const uint32_t mn1[2] = {h1.z & 0x3F3F3F3Fu, ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u)};
-      // exact int32 sums over the super-block, per token quad and row (0 / 1 = r0 / r0 + 8):
+      // exact int32 sums over the super-block, per token tile and row (0 / 1 = r0 / r0 + 8):
       //   PH / PL = 16 * sum_j sc_j * C_hi / C_lo (|.| < 2^29), Q = sum_j m_j * S_j (|.| < 2^28);
       // odd sub-blocks enter the MMA as 16 q, even ones as q with their scale taken 16 times
-      int PH[NQ][2], PL[NQ][2], Q[NQ][2];
+      int PH[NP][2], PL[NP][2], Q[NP][2];
 #pragma unroll
-      for (int mq = 0; mq < NQ; ++mq)
+      for (int mq = 0; mq < NP; ++mq)
 #pragma unroll
         for (int r = 0; r < 2; ++r) PH[mq][r] = PL[mq][r] = Q[mq][r] = 0;
 #pragma unroll
@@ -242,14 +247,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t w01 = *reinterpret_cast<const uint32_t*>(p0 + 32 + 32 * G + 4 * t);
         const uint32_t w10 = *reinterpret_cast<const uint32_t*>(p1 + 16 + 32 * G + 4 * t);
         const uint32_t w11 = *reinterpret_cast<const uint32_t*>(p1 + 32 + 32 * G + 4 * t);
-        int2 S2[NQ];   // sums of sub-blocks 2G, 2G + 1 for token 4 mq + t
+        int2 S2[NP];   // sums of sub-blocks 2G, 2G + 1 for the lane's token and plane pair
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq) {
-          const int tok = 4 * mq + t;
+        for (int mq = 0; mq < NP; ++mq) {
+          const int tok = 2 * mq + ptok;
           if constexpr (XP)
-            S2[mq] = tok < M ? make_int2(sstage[(2 * G) * MAXM + tok], sstage[(2 * G + 1) * MAXM + tok]) : make_int2(0, 0);
+            S2[mq] = tok < M ? make_int2(sstage[(4 * G + pp) * MAXM + tok], sstage[(4 * G + 2 + pp) * MAXM + tok])
+                             : make_int2(0, 0);
           else
-            S2[mq] = tok < M ? *reinterpret_cast<const int2*>(gsum + tok * gstride + i * 8 + 2 * G) : make_int2(0, 0);
+            S2[mq] = tok < M ? *reinterpret_cast<const int2*>(gsum + (2 * tok + pp) * gstride + i * 8 + 2 * G)
+                             : make_int2(0, 0);
         }
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -262,11 +269,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int m0 = (int)__byte_perm(mn0[j >> 2], 0u, 0x4440u + (j & 3));
           const int m1 = (int)__byte_perm(mn1[j >> 2], 0u, 0x4440u + (j & 3));
 #pragma unroll
-          for (int mq = 0; mq < NQ; ++mq) {
-            const int slot = 8 * mq + g;
+          for (int mq = 0; mq < NP; ++mq) {
+            const int btk = 2 * mq + btok;
             uint32_t b0 = 0u, b1 = 0u;
-            if (slot < slots) {
-              const uint32_t xa = xstage + ((j * 4 + t) * sstride + (slot ^ swz)) * 8;
+            if (bld && btk < M) {
+              const uint32_t xa = xstage + ((j * 4 + t) * sstride + 3 * btk + bpl) * 8;
               asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(xa));
             }
             int d[4] = {0, 0, 0, 0};
@@ -284,36 +291,37 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float2 dd0 = __half22float2(u32_as_h2(h0.x));   // (d, dmin) of row r0
       const float2 dd1 = __half22float2(u32_as_h2(h1.x));   // and of row r0 + 8
 #pragma unroll
-      for (int mq = 0; mq < NQ; ++mq) {
+      for (int mq = 0; mq < NP; ++mq) {
+        const int tok = 2 * mq + ptok;
+        float fe = 0.f;
+        if (tok < M) fe = __int_as_float(XP ? sstage[16 * MAXM + tok] : gexp[tok * nbl_max + i]);
         const float P0 = 0.0625f * fmaf(256.f, (float)PH[mq][0], (float)PL[mq][0]);
         const float P1 = 0.0625f * fmaf(256.f, (float)PH[mq][1], (float)PL[mq][1]);
-        acc[mq][0] = fmaf(dd0.x, P0, fmaf(-dd0.y, (float)Q[mq][0], acc[mq][0]));
-        acc[mq][1] = fmaf(dd1.x, P1, fmaf(-dd1.y, (float)Q[mq][1], acc[mq][1]));
+        acc[mq][0] = fmaf(dd0.x * fe, P0, fmaf(-dd0.y * fe, (float)Q[mq][0], acc[mq][0]));
+        acc[mq][1] = fmaf(dd1.x * fe, P1, fmaf(-dd1.y * fe, (float)Q[mq][1], acc[mq][1]));
       }
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_empty + 8 * s);
     }
 
-    // non-finite activation rows give NaN (the integer staging cannot carry inf / nan)
-    auto finish = [&](int tok, float v) {
-      if constexpr (XP) {
-        const int e = a.xe[tok0 + tok];
-        return e != gemv::kNonFinite ? v * exp2i(e) : __int_as_float(0x7fc00000);
-      } else {
-        const float mx = __uint_as_float(sh_max[tok]);
-        return mx < 3.0e38f ? v * exp2i(sh_exp[tok]) : __int_as_float(0x7fc00000);
+    // the (b2, b1) lane's sums count 2^8 times the (0, b0) lane's; add the pair (exact scaling)
+#pragma unroll
+    for (int mq = 0; mq < NP; ++mq)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float v = pp ? acc[mq][h] : 256.f * acc[mq][h];
+        acc[mq][h] = v + __shfl_xor_sync(0xffffffffu, v, 1);
       }
-    };
     if (cs == 1) {
 #pragma unroll
-      for (int mq = 0; mq < NQ; ++mq) {
-        const int tok = 4 * mq + t;
-        if (tok < M) {
+      for (int mq = 0; mq < NP; ++mq) {
+        const int tok = 2 * mq + ptok;
+        if (pp == 0 && tok < M) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int row = blockIdx.y * kRows + r0 + 8 * h;
             if (row < a.N) {
-              float v = finish(tok, acc[mq][h]);
+              float v = acc[mq][h];
               if (a.bias) v += a.bias[row];
               store_from_float(a.out, a.out_dtype, (long)(tok0 + tok) * a.ldo + row, v);
             }
@@ -331,9 +339,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t rb = ptx::mapa(ptx::smem_addr(red), owner);
         const uint32_t rbar = ptx::mapa(bar_red, owner);
 #pragma unroll
-        for (int mq = 0; mq < NQ; ++mq) {
-          const int tok = 4 * mq + t;
-          if (tok < M) st_async_f32(rb + ((rank * MAXM + tok) * rows_max + (r - orow)) * 4, finish(tok, acc[mq][h]), rbar);
+        for (int mq = 0; mq < NP; ++mq) {
+          const int tok = 2 * mq + ptok;
+          if (pp == 0 && tok < M) st_async_f32(rb + ((rank * MAXM + tok) * rows_max + (r - orow)) * 4, acc[mq][h], rbar);
         }
       }
     }
@@ -376,22 +384,25 @@ EncodeTiledFn encode_fn() {
 }
 
 constexpr int kNST = 4;
+constexpr int kXpTokens = 8;   // tokens per z-slice when the activations are staged in global memory
 
-// dynamic shared memory of one CTA with an nst-stage ring, as the kernel carves it up (xp:
-// activations staged in global memory and carried by the ring)
-size_t smem_bytes(int mchunk, int nb, int cs, int nq, int nst, bool xp) {
+// dynamic shared memory of one CTA with an nst-stage ring for z-slices of mchunk tokens, as the
+// kernel carves it up (xp: activations staged in global memory and carried by the ring)
+size_t smem_bytes(int mchunk, int nb, int cs, int nst, bool xp) {
   const int nbl_max = (nb + cs - 1) / cs;
-  const size_t red = cs > 1 ? (size_t)cs * 4 * nq * ((kRows + cs - 1) / cs) * 4 : 0;
+  const int maxm = xp ? kXpTokens : (mchunk <= 2 ? 2 : 4);
+  const size_t red = cs > 1 ? (size_t)cs * maxm * ((kRows + cs - 1) / cs) * 4 : 0;
   if (xp) {
-    const size_t stage = kStageBytes + (size_t)kBlkVals * gemv::xb_slots(8 * nq) + 8 * 4 * nq * 4;
+    const size_t stage = kStageBytes + (size_t)kBlkVals * gemv::xb3_slots(kXpTokens) + q4k_sum_ints(kXpTokens) * 4;
     return 1024 + (size_t)nst * stage + 2 * nst * 8 + 16 + red;
   }
-  const size_t xs = ((size_t)nbl_max * kBlkVals * gemv::xb_slots(2 * mchunk) + 15) & ~(size_t)15;
-  const size_t gsb = ((size_t)mchunk * (nbl_max * 8 + 2) * 4 + 15) & ~(size_t)15;
-  return 1024 + (size_t)nst * kStageBytes + 2 * nst * 8 + 16 + xs + gsb + red;
+  const size_t xs = ((size_t)nbl_max * kBlkVals * gemv::xb3_slots(mchunk) + 15) & ~(size_t)15;
+  const size_t gsb = ((size_t)2 * mchunk * (nbl_max * 8 + 2) * 4 + 15) & ~(size_t)15;
+  const size_t geb = ((size_t)mchunk * nbl_max * 4 + 15) & ~(size_t)15;
+  return 1024 + (size_t)nst * kStageBytes + 2 * nst * 8 + 16 + xs + gsb + geb + red;
 }
 
-template <int NQ, int NST, bool XP>
+template <int NP, int NST, bool XP>
 int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return -1;
@@ -405,7 +416,7 @@ int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return -1;
-  auto kern = q4k_gemv_tma_kernel<NQ, NST, XP>;
+  auto kern = q4k_gemv_tma_kernel<NP, NST, XP>;
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -421,10 +432,10 @@ int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.cs, (a.N + kRows - 1) / kRows, (a.M + a.mchunk - 1) / a.mchunk);
   if constexpr (XP) {
-    // stage the activations once: one CTA per token row, chunks of 4 NQ tokens
+    // stage the activations once: one CTA per token row, chunks of kXpTokens tokens
     const XSrc xsrc{a.x, nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, a.M, 0};
-    prestage_x_kernel<8, 32, 4 * NQ><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg), a.chunk_bytes,
-                                                         a.sum_off, const_cast<int*>(a.xe));
+    prestage_x3_kernel<8, 32, 256, kXpTokens, 1><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg),
+                                                                      a.chunk_bytes, a.sum_off);
     const int rc = cuda_status(cudaGetLastError(), "q4k prestage launch");
     if (rc) return rc;
   }
@@ -449,16 +460,25 @@ int launch(const Q4kTmaArgs& a, const uint8_t* raw, size_t smem, cudaStream_t st
 
 }  // namespace
 
+// Bytes of the global activation staging of an M-token call (0 up to 4 tokens).
+size_t q4k_stage_workspace(int M, int K) {
+  if (M <= 4) return 0;
+  const long sum_off = (long)K * gemv::xb3_slots(kXpTokens);
+  const long chunk = (sum_off + (long)(K / kBlkVals) * q4k_sum_ints(kXpTokens) * 4 + 255) & ~255L;
+  return (size_t)((M + kXpTokens - 1) / kXpTokens) * (size_t)chunk;
+}
+
 // Returns true (and the launch status in *rc) when the TMA-fed kernel takes this call.
-// Token chunk (tokens per z-slice, 4 NQ at most) and cluster size are chosen so the CTAs fill
-// whole resident waves of the SMs as evenly as possible, two CTAs per SM where they fit.
+// Up to 4 tokens: one z-slice that stages its own activations; more: activations staged once in
+// global memory (the caller's workspace when large enough, else the stream-ordered allocator),
+// z-slices of 8 tokens. The cluster size is chosen so the CTAs fill whole resident waves of the
+// SMs as evenly as possible, two CTAs per SM where they fit.
 bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
-                  int out_dtype, long ldo, int M, int K, int N, cudaStream_t st, int* rc) {
-  static int enabled = -1, sms = 0, chunk_max = 8;
+                  int out_dtype, long ldo, int M, int K, int N, cudaStream_t st, int* rc, void* workspace,
+                  size_t ws_bytes) {
+  static int enabled = -1, sms = 0;
   if (enabled < 0) {
     enabled = env_int("QL_Q4K_TMA", 1);
-    chunk_max = env_int("QL_Q4K_CHUNK", 8);
-    if (chunk_max != 4 && chunk_max != 16) chunk_max = 8;
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -472,16 +492,9 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   a.bias = bias; a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N;
   a.nb = K / kBlkVals;
-  // up to 4 tokens: one z-slice that stages its own activations; more: activations staged
-  // once in global memory (prestage_x_kernel), z-slices of 4 NQ tokens
-  static int prestage = -1;
-  if (prestage < 0) prestage = env_int("QL_Q4K_PRESTAGE", 1);
-  const bool xp = M > 4 && prestage;
-  int mchunk = M <= 4 ? 4 : (M <= 8 || chunk_max == 8 ? 8 : (chunk_max == 4 ? 4 : 16));
-  if (M > 8 && chunk_max == 4) mchunk = 4;
-  if (mchunk > M && !xp) mchunk = M;
+  const bool xp = M > 4;
+  const int mchunk = xp ? kXpTokens : M;
   a.mchunk = mchunk;
-  const int nq = (mchunk + 3) / 4;
   const int zdim = (M + mchunk - 1) / mchunk;
   const int tiles = (N + kRows - 1) / kRows * zdim;
   const size_t per_sm = 228 * 1024;   // shared memory per SM; each CTA also reserves 1 KB
@@ -489,7 +502,7 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   double best = -1.0;
   for (int ns = kNST; ns >= 2; ns -= 2) {   // ring depths built: 4 and 2
     for (int c = 1; c <= 8 && c <= a.nb; ++c) {
-      const size_t sm = smem_bytes(mchunk, a.nb, c, nq, ns, xp);
+      const size_t sm = smem_bytes(mchunk, a.nb, c, ns, xp);
       if (sm > 220 * 1024) continue;
       const int fit = (int)(per_sm / (sm + 1024 + 256));
       const int per = fit >= 2 ? 2 : fit;
@@ -511,39 +524,41 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   if (best_cs == 0) return false;
   a.cs = best_cs;
   a.nst = best_nst;
-  const size_t smem = smem_bytes(mchunk, a.nb, a.cs, nq, a.nst, xp);
+  const size_t smem = smem_bytes(mchunk, a.nb, a.cs, a.nst, xp);
   void* ws = nullptr;
+  bool owned = false;
   if (xp) {
-    // per chunk: B operand of all K (K * slots bytes), then [K / 32][4 NQ] sums; then exponents
-    a.sum_off = (long)K * gemv::xb_slots(8 * nq);
-    a.chunk_bytes = (a.sum_off + (long)(K / 32) * 4 * nq * 4 + 255) & ~255L;
-    const size_t need = (size_t)zdim * a.chunk_bytes + (size_t)M * 4;
-    const int arc = cuda_status(cudaMallocAsync(&ws, need, st), "cudaMallocAsync(q4k staging)");
-    if (arc) {
-      *rc = arc;
-      return true;
+    // per chunk: B operand of all K (K * slots bytes), then one sums record per super-block
+    a.sum_off = (long)K * gemv::xb3_slots(kXpTokens);
+    a.chunk_bytes = (a.sum_off + (long)a.nb * q4k_sum_ints(kXpTokens) * 4 + 255) & ~255L;
+    const size_t need = q4k_stage_workspace(M, K);
+    if (workspace && ws_bytes >= need) {
+      ws = workspace;
+    } else {
+      const int arc = stream_alloc(&ws, need, st, "ql_q4k_matmul: staging");
+      if (arc) {
+        *rc = arc;
+        return true;
+      }
+      owned = true;
     }
     a.xg = reinterpret_cast<const uint8_t*>(ws);
-    a.xe = reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(ws) + (size_t)zdim * a.chunk_bytes);
   }
   int r;
   if (xp) {
-    switch (nq) {
-      case 2: r = a.nst == kNST ? launch<2, kNST, true>(a, raw, smem, st) : launch<2, 2, true>(a, raw, smem, st); break;
-      default: r = a.nst == kNST ? launch<4, kNST, true>(a, raw, smem, st) : launch<4, 2, true>(a, raw, smem, st); break;
+    r = a.nst == kNST ? launch<4, kNST, true>(a, raw, smem, st) : launch<4, 2, true>(a, raw, smem, st);
+    if (owned) {
+      const int frc = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(q4k staging)");
+      if (r == 0) r = frc;
     }
-    const int frc = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(q4k staging)");
-    if (r == 0) r = frc;
     if (r < 0) {   // declined after the staging ran: report, the register kernel would redo it
       set_error("ql_q4k_matmul: tensor-map encoding failed");
       r = QL_ERR_CUDA;
     }
+  } else if (M <= 2) {
+    r = a.nst == kNST ? launch<1, kNST, false>(a, raw, smem, st) : launch<1, 2, false>(a, raw, smem, st);
   } else {
-    switch (nq) {
-      case 1: r = a.nst == kNST ? launch<1, kNST, false>(a, raw, smem, st) : launch<1, 2, false>(a, raw, smem, st); break;
-      case 2: r = a.nst == kNST ? launch<2, kNST, false>(a, raw, smem, st) : launch<2, 2, false>(a, raw, smem, st); break;
-      default: r = a.nst == kNST ? launch<4, kNST, false>(a, raw, smem, st) : launch<4, 2, false>(a, raw, smem, st); break;
-    }
+    r = a.nst == kNST ? launch<2, kNST, false>(a, raw, smem, st) : launch<2, 2, false>(a, raw, smem, st);
   }
   if (r < 0) return false;
   *rc = r;

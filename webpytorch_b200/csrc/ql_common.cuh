@@ -27,6 +27,15 @@ int cuda_status(cudaError_t e, const char* where);
 // Launch flags set through ql_set_launch_flags (QL_LAUNCH_* bits).
 int launch_flags();
 
+// Stream-ordered scratch allocation (cudaMallocAsync) for calls given too small a workspace;
+// fails with QL_ERR_UNSUPPORTED while an AllocGuard is alive on the calling thread.
+int stream_alloc(void** p, size_t bytes, cudaStream_t st, const char* what);
+struct AllocGuard {
+  AllocGuard();
+  ~AllocGuard();
+  bool prev;
+};
+
 // Integer knob from the environment (benchmark tuning only), read once per name by the caller.
 int env_int(const char* name, int dflt);
 

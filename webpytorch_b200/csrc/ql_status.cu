@@ -27,6 +27,21 @@ static std::atomic<int> g_launch_flags{0};
 
 int launch_flags() { return g_launch_flags.load(std::memory_order_relaxed); }
 
+// Set by the allocation-free entry point for the duration of its call: every stream-ordered
+// allocation the kernels' host code would make fails instead (see stream_alloc).
+static thread_local bool g_alloc_forbidden = false;
+
+AllocGuard::AllocGuard() : prev(g_alloc_forbidden) { g_alloc_forbidden = true; }
+AllocGuard::~AllocGuard() { g_alloc_forbidden = prev; }
+
+int stream_alloc(void** p, size_t bytes, cudaStream_t st, const char* what) {
+  if (g_alloc_forbidden) {
+    set_error("%s: %zu bytes of scratch needed, but this call may not allocate", what, bytes);
+    return QL_ERR_UNSUPPORTED;
+  }
+  return cuda_status(cudaMallocAsync(p, bytes, st), what);
+}
+
 int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return (v && *v) ? atoi(v) : dflt;

@@ -102,7 +102,7 @@ class StackedExperts:
 
 def tile_rows_for(P, E, K, gs, max_rows):
     """Tile height of the routing table the grouped matmul wants for this call (32 / 64 / 128 for
-    the tensor-core GEMM, 4 / 8 / 16 for the decode GEMV)."""
+    the tensor-core GEMM, 4 or 8 for the decode GEMV)."""
     return _ffi.load().ql_moe_tile_rows(P, E, K, gs, max_rows)
 
 

@@ -65,6 +65,17 @@ def gptq_dequant(qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, g_idx=None, 
     return W
 
 
+_ws_cache = {}
+
+
+def _workspace_bytes(M, K):
+    """ql_gptq_matmul_workspace(M, K), remembered per shape."""
+    n = _ws_cache.get((M, K))
+    if n is None:
+        n = _ws_cache[(M, K)] = int(_ffi.fn("ql_gptq_matmul_workspace")(M, K))
+    return n
+
+
 def _gptq_matmul(xf, qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, *, x_perm=None, bias=None,
                  out=None, out_dtype=torch.float32, stream=None):
     """y[M, N] = xf[M, K] @ dequant(qweight, qzeros, scales) (+ bias), on the GPU.
@@ -80,7 +91,7 @@ def _gptq_matmul(xf, qweight, qzeros, scales, K, N, gs, bits, zoff=0.0, *, x_per
         out = torch.empty((M, N), dtype=out_dtype, device=xf.device)
     # calls of more than 4 tokens stage x in a workspace (the tensor-core path's fp16 copy or the
     # decode path's MMA operand); take it from torch's allocator
-    ws_bytes = _ffi.load().ql_gptq_matmul_workspace(M, K) if M > 4 else 0
+    ws_bytes = _workspace_bytes(M, K) if M > 4 else 0
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xf.device) if ws_bytes else None
     _ffi.call("ql_gptq_matmul_ws", xf.data_ptr(), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(x_perm),
               qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), _ffi.dtype_code(scales.dtype),
