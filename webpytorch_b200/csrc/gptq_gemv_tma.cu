@@ -79,6 +79,12 @@ struct TmaGemvArgs {
   int g_max_tiles;  // host: table capacity (grid z)
   int n_experts;    // host: stacked weight matrices (1 when dense)
   int glu;          // > 0: x rows are [gate | up] glu elements apart (SwiGLU applied when staging)
+  // dense calls of up to 4 tokens whose rows of x are 16-byte aligned (no gather): the producer
+  // copies the CTA's slice of x into shared memory with bulk copies ahead of the weights, so the
+  // consumers' staging reads shared memory instead of queueing behind the weight stream
+  int xbulk;
+  int xsize;      // bytes per element of x
+  int pdl;        // launched as a programmatic dependent (x copies wait for the previous kernel)
   // dense calls of more than 4 tokens: activations staged once in global memory, blockIdx.z
   // taking tokens [z * MAXM, z * MAXM + MAXM) from chunk z at xg + z * xg_chunk (the B operand
   // of all K, then per group [S1 | S0 | fe][MAXM] at xg_sum_off)
@@ -116,7 +122,7 @@ struct TmaLayout {
   static constexpr int kGBytes = XP ? GPS * 3 * MAXM * 4 : 0;
   static constexpr int kStageBytes = (kWSZBytes + kXBytes + kGBytes + 1023) & ~1023;
   static constexpr int kBarOff = NST * kStageBytes;
-  static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier, abort flag
+  static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 32;   // + abort flag, reduction and x barriers
 };
 
 // NP MMA tiles of two tokens each (MAXM = 2 NP tokens per CTA).
@@ -141,6 +147,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_empty = bar_full + 8 * NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kBarOff + 16 * NST);
   const uint32_t bar_red = bar_full + 16 * NST + 8;   // partial sums received from the cluster
+  const uint32_t bar_x = bar_full + 16 * NST + 16;    // the bulk copy of x (xbulk)
 
   // which rows this CTA takes: grouped mode reads the tile table (uniform over the cluster,
   // which shares blockIdx.z; slots without rows leave before any barrier), dense calls of more
@@ -177,7 +184,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int xs_bytes = XP ? 0 : (klen_max * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
   const int gs_bytes = XP ? 0 : (3 * M * gstride * 4 + 15) & ~15;
-  float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes);
+  // xbulk: the raw rows of x for this CTA's K slice, klen_max elements apart
+  unsigned char* xraw = smem + L::kXsOff + xs_bytes + gs_bytes;
+  const int xr_bytes = a.xbulk ? (M * klen_max * a.xsize + 15) & ~15 : 0;
+  float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes + xr_bytes);
   // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16 (only
   // with cs > 1); kred: K-way partials (KW == 2), [SW * 32 lanes][NP * 4]
   float* kred = red + (a.cs > 1 ? (TC + 64) * MAXM : 0);
@@ -196,12 +206,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::mbar_init(bar_empty + 8 * s, SW);
     }
     ptx::mbar_init(bar_red, 1);
+    ptx::mbar_init(bar_x, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     if (cs > 1) ptx::mbar_arrive_expect_tx(bar_red, (uint32_t)(cs * M * (oq1 - oq0) * 16));
   }
   __syncthreads();
   if (cs > 1) cluster_arrive_relaxed();   // waited for before the first remote store
+
+  // the bulk copy of this CTA's x slice (one copy per token row)
+  auto copy_x = [&]() {
+    pdl_wait();   // x may be the previous kernel's output
+    const uint32_t row_bytes = (uint32_t)(klen * a.xsize);
+    ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)M * row_bytes);
+    const char* xs = reinterpret_cast<const char*>(a.x) + (size_t)s0 * kStageK * a.xsize;
+    for (int m = 0; m < M; ++m)
+      ptx::bulk_load(ptx::smem_addr(xraw + (size_t)m * klen_max * a.xsize), xs + (size_t)(row0 + m) * a.ldx * a.xsize,
+                     row_bytes, bar_x);
+  };
 
   if (warp == kCW) {
     // ------------------------------------------------------------ producer warp
@@ -212,6 +234,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int strip0 = blockIdx.y * SW;
       const int wrow0 = e * a.g_wrows, grow0 = e * a.g_grows;   // expert's first rows (0 when dense)
       if (XP) pdl_wait();   // the staged activations are the previous kernel's output
+      // x goes first into the memory queue, unless this grid may start before the previous
+      // kernel ends: then the weights (independent of it) go first and x after the ring's fill
+      const bool x_first = a.xbulk && !a.pdl;
+      const int x_after = a.xbulk && a.pdl ? min(NST, nst) - 1 : -1;
+      if (x_first) copy_x();
       int i = 0;
       bool ok = true;
       for (; i < nst; ++i) {
@@ -237,10 +264,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           ptx::bulk_load(st + L::kWSZBytes + L::kXBytes, xgc + a.xg_sum_off + (long)(s0 + i) * L::kGBytes, L::kGBytes,
                          fb);
         }
+        if (i == x_after) copy_x();
       }
       if (nst <= NST) pdl_trigger();
       if (!ok) {
         for (int j = i > NST ? i - NST : 0; j < i; ++j) ptx::mbar_wait_drain(bar_full + 8 * (j % NST), (j / NST) & 1);
+        if (x_first || (x_after >= 0 && i > x_after)) ptx::mbar_wait_drain(bar_x, 0);
       }
     }
     __syncwarp();
@@ -264,17 +293,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int btok = gq >> 2, bpl = (gq & 3) == 3 ? 2 : (gq & 3);
     const bool bld = (gq & 3) != 2;
     pdl_wait();   // x may be the previous kernel's output
+    bool x_ok = true;
     if constexpr (!XP) {
-      // this CTA's rows: gathered through x_rows, else x itself from row row0 on
-      const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
-      const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
-                      a.ldx, a.x_dtype, a.x_vec, M, a.glu};
       auto sums = [&](int m, int g, int s1, int s0v) {
         gsum[(3 * m) * gstride + g] = s1;
         gsum[(3 * m + 1) * gstride + g] = s0v;
       };
       auto expo = [&](int m, int g, float fe) { gsum[(3 * m + 2) * gstride + g] = __float_as_int(fe); };
-      gemv::stage_x3<BITS, GS, GS, true>(xsrc, s0 * kStageK, klen, sstride, xb, sums, expo, tid, kCW * 32);
+      if (a.xbulk) {
+        // the slice of x arrives in shared memory by bulk copy; stage it from there
+        x_ok = ptx::mbar_wait(bar_x, 0, abort_flag);
+        const XSrc xsrc{xraw, nullptr, nullptr, klen_max, a.x_dtype, 1, M, 0};
+        gemv::stage_x3<BITS, GS, GS, true>(xsrc, 0, x_ok ? klen : 0, sstride, xb, sums, expo, tid, kCW * 32);
+      } else {
+        // this CTA's rows: gathered through x_rows, else x itself from row row0 on
+        const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
+        const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
+                        a.ldx, a.x_dtype, a.x_vec, M, a.glu};
+        gemv::stage_x3<BITS, GS, GS, true>(xsrc, s0 * kStageK, klen, sstride, xb, sums, expo, tid, kCW * 32);
+      }
     }
 
     float acc[NP][4];
@@ -285,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     const uint32_t strip_off = strip * L::kStripBytes;
     const uint32_t xb_base = ptx::smem_addr(xb);
-    for (int i = kway; i < nst; i += KW) {
+    for (int i = kway; i < (x_ok ? nst : 0); i += KW) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
       const uint32_t st = sbase + s * L::kStageBytes;
@@ -518,8 +555,9 @@ constexpr int kXpTokens = 8;   // tokens per CTA when the activations are staged
 // Dynamic shared memory of one CTA (ring of nst = NST stages) that takes m tokens, as the
 // kernel's prologue carves it up: 1 KB of alignment slack, the ring, the barriers, the staged
 // activations and their group sums / factors (unless xp: then each stage carries its own), the
+// raw slice of x when it arrives by bulk copy (xbulk_size = bytes per element, else 0), the
 // split-K receive buffer (cs > 1) and the K-way hand-off (128-column tiles).
-size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int nstage, bool xp) {
+size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int nstage, bool xp, int xbulk_size = 0) {
   const int per = 32 / bits, tc = 32 * sw, gps = kStageK / kgs, rows = kStageK / per;
   const int np = xp ? kXpTokens / 2 : np_of(m), maxm = 2 * np;
   const size_t wsz = ((size_t)sw * rows * 128 + (size_t)gps * tc * scb + (size_t)gps * (tc / per) * 4 + 15) & ~(size_t)15;
@@ -531,6 +569,7 @@ size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int 
   if (!xp) {
     b += ((size_t)nst_max * kStageK * gemv::xb3_slots(m) + 15) & ~(size_t)15;
     b += ((size_t)3 * m * (ng_max | 1) * 4 + 15) & ~(size_t)15;
+    if (xbulk_size) b += ((size_t)m * nst_max * kStageK * xbulk_size + 15) & ~(size_t)15;
   }
   if (cs > 1) b += (size_t)(tc + 64) * maxm * 4;
   if (sw < kCW) b += (size_t)sw * 32 * np * 4 * 4;
@@ -565,7 +604,8 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
                  TC / L::PER, L::GPS))
     return -1;
   auto kern = gptq_gemv_tma_kernel<BITS, GS, NP, NST, SCB, SW, XP>;
-  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, XP ? kXpTokens : a.M, a.nstage, XP);
+  const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, XP ? kXpTokens : a.M, a.nstage, XP,
+                              a.xbulk ? a.xsize : 0);
   if (smem > kMaxSmem) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -652,7 +692,7 @@ void choose_split(TmaGemvArgs& a, int N, int m, int zdim, int sms, int ctas_per_
     const int cap = nst_cap(bits, w), half = nst_half(bits, w);
     for (int ns = cap; ns >= half; ns = (ns == cap && m > 2 && half < cap && !xp) ? half : 0) {
       for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, m, a.nstage, xp);
+        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, m, a.nstage, xp, a.xbulk ? a.xsize : 0);
         if (sm > (size_t)kMaxSmem) continue;
         const int fit = (int)(per_sm / (sm + 1024 + 256));
         const int per = fit < ctas_per_sm ? fit : ctas_per_sm;
@@ -745,6 +785,9 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
     a.xg_sum_off = (long)K * gemv::xb3_slots(kXpTokens);
   }
   const int zdim = need ? (M + kXpTokens - 1) / kXpTokens : 1;
+  a.xsize = x_dtype == QL_F32 ? 4 : 2;
+  a.pdl = (launch_flags() & QL_LAUNCH_PDL) ? 1 : 0;
+  a.xbulk = !need && x_perm == nullptr && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * a.xsize) % 16 == 0;
   choose_split(a, N, need ? kXpTokens : M, zdim, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2,
                need != 0);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);

@@ -72,6 +72,10 @@ struct Q4kTmaArgs {
   // xg + c * chunk_bytes (B operand of all K, then the per-super-block sums at sum_off)
   const uint8_t* xg;
   long chunk_bytes, sum_off;
+  // up to 4 tokens with 16-byte aligned rows of x: the producer copies the CTA's slice of x into
+  // shared memory by bulk copy ahead of the weights (xsize = bytes per element; pdl = launched
+  // as a programmatic dependent, so x is copied after the first ring fill)
+  int xbulk, xsize, pdl;
 };
 
 // activation source in the form gemv::load_x8 reads
@@ -95,7 +99,7 @@ struct Layout {
   static constexpr int kSBytes = XP ? q4k_sum_ints(MAXM) * 4 : 0;
   static constexpr int kStage = kStageBytes + kXBytes + kSBytes;   // a multiple of 128
   static constexpr int kBarOff = NST * kStage;
-  static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 16;   // + reduction barrier + abort flag
+  static constexpr int kXsOff = kBarOff + 2 * NST * 8 + 32;   // + reduction barrier, abort flag, x barrier
 };
 
 __device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
@@ -119,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t bar_empty = bar_full + 8 * NST;
   const uint32_t bar_red = bar_full + 16 * NST;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kBarOff + 16 * NST + 8);
+  const uint32_t bar_x = bar_full + 16 * NST + 16;   // the bulk copy of x (xbulk)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rank = blockIdx.x, cs = a.cs;
@@ -139,9 +144,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int gs_bytes = XP ? 0 : (2 * M * gstride * 4 + 15) & ~15;
   int* gexp = gsum + gs_bytes / 4;
   const int ge_bytes = XP ? 0 : (M * nbl_max * 4 + 15) & ~15;
+  // xbulk: the raw rows of x for this CTA's super-blocks, nbl_max * 256 elements apart
+  unsigned char* xraw = smem + L::kXsOff + xs_bytes + gs_bytes + ge_bytes;
+  const int xr_bytes = a.xbulk ? (M * nbl_max * kBlkVals * a.xsize + 15) & ~15 : 0;
   // split-K partials received by this rank: [cs ranks][MAXM tokens][rows_max rows]; rank q
   // owns the CTA rows [orow(q), orow(q + 1)), orow(q) = ceil(q * kRows / cs)
-  float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes + ge_bytes);
+  float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes + ge_bytes + xr_bytes);
   const int rows_max = (kRows + cs - 1) / cs;
   const int or0 = (rank * kRows + cs - 1) / cs, or1 = ((rank + 1) * kRows + cs - 1) / cs;
 
@@ -151,12 +159,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       ptx::mbar_init(bar_empty + 8 * s, kCW);
     }
     ptx::mbar_init(bar_red, 1);
+    ptx::mbar_init(bar_x, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     if (cs > 1) ptx::mbar_arrive_expect_tx(bar_red, (uint32_t)(cs * M * (or1 - or0) * 4));
   }
   __syncthreads();
   if (cs > 1) cluster_arrive_relaxed();   // waited for before the first remote store
+
+  // the bulk copy of this CTA's x slice (one copy per token row)
+  auto copy_x = [&]() {
+    pdl_wait();   // x may be the previous kernel's output
+    const uint32_t row_bytes = (uint32_t)(nbl * kBlkVals * a.xsize);
+    ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)M * row_bytes);
+    const char* xs = reinterpret_cast<const char*>(a.x) + (size_t)b0 * kBlkVals * a.xsize;
+    for (int m = 0; m < M; ++m)
+      ptx::bulk_load(ptx::smem_addr(xraw + (size_t)m * nbl_max * kBlkVals * a.xsize),
+                     xs + (size_t)(tok0 + m) * a.ldx * a.xsize, row_bytes, bar_x);
+  };
 
   if (warp == kCW) {
     // ------------------------------------------------------------ producer warp
@@ -165,6 +185,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int row0 = blockIdx.y * kRows;
       const uint8_t* xgc = XP ? a.xg + (long)blockIdx.z * a.chunk_bytes : nullptr;
       if (XP) pdl_wait();   // the staged activations are the previous kernel's output
+      // x goes first into the memory queue, unless this grid may start before the previous
+      // kernel ends: then the weights (independent of it) go first and x after the ring's fill
+      const bool x_first = a.xbulk && !a.pdl;
+      const int x_after = a.xbulk && a.pdl ? min(NST, nbl) - 1 : -1;
+      if (x_first) copy_x();
       int i = 0;
       bool ok = true;
       for (; i < nbl; ++i) {
@@ -182,10 +207,12 @@ __global__ void __launch_bounds__(kThreads, 2)
           ptx::bulk_load(st + kStageBytes, xgc + (long)(b0 + i) * L::kXBytes, L::kXBytes, fb);
           ptx::bulk_load(st + kStageBytes + L::kXBytes, xgc + a.sum_off + (long)(b0 + i) * L::kSBytes, L::kSBytes, fb);
         }
+        if (i == x_after) copy_x();
       }
       if (nbl <= NST) pdl_trigger();
       if (!ok) {
         for (int j = i > NST ? i - NST : 0; j < i; ++j) ptx::mbar_wait_drain(bar_full + 8 * (j % NST), (j / NST) & 1);
+        if (x_first || (x_after >= 0 && i > x_after)) ptx::mbar_wait_drain(bar_x, 0);
       }
     }
     __syncwarp();
@@ -200,9 +227,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int btok = g >> 2, bpl = (g & 3) == 3 ? 2 : (g & 3);
     const bool bld = (g & 3) != 2;
     pdl_wait();   // x may be the previous kernel's output
+    bool x_ok = true;
     if constexpr (!XP) {
-      const XSrc xsrc{reinterpret_cast<const char*>(a.x) + (size_t)tok0 * a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u),
-                      nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, M, 0};
       // int8 staging order = natural K order: a 32-K step's B fragment (t) holds K 4t .. 4t + 3
       // and 16 + 4t .. 16 + 4t + 3; sums per 32 values (one sub-block), exponents per super-block
       auto sums = [&](int m, int sb, int s1, int s0v) {
@@ -210,7 +236,16 @@ __global__ void __launch_bounds__(kThreads, 2)
         gsum[(2 * m + 1) * gstride + sb] = s0v;
       };
       auto expo = [&](int m, int b, float fe) { gexp[m * nbl_max + b] = __float_as_int(fe); };
-      gemv::stage_x3<8, 32, 256, true>(xsrc, b0 * kBlkVals, nbl * kBlkVals, sstride, xb, sums, expo, tid, kCW * 32);
+      if (a.xbulk) {
+        // the slice of x arrives in shared memory by bulk copy; stage it from there
+        x_ok = ptx::mbar_wait(bar_x, 0, abort_flag);
+        const XSrc xsrc{xraw, nullptr, nullptr, (long)nbl_max * kBlkVals, a.x_dtype, 1, M, 0};
+        gemv::stage_x3<8, 32, 256, true>(xsrc, 0, x_ok ? nbl * kBlkVals : 0, sstride, xb, sums, expo, tid, kCW * 32);
+      } else {
+        const XSrc xsrc{reinterpret_cast<const char*>(a.x) + (size_t)tok0 * a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u),
+                        nullptr, nullptr, a.ldx, a.x_dtype, a.x_vec, M, 0};
+        gemv::stage_x3<8, 32, 256, true>(xsrc, b0 * kBlkVals, nbl * kBlkVals, sstride, xb, sums, expo, tid, kCW * 32);
+      }
     }
 
     float acc[NP][2];
@@ -218,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int mq = 0; mq < NP; ++mq) acc[mq][0] = acc[mq][1] = 0.f;
     const int r0 = warp * 16 + g;
     const uint32_t xb_base = ptx::smem_addr(xb);
-    for (int i = 0; i < nbl; ++i) {
+    for (int i = 0; i < (x_ok ? nbl : 0); ++i) {
       const int s = i % NST;
       if (!ptx::mbar_wait(bar_full + 8 * s, (i / NST) & 1, abort_flag)) break;
       const unsigned char* p0 = smem + s * L::kStage + r0 * kBlkBytes;
@@ -388,18 +423,19 @@ constexpr int kXpTokens = 8;   // tokens per z-slice when the activations are st
 
 // dynamic shared memory of one CTA with an nst-stage ring for z-slices of mchunk tokens, as the
 // kernel carves it up (xp: activations staged in global memory and carried by the ring)
-size_t smem_bytes(int mchunk, int nb, int cs, int nst, bool xp) {
+size_t smem_bytes(int mchunk, int nb, int cs, int nst, bool xp, int xbulk_size = 0) {
   const int nbl_max = (nb + cs - 1) / cs;
   const int maxm = xp ? kXpTokens : (mchunk <= 2 ? 2 : 4);
   const size_t red = cs > 1 ? (size_t)cs * maxm * ((kRows + cs - 1) / cs) * 4 : 0;
   if (xp) {
     const size_t stage = kStageBytes + (size_t)kBlkVals * gemv::xb3_slots(kXpTokens) + q4k_sum_ints(kXpTokens) * 4;
-    return 1024 + (size_t)nst * stage + 2 * nst * 8 + 16 + red;
+    return 1024 + (size_t)nst * stage + 2 * nst * 8 + 32 + red;
   }
   const size_t xs = ((size_t)nbl_max * kBlkVals * gemv::xb3_slots(mchunk) + 15) & ~(size_t)15;
   const size_t gsb = ((size_t)2 * mchunk * (nbl_max * 8 + 2) * 4 + 15) & ~(size_t)15;
   const size_t geb = ((size_t)mchunk * nbl_max * 4 + 15) & ~(size_t)15;
-  return 1024 + (size_t)nst * kStageBytes + 2 * nst * 8 + 16 + xs + gsb + geb + red;
+  const size_t xrb = ((size_t)mchunk * nbl_max * kBlkVals * xbulk_size + 15) & ~(size_t)15;
+  return 1024 + (size_t)nst * kStageBytes + 2 * nst * 8 + 32 + xs + gsb + geb + xrb + red;
 }
 
 template <int NP, int NST, bool XP>
@@ -495,6 +531,10 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   const bool xp = M > 4;
   const int mchunk = xp ? kXpTokens : M;
   a.mchunk = mchunk;
+  a.xsize = x_dtype == QL_F32 ? 4 : 2;
+  a.pdl = (launch_flags() & QL_LAUNCH_PDL) ? 1 : 0;
+  a.xbulk = !xp && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * a.xsize) % 16 == 0;
+  const int xbs = a.xbulk ? a.xsize : 0;
   const int zdim = (M + mchunk - 1) / mchunk;
   const int tiles = (N + kRows - 1) / kRows * zdim;
   const size_t per_sm = 228 * 1024;   // shared memory per SM; each CTA also reserves 1 KB
@@ -502,7 +542,7 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   double best = -1.0;
   for (int ns = kNST; ns >= 2; ns -= 2) {   // ring depths built: 4 and 2
     for (int c = 1; c <= 8 && c <= a.nb; ++c) {
-      const size_t sm = smem_bytes(mchunk, a.nb, c, ns, xp);
+      const size_t sm = smem_bytes(mchunk, a.nb, c, ns, xp, xbs);
       if (sm > 220 * 1024) continue;
       const int fit = (int)(per_sm / (sm + 1024 + 256));
       const int per = fit >= 2 ? 2 : fit;
@@ -524,7 +564,7 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
   if (best_cs == 0) return false;
   a.cs = best_cs;
   a.nst = best_nst;
-  const size_t smem = smem_bytes(mchunk, a.nb, a.cs, a.nst, xp);
+  const size_t smem = smem_bytes(mchunk, a.nb, a.cs, a.nst, xp, xbs);
   void* ws = nullptr;
   bool owned = false;
   if (xp) {
