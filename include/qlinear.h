@@ -184,6 +184,40 @@ QL_API int ql_q4k_matmul_ws(const void* x, int x_dtype, long ldx, const uint8_t*
                             void* out, int out_dtype, long ldo, int M, int K, int N, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/*
+ * Exact fp32 dequantisation of a GGUF weight of ggml type Q8_0 (8), Q4_K (12), Q5_K (13) or
+ * Q6_K (14): W[n, k] for the [N, K] tensor stored as N rows of K / block blocks, each value
+ * rounded exactly as the reference's numpy expression ((d*sc)*q for Q6_K, d*q for Q8_0,
+ * (d*sc*q) - (dmin*m) for Q4_K / Q5_K). K % 256 == 0.
+ * Replaces: webtorch/ggufload.py:140-145,190-246 (dequant: Q8_0, Q4_K, Q5_K, Q6_K branches).
+ */
+QL_API int ql_ggml_dequant(int ggml_type, const uint8_t* raw, float* W, int N, int K, void* stream);
+
+/*
+ * y[M, N] = x[M, K] @ W[N, K]^T (+ bias) with W decoded from the GGUF bytes inside the kernel,
+ * for ggml types Q8_0, Q4_K, Q5_K, Q6_K (the ids above; Q4_K goes to ql_q4k_matmul). Rows must
+ * be 4-byte aligned (Q8_0: K % 64 == 0, Q6_K: K % 512 == 0). Other arguments as ql_q4k_matmul.
+ * Replaces: webtorch/_core.py:3720-3734 (ggml_matmul) with the decode fragments of
+ *           _core.py:3071-3177 dispatched by _GGML_TYPES (_core.py:3608-3638).
+ */
+QL_API int ql_ggml_matmul(const void* x, int x_dtype, long ldx, const uint8_t* raw, int ggml_type,
+                          const float* bias, void* out, int out_dtype, long ldo, int M, int K, int N,
+                          void* stream);
+
+/*
+ * GPTQ-format quantisation of a dense weight W (out = N rows of in = K values, of w_dtype, row
+ * stride ldw) on the GPU: asymmetric min/max per group of gs input rows, zero-padded to
+ * Kp = K rounded up to gs and Np = N rounded up to 32/bits. Writes qweight int32 [Kp/per, Np],
+ * qzeros int32 [Kp/gs, Np/per] storing (zero point - zero_store_offset) (1: AutoGPTQ's zp - 1,
+ * 0: the reference's own packing) and scales [Kp/gs, Np] (QL_F16 or QL_F32). Bit-identical to
+ * the reference's float32 numpy quantiser.
+ * Replaces: webtorch/quantize.py:80-106 (_quantize_raw, _pack_autogptq) and, with
+ *           zero_store_offset 0, webtorch/_core.py:3782-3824 (_gptq_quantize) on float32 weights.
+ */
+QL_API int ql_gptq_quantize(const void* W, int w_dtype, long ldw, int N, int K, int gs, int bits,
+                            int zero_store_offset, int32_t* qweight, int32_t* qzeros, void* scales,
+                            int scales_dtype, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Mixture-of-experts block. Replaces the body of `moe_mlp` (webtorch/lm_engine.py:294-329):
  * the host-side softmax / argpartition / per-expert loop becomes device routing plus two

@@ -176,3 +176,32 @@ def pack_autogptq(q, sc, zp, gs, bits):
 def sort_rows(qweight, perm, bits):
     """Row k' of the result holds value perm[k'] of qweight (loader-side desc_act sort)."""
     return pack_rows(unpack_rows(qweight, bits)[np.asarray(perm)], bits)
+
+
+def quantize_raw(W_out_in, gs, bits):
+    """The AutoGPTQ writer's quantiser, webtorch/quantize.py:80-95 (`_quantize_raw`): the (out, in)
+    weight in float32, transposed to (K, N), zero-padded to Kp (multiple of gs) and Np (multiple
+    of per); returns q [Kp, Np], scales [Kp/gs, Np] float32, zero points [Kp/gs, Np]."""
+    Wt = np.ascontiguousarray(np.asarray(W_out_in, np.float32).T)
+    K, N = Wt.shape
+    qmax = (1 << bits) - 1
+    per = 32 // bits
+    Kp = K + ((-K) % gs)
+    Np = N + ((-N) % per)
+    if Kp != K or Np != N:
+        Wt = np.pad(Wt, ((0, Kp - K), (0, Np - N)))
+    nG = Kp // gs
+    sc = np.empty((nG, Np), np.float32)
+    zp = np.empty((nG, Np), np.int32)
+    q = np.empty((Kp, Np), np.int32)
+    for g in range(nG):
+        blk = Wt[g * gs:(g + 1) * gs]
+        lo = blk.min(0)
+        hi = blk.max(0)
+        s = (hi - lo) / qmax
+        s[s == 0] = 1e-8
+        z = np.clip(np.round(-lo / s), 0, qmax).astype(np.int32)
+        sc[g] = s
+        zp[g] = z
+        q[g * gs:(g + 1) * gs] = np.clip(np.round(blk / s) + z, 0, qmax).astype(np.int32)
+    return q, sc, zp

@@ -17,7 +17,15 @@ Cases:
   q4k_*.npz        raw Q4_K bytes, `ggufload.dequant` output and x @ W.T.
   moe_*.npz        `lm_engine.moe_mlp` with a stub router returning fixed logits and
                    `QuantizedLinear.from_autogptq` experts.
+  ggml_<type>_*.npz  raw Q8_0 / Q5_K / Q6_K bytes (benchmark-like and unrestricted random),
+                   `ggufload.dequant` output and x @ W.T.
+  gptq_writer_*.npz  the AutoGPTQ writer: `quantize._quantize_raw` + `_pack_autogptq` on a
+                   padded (out, in) weight (qweight, qzeros storing zp - 1, fp16 scales, g_idx).
+  gguf_parse.npz   a small GGUF file (metadata of every value type, a 2-D Q4_K weight, a stacked
+                   Q6_K expert tensor, an F32 norm) and `ggufload.parse_header`'s view of it.
 """
+import json
+import struct
 import os
 import sys
 
@@ -34,8 +42,9 @@ def _import_reference(path):
     from webtorch import _core as wt  # noqa
     from webtorch import ggufload as G  # noqa
     from webtorch import lm_engine as LE  # noqa
+    from webtorch import quantize as Q  # noqa
     assert not wt.GPU, "the reference must run its numpy path here"
-    return wt, G, LE
+    return wt, G, LE, Q
 
 
 def gptq_ref_cases(wt):
@@ -191,17 +200,106 @@ def moe_shared_case(wt, LE):
     np.savez_compressed(os.path.join(HERE, "moe_shared_E%d_k%d_T%d.npz" % (E, top_k, T)), **d)
 
 
+def ggml_kquant_cases(G):
+    ids = {"Q8_0": 8, "Q5_K": 13, "Q6_K": 14}
+    for t, tid in ids.items():
+        rng = np.random.default_rng(tid)
+        N, K = 64, 1024
+        raw = synth.ggml_weights(t, N, K, rng=rng)
+        W = np.asarray(G.dequant(tid, raw.tobytes(), N * K), np.float32).reshape(N, K)
+        d = {"N": N, "K": K, "raw": raw, "W": W, "type_id": tid}
+        for M in (1, 3, 8):
+            x = rng.standard_normal((M, K)).astype(np.float32)
+            d["x_%d" % M] = x
+            d["y_%d" % M] = (x @ W.T).astype(np.float32)
+        np.savez_compressed(os.path.join(HERE, "ggml_%s_synth.npz" % t), **d)
+        # unrestricted random bytes (inf / nan scales included)
+        vals, nbytes = (32, 34) if t == "Q8_0" else (256, {"Q5_K": 176, "Q6_K": 210}[t])
+        raw = rng.integers(0, 256, (8, (512 // vals) * nbytes), dtype=np.uint8)
+        W = np.asarray(G.dequant(tid, raw.tobytes(), 8 * 512), np.float32).reshape(8, 512)
+        np.savez_compressed(os.path.join(HERE, "ggml_%s_rawbytes.npz" % t), N=8, K=512, raw=raw, W=W, type_id=tid)
+
+
+def gptq_writer_cases(Q):
+    for (N, K, gs, bits, seed) in [(100, 200, 64, 4, 0), (64, 256, 128, 8, 1), (480, 896, 128, 4, 2)]:
+        rng = np.random.default_rng(seed)
+        W = (rng.standard_normal((N, K)) * 0.05).astype(np.float16)
+        W[0, :gs] = 0.25          # a group with one value: s = 0 -> 1e-8
+        q, sc, zp, K_, N_, Kp, Np = Q._quantize_raw(W, gs, bits)
+        qw, qz, scq, gidx = Q._pack_autogptq(q, sc, zp, gs, bits)
+        np.savez_compressed(os.path.join(HERE, "gptq_writer_N%d_K%d_g%d_b%d.npz" % (N, K, gs, bits)), W=W, N=N, K=K,
+                            gs=gs, bits=bits, Kp=Kp, Np=Np, qweight=qw, qzeros=qz, scales=scq, g_idx=gidx)
+
+
+def _gguf_bytes(meta, tensors, align=32):
+    """A GGUF v3 file: header, metadata KV, tensor infos, aligned data (test-fixture builder)."""
+    def s_(x):
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    def val(t, v):
+        fmt = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q", 12: "<d"}
+        if t == 8:
+            return s_(v)
+        if t == 9:
+            at, items = v
+            return struct.pack("<IQ", at, len(items)) + b"".join(val(at, i) for i in items)
+        return struct.pack(fmt[t], v)
+    out = struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(meta))
+    for k, (t, v) in meta.items():
+        out += s_(k) + struct.pack("<I", t) + val(t, v)
+    off, data = 0, b""
+    for name, dims, ttype, raw in tensors:
+        pad = (-off) % align
+        data += b"\0" * pad
+        off += pad
+        out += s_(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims) + \
+            struct.pack("<IQ", ttype, off)
+        data += raw
+        off += len(raw)
+    out += b"\0" * ((-len(out)) % align)
+    return out + data
+
+
+def gguf_parse_case(G):
+    rng = np.random.default_rng(7)
+    q4 = synth.q4k_weights(48, 512, rng=rng)                  # [out 48, in 512]
+    q6 = synth.ggml_weights("Q6_K", 4 * 32, 512, rng=rng)     # 4 experts x [out 32, in 512]
+    norm = rng.standard_normal(512).astype(np.float32)
+    meta = {"general.architecture": (8, "qwen3moe"), "general.alignment": (4, 32), "a.u8": (0, 7),
+            "a.i8": (1, -3), "a.u16": (2, 500), "a.i16": (3, -500), "a.i32": (5, -70000), "a.f32": (6, 0.5),
+            "a.bool": (7, True), "a.u64": (10, 2 ** 40), "a.i64": (11, -2 ** 40), "a.f64": (12, 0.25),
+            "a.arr": (9, (5, [1, -2, 3])), "a.strs": (9, (8, ["x", "yz"]))}
+    tensors = [("blk.0.attn_norm.weight", [512], 0, norm.tobytes()),
+               ("blk.0.attn_q.weight", [512, 48], 12, q4.tobytes()),
+               ("blk.0.ffn_gate_exps.weight", [512, 32, 4], 14, q6.tobytes())]
+    buf = _gguf_bytes(meta, tensors)
+    version, md, infos, data_start = G.parse_header(buf)
+    names = [t["name"] for t in infos]
+    np.savez_compressed(os.path.join(HERE, "gguf_parse.npz"), gguf=np.frombuffer(buf, np.uint8), version=version,
+                        meta=json.dumps(md), names=json.dumps(names),
+                        dims=json.dumps([[int(d) for d in t["dims"]] for t in infos]),
+                        types=np.array([t["type"] for t in infos], np.int32),
+                        offsets=np.array([t["offset"] for t in infos], np.int64), data_start=data_start,
+                        W_q4=np.asarray(G.dequant(12, q4.tobytes(), 48 * 512), np.float32).reshape(48, 512),
+                        W_q6=np.asarray(G.dequant(14, q6.tobytes(), 128 * 512), np.float32).reshape(4, 32, 512),
+                        norm=norm)
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("WEBTORCH_REFERENCE")
     if not ref:
         sys.exit("usage: make_golden.py <reference checkout> (or set WEBTORCH_REFERENCE)")
-    wt, G, LE = _import_reference(ref)
+    wt, G, LE, Q = _import_reference(ref)
     gptq_ref_cases(wt)
     gptq_autogptq_cases(wt)
     gptq_fromlinear_case(wt)
     q4k_cases(G)
     moe_cases(wt, LE)
     moe_shared_case(wt, LE)
+    ggml_kquant_cases(G)
+    gptq_writer_cases(Q)
+    gguf_parse_case(G)
     print("golden fixtures written to", HERE)
 
 

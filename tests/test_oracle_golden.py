@@ -123,3 +123,31 @@ def test_moe_vs_reference(name):
     norm = bool(int(d["norm_topk_prob"])) if "norm_topk_prob" in d else True
     y = om.moe_mlp(d["x"], d["logits"], experts, top_k, norm, shared, shared_gate)
     assert max_rel_err(y, d["y"]) < 1e-6
+
+
+# ---------------------------------------------------------------------------------------
+# other GGUF types, the AutoGPTQ writer (fixtures made by the reference)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", golden_files("ggml_"))
+def test_ggml_oracle_matches_reference_dequant(name):
+    from oracle import ggml as ogg
+    d = golden(name)
+    tname = {8: "Q8_0", 13: "Q5_K", 14: "Q6_K"}[int(d["type_id"])]
+    N, K = int(d["N"]), int(d["K"])
+    W = ogg.dequant(tname, d["raw"].tobytes(), N * K).reshape(N, K)
+    assert same_bits_or_both_nan(W, d["W"])
+    for M in (1, 3, 8):
+        if "x_%d" % M in d:
+            y = ogg.matmul(d["x_%d" % M], d["raw"].tobytes(), tname, K, N)
+            assert np.array_equal(y, d["y_%d" % M])
+
+
+@pytest.mark.parametrize("name", golden_files("gptq_writer_"))
+def test_writer_oracle_matches_reference(name):
+    d = golden(name)
+    gs, bits = int(d["gs"]), int(d["bits"])
+    q, sc, zp = og.quantize_raw(d["W"], gs, bits)
+    qw, qz, scq, gidx = og.pack_autogptq(q, sc, zp, gs, bits)
+    assert np.array_equal(qw, d["qweight"]) and np.array_equal(qz, d["qzeros"])
+    assert np.array_equal(scq.view(np.uint16), d["scales"].view(np.uint16))
+    assert np.array_equal(gidx, d["g_idx"])

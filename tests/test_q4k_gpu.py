@@ -77,4 +77,4 @@ def test_bias_ragged_rows_and_host_io(K):
 
 def test_unsupported_type_raises():
     with pytest.raises(NotImplementedError):
-        GGMLLinear(b"\x00" * 34, "Q8_0", 32, 1)
+        GGMLLinear(b"\x00" * 84, "Q2_K", 256, 1)

@@ -37,6 +37,11 @@ SIGNATURES = {
     "ql_q4k_dequant": (_c_int, [_vp, _vp, _c_int, _c_int, _vp]),
     "ql_q4k_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp]),
     "ql_q4k_matmul_workspace": (ctypes.c_size_t, [_c_int, _c_int]),
+    "ql_ggml_dequant": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _vp]),
+    "ql_ggml_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _c_int, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int,
+                                _vp]),
+    "ql_gptq_quantize": (_c_int, [_vp, _c_int, _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
+                                  _vp]),
     "ql_q4k_matmul_ws": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp,
                                   ctypes.c_size_t, _vp]),
     "ql_moe_route": (_c_int, [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

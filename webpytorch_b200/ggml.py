@@ -1,23 +1,25 @@
-"""GGUF Q4_K linear: the drop-in for webtorch's `GGMLLinear` / `ggml_matmul`.
+"""GGUF quantised linear: the drop-in for webtorch's `GGMLLinear` / `ggml_matmul`.
 
 Interface parity with the reference (webtorch/_core.py:4377-4406, 3720-3734):
   * `GGMLLinear(raw, type_name, K, N, bias=None)` takes the tensor's bytes exactly as the GGUF
-    file stores them ([N rows] x [K/256 super-blocks] x 144 bytes for Q4_K).
+    file stores them ([N rows] x [K / block] blocks; Q4_K: 256 values in 144 bytes).
   * `forward(x: [..., K]) -> [..., N]` in fp32, plus bias.
   * `ggml_matmul(xf, raw, type_name, K, N)` is the function-level boundary.
 
-The bytes go to the GPU unchanged (no transpose: the CUDA kernel reads the file's row layout
-coalesced) and are decoded inside the matmul. Only Q4_K has a native kernel here; the other
-ggml types raise NotImplementedError.
+The bytes go to the GPU unchanged (no transpose: the CUDA kernels read the file's row layout)
+and are decoded inside the matmul. Native kernels: Q4_K (TMA-fed integer-MMA GEMV), Q8_0, Q5_K
+and Q6_K (the types of Q4_K_M / Q5_K_M / Q8_0 files, webtorch/_core.py:3071-3177). Other ggml
+types raise NotImplementedError.
 """
 import numpy as np
 import torch
 
 from . import _ffi
 
-__all__ = ["GGMLLinear", "ggml_matmul", "q4k_dequant", "NATIVE_TYPES"]
+__all__ = ["GGMLLinear", "ggml_matmul", "q4k_dequant", "ggml_dequant", "NATIVE_TYPES"]
 
-NATIVE_TYPES = {"Q4_K": (256, 144)}   # values per block, bytes per block
+# values per block, bytes per block, ggml type id
+NATIVE_TYPES = {"Q4_K": (256, 144, 12), "Q8_0": (32, 34, 8), "Q5_K": (256, 176, 13), "Q6_K": (256, 210, 14)}
 
 
 def _device(device=None):
@@ -35,6 +37,17 @@ def q4k_dequant(raw, K, N, stream=None):
     return W
 
 
+def ggml_dequant(raw, type_name, K, N, stream=None):
+    """Exact fp32 [N, K] weight from raw GGUF bytes of a native type (bit-identical to
+    ggufload.dequant)."""
+    if type_name not in NATIVE_TYPES:
+        raise NotImplementedError("no native B200 kernel for ggml type %s" % type_name)
+    W = torch.empty((N, K), dtype=torch.float32, device=raw.device)
+    _ffi.call("ql_ggml_dequant", NATIVE_TYPES[type_name][2], _ffi.ptr(raw), _ffi.ptr(W), N, K,
+              _ffi.stream_ptr(stream))
+    return W
+
+
 def ggml_matmul(xf, raw, type_name, K, N, *, bias=None, out=None, out_dtype=torch.float32, stream=None):
     """y[M, N] = xf[M, K] @ W[N, K].T (+ bias) with W decoded from `raw` inside the kernel."""
     if type_name not in NATIVE_TYPES:
@@ -47,9 +60,14 @@ def ggml_matmul(xf, raw, type_name, K, N, *, bias=None, out=None, out_dtype=torc
     M = xf.shape[0]
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype, device=xf.device)
-    _ffi.call("ql_q4k_matmul", _ffi.ptr(xf), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(raw),
-              _ffi.ptr(bias), _ffi.ptr(out), _ffi.dtype_code(out.dtype), out.stride(0), M, K, N,
-              _ffi.stream_ptr(stream))
+    if type_name == "Q4_K":
+        _ffi.call("ql_q4k_matmul", _ffi.ptr(xf), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(raw),
+                  _ffi.ptr(bias), _ffi.ptr(out), _ffi.dtype_code(out.dtype), out.stride(0), M, K, N,
+                  _ffi.stream_ptr(stream))
+    else:
+        _ffi.call("ql_ggml_matmul", _ffi.ptr(xf), _ffi.dtype_code(xf.dtype), xf.stride(0), _ffi.ptr(raw),
+                  NATIVE_TYPES[type_name][2], _ffi.ptr(bias), _ffi.ptr(out), _ffi.dtype_code(out.dtype),
+                  out.stride(0), M, K, N, _ffi.stream_ptr(stream))
     return out
 
 
@@ -61,7 +79,7 @@ class GGMLLinear(torch.nn.Module):
         if type_name not in NATIVE_TYPES:
             raise NotImplementedError("no native B200 kernel for ggml type %s" % type_name)
         dev = _device(device)
-        vals, blk = NATIVE_TYPES[type_name]
+        vals, blk, _ = NATIVE_TYPES[type_name]
         K, N = int(K), int(N)
         if K % vals:
             raise ValueError("K=%d is not a multiple of the %s block (%d)" % (K, type_name, vals))
@@ -80,7 +98,7 @@ class GGMLLinear(torch.nn.Module):
                              torch.as_tensor(np.asarray(bias, np.float32)).to(dev).contiguous())
 
     def dequantized(self):
-        return q4k_dequant(self.raw, self.Kt, self.Nt)
+        return ggml_dequant(self.raw, self.type_name, self.Kt, self.Nt)
 
     def forward(self, x, out_dtype=torch.float32, out=None):
         host = not x.is_cuda

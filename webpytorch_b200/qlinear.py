@@ -33,7 +33,10 @@ def _device(device=None):
 def _to_dev(a, dtype, device):
     if isinstance(a, torch.Tensor):
         return a.to(device=device, dtype=dtype).contiguous()
-    return torch.from_numpy(np.ascontiguousarray(np.asarray(a))).to(device=device, dtype=dtype).contiguous()
+    a = np.ascontiguousarray(np.asarray(a))
+    if not a.flags.writeable:     # e.g. a view of a memory-mapped checkpoint
+        a = a.copy()
+    return torch.from_numpy(a).to(device=device, dtype=dtype).contiguous()
 
 
 def _param_array(p):
@@ -51,6 +54,8 @@ def _scale_tensor(scales, device):
         dt = scales.dtype if scales.dtype in (torch.float16, torch.bfloat16, torch.float32) else torch.float32
         return scales.to(device=device, dtype=dt).contiguous()
     a = np.asarray(scales)
+    if not a.flags.writeable:
+        a = a.copy()
     dt = torch.float16 if a.dtype == np.float16 else torch.float32
     return torch.from_numpy(np.ascontiguousarray(a.astype(np.float16 if dt == torch.float16 else np.float32))
                             ).to(device).contiguous()

@@ -65,3 +65,26 @@ def moe_experts(E, hidden, inter, bits=4, gs=128, seed=0, rng=None):
                     "up": gptq_weights(hidden, inter, bits, gs, rng=rng),
                     "down": gptq_weights(inter, hidden, bits, gs, rng=rng)})
     return out
+
+
+def ggml_weights(type_name, N, K, seed=0, rng=None):
+    """Raw GGUF bytes [N, K/block * bytes] of a Q8_0, Q5_K or Q6_K weight: fp16 scales (d, dmin)
+    uniform on [1e-3, 1e-2], every other byte uniform (6-bit scale/min fields as Q4_K's)."""
+    rng = rng if rng is not None else np.random.default_rng(seed)
+    if type_name == "Q4_K":
+        return q4k_weights(N, K, rng=rng)
+    vals, nbytes = {"Q8_0": (32, 34), "Q5_K": (256, 176), "Q6_K": (256, 210)}[type_name]
+    assert K % vals == 0
+    nb = N * (K // vals)
+    blk = rng.integers(0, 256, size=(nb, nbytes), dtype=np.uint8)
+    d = rng.uniform(1e-3, 1e-2, size=(nb, 2)).astype(np.float16).view(np.uint8).reshape(nb, 4)
+    if type_name == "Q8_0":
+        blk[:, 0:2] = d[:, 0:2]
+    elif type_name == "Q5_K":
+        blk[:, 0:4] = d
+        sc = rng.integers(0, 64, size=(nb, 8), dtype=np.uint8)
+        mn = rng.integers(0, 64, size=(nb, 8), dtype=np.uint8)
+        blk[:, 4:16] = pack_q4k_scales(sc, mn)
+    else:
+        blk[:, 208:210] = d[:, 0:2]
+    return blk.reshape(N, (K // vals) * nbytes)
