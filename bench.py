@@ -221,6 +221,49 @@ def bench_q4k(dev, g, hbm):
     return res
 
 
+DEC_CFG = {"H": 3584, "NH": 28, "NKV": 4, "HD": 128, "I": 18944, "L": 28, "pos": 512, "lmax": 1024}
+
+
+def bench_decode(dev, g, hbm, steps=50):
+    """The decode step (8(f) row 1) on a synthetic Qwen2.5-7B-shaped stack: 28 layers of H=3584,
+    28 query / 4 key-value heads of 128, SwiGLU I=18944, int4 g128 AutoGPTQ weights with q/k/v
+    biases, KV cache filled up to position 512; one graph replay per token (5 launches a layer)."""
+    torch = torch_mod()
+    from webpytorch_b200.decode import DecodeLayer, DecodeStack
+    from webpytorch_b200.qlinear import QuantizedLinear
+    c = DEC_CFG
+    H, NH, NKV, HD, I, L = c["H"], c["NH"], c["NKV"], c["HD"], c["I"], c["L"]
+
+    def lin(K, N, bias=False):
+        qw, qz, sc = rand_gptq(K, N, dev, g)
+        b = torch.randn(N, device=dev, generator=g) * 0.1 if bias else None
+        return QuantizedLinear(qw, qz, sc, b, K, N, K, N, GS, 4, zero_offset=1.0, device=dev)
+    layers = []
+    for _ in range(L):
+        layers.append(DecodeLayer(lin(H, NH * HD, True), lin(H, NKV * HD, True), lin(H, NKV * HD, True),
+                                  lin(NH * HD, H), lin(H, I), lin(H, I), lin(I, H),
+                                  torch.rand(H, device=dev, generator=g) + 0.5,
+                                  torch.rand(H, device=dev, generator=g) + 0.5))
+    stack = DecodeStack(layers, H, NH, NKV, HD, c["lmax"])
+    for kc, vc in zip(stack.kc, stack.vc):   # a context of `pos` earlier tokens
+        kc.normal_(generator=g)
+        vc.normal_(generator=g)
+    emb = torch.randn(H, device=dev, generator=g)
+    for _ in range(3):
+        stack.step(emb, c["pos"])
+    torch.cuda.synchronize()
+    ms = event_time(stack.graph.replay, steps)
+    wbytes = sum(l.nbytes() for l in layers)
+    kv = L * 2 * NKV * (c["pos"] + 1) * HD * 4
+    return {"workload": "synthetic Qwen2.5-7B-shaped decode stack: %d layers, H=%d, heads %d/%d x %d, I=%d, int4 "
+                        "g128, context position %d, one CUDA-graph replay per token (%d launches)"
+                        % (L, H, NH, NKV, HD, I, c["pos"], stack.launches_per_step()),
+            "ms_per_token": round(ms, 4), "tokens/s": round(1e3 / ms, 1),
+            "weight_MB_per_token": round(wbytes / 1e6, 1), "kv_MB_per_token": round(kv / 1e6, 1),
+            "GB/s": round((wbytes + kv) / (ms / 1e3) / 1e9, 1),
+            "frac_of_hbm": round((wbytes + kv) / (ms / 1e3) / 1e9 / hbm, 4)}
+
+
 def profile_case(name):
     """A small, fixed launch sequence of one kernel for `ncu` (few launches, a few GB at most;
     inputs larger than L2 where the kernel streams weights)."""
@@ -647,12 +690,14 @@ def main():
             del ql, qw, qz, sc
         torch.cuda.empty_cache()
 
-    moe_res, q4k_res, moe_ep = {}, {}, {}
+    moe_res, q4k_res, moe_ep, dec_res = {}, {}, {}, {}
     if not args.skip_extra:
         hbm0, bf0, _ = peaks()
         if world == 1:
             q4k_res = bench_q4k(dev, g, hbm0)
             moe_res = bench_moe(dev, g, hbm0, bf0)
+            dec_res = bench_decode(dev, g, hbm0)
+            torch.cuda.empty_cache()
         moe_ep = bench_moe_ep(dev, g, world, timed)
 
     tot_bytes = step_bytes() * args.steps * world
@@ -695,6 +740,7 @@ def main():
                 "expert_GB/s basis": "active experts' packed weights+scales+zeros per layer / layer time",
                 "T": moe_res},
         "moe_ep": moe_ep,
+        "decode": dec_res,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "eager calls of the operator boundary (_gptq_matmul via ctypes), one pinned-host "

@@ -218,6 +218,47 @@ QL_API int ql_gptq_quantize(const void* W, int w_dtype, long ldw, int N, int K, 
                             int zero_store_offset, int32_t* qweight, int32_t* qzeros, void* scales,
                             int scales_dtype, void* stream);
 
+/*
+ * The quantized linear of a decode step with its neighbours fused in (decode path, M <= 16):
+ *   a = x                                        (glu == 0, norm_weight == NULL)
+ *   a = silu(x[:, :K]) * x[:, K:2K]              (glu == K: x rows hold [gate | up], ldx >= 2K)
+ *   a = x / sqrt(mean(x^2) + norm_eps) * w       (norm_weight w [K] fp32: RMSNorm over each row)
+ *   out = a @ dequant(W) + bias + residual       (bias, residual [M, ld_residual] fp32, optional)
+ * residual may be the same buffer as out (each element is read and written by one thread).
+ * The norm and SwiGLU prologues are applied while the activations are staged for the integer MMA
+ * (no separate launch, no intermediate); arguments otherwise as ql_gptq_matmul_ws. M > 16 and
+ * shapes outside the TMA-fed GEMV (N % 32, K % 128, group size) return QL_ERR_UNSUPPORTED.
+ * Replaces: the decode step's `_rms` -> q/k/v / gate / up projections, `silu(gate) * up` -> down,
+ *           and the residual adds (webtorch/lm_engine.py:62-64,84-87,89-107; llm.py:1591-1616).
+ */
+QL_API int ql_gptq_matmul_fused(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                                const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                int scales_dtype, const float* bias, const float* norm_weight, float norm_eps,
+                                int glu, const float* residual, long ld_residual, void* out, int out_dtype,
+                                long ldo, int M, int K, int N, int gs, int bits, float zero_offset,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One decode position of grouped-query attention: qkv [1, (NH + 2 NKV) * HD] fp32 (q heads, then
+ * k, then v), rotary tables rope_cos / rope_sin [lmax, HD/2] fp32, position pos[0] read on the
+ * device (int32, so a captured graph replays for every token), caches kcache / vcache
+ * [NKV, lmax, HD] fp32 (this position's rotated k and v are written), out [NH * HD] fp32 =
+ * softmax(q_rot . K[0..pos]^T * scale) . V per head (key/value head h / (NH / NKV)). A position
+ * outside 0 .. lmax - 1 writes NaN outputs and leaves the caches alone. Positions are split over
+ * CTAs of 64; workspace (>= ql_decode_attention_workspace bytes, 256-byte aligned) holds their
+ * partial results and one counter per head, which must be zero before the first call (the kernel
+ * leaves them at zero). Calls that share a workspace must not overlap on the GPU.
+ * Replaces: webtorch/lm_engine.py:66-74 (_rope, _rot) and the attention of _block
+ *           (lm_engine.py:89-101) / _decode_fwd (llm.py:1596-1611) at one position.
+ */
+QL_API int ql_decode_attention(const float* qkv, int NH, int NKV, int HD, const float* rope_cos,
+                               const float* rope_sin, const int32_t* pos, float* kcache, float* vcache, int lmax,
+                               float scale, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace ql_decode_attention needs for NH heads of HD over a cache of lmax positions.
+ * No counterpart in the reference. */
+QL_API size_t ql_decode_attention_workspace(int NH, int HD, int lmax);
+
 /* ---------------------------------------------------------------------------------------
  * Mixture-of-experts block. Replaces the body of `moe_mlp` (webtorch/lm_engine.py:294-329):
  * the host-side softmax / argpartition / per-expert loop becomes device routing plus two

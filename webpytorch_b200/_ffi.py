@@ -40,6 +40,12 @@ SIGNATURES = {
     "ql_ggml_dequant": (_c_int, [_c_int, _vp, _vp, _c_int, _c_int, _vp]),
     "ql_ggml_matmul": (_c_int, [_vp, _c_int, _c_long, _vp, _c_int, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int,
                                 _vp]),
+    "ql_gptq_matmul_fused": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _c_float, _c_int, _vp,
+                                      _c_long, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float,
+                                      _vp, ctypes.c_size_t, _vp]),
+    "ql_decode_attention": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _c_float, _vp, _vp,
+                                     ctypes.c_size_t, _vp]),
+    "ql_decode_attention_workspace": (ctypes.c_size_t, [_c_int, _c_int, _c_int]),
     "ql_gptq_quantize": (_c_int, [_vp, _c_int, _c_long, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _vp, _vp, _c_int,
                                   _vp]),
     "ql_q4k_matmul_ws": (_c_int, [_vp, _c_int, _c_long, _vp, _vp, _vp, _c_int, _c_long, _c_int, _c_int, _c_int, _vp,

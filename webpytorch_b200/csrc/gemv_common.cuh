@@ -6,6 +6,17 @@
 #include "ql_common.cuh"
 
 namespace ql {
+
+// Options of the fused decode-step GEMV (ql_gptq_matmul_fused): RMSNorm weight / eps folded into
+// the activation staging, SwiGLU of [gate | up] rows (glu = K), and a residual added to the output.
+struct GemvFused {
+  const float* norm_w;
+  float norm_eps;
+  int glu;
+  const float* res;
+  long ldres;
+};
+
 namespace gemv {
 
 // Position of value j of a packed word inside the fp16 staging of x. The register unpack
@@ -25,13 +36,17 @@ __device__ __forceinline__ float swiglu(float g, float u) { return g / (1.0f + e
 
 // 8 consecutive activations x[m, k .. k+7] (through x_perm when set) as floats. With a.glu > 0
 // a row holds [gate | up] halves a.glu elements apart and the activation is silu(gate) * up.
+// With a.nw (RMSNorm folded into the load) each value is multiplied by the token's factor
+// a.nr[m] = 1 / sqrt(mean(x^2) + eps) and by the norm weight of its K index.
 template <class Args>
 __device__ __forceinline__ void load_x8(const Args& a, int m, int k, float (&v)[8]) {
   if (a.glu) {
     const long base = (long)(a.x_rows ? a.x_rows[m] : m) * a.ldx;
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      v[j] = swiglu(load_as_float(a.x, a.x_dtype, base + k + j), load_as_float(a.x, a.x_dtype, base + a.glu + k + j));
+    for (int j = 0; j < 8; ++j) {
+      const int src = a.x_perm ? a.x_perm[k + j] : k + j;
+      v[j] = swiglu(load_as_float(a.x, a.x_dtype, base + src), load_as_float(a.x, a.x_dtype, base + a.glu + src));
+    }
     return;
   }
   const long base = (long)(a.x_rows ? a.x_rows[m] : m) * a.ldx;   // x_rows: gather of token rows
@@ -59,13 +74,32 @@ __device__ __forceinline__ void load_x8(const Args& a, int m, int k, float (&v)[
       v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
       v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
     }
+    if (a.nw) {
+      const float r = a.nr[m];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * r * a.nw[k + j];
+    }
   } else {
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int src = a.x_perm ? a.x_perm[k + j] : k + j;
       v[j] = load_as_float(a.x, a.x_dtype, base + src);
+      if (a.nw) v[j] = v[j] * a.nr[m] * a.nw[src];
     }
   }
+}
+
+// Sum of squares of token row m's K values of x (any order), reduced over the calling threads'
+// warp (each lane covers a strided share). x_rows / x_perm / glu are not involved.
+template <class Args>
+__device__ __forceinline__ float row_sumsq_part(const Args& a, int m, int K, int part, int nparts) {
+  float s = 0.f;
+  const long base = (long)m * a.ldx;
+  for (int k = part; k < K; k += nparts) {
+    const float v = load_as_float(a.x, a.x_dtype, base + k);
+    s = fmaf(v, v, s);
+  }
+  return s;
 }
 
 // Stage x[:, kbase : kbase + klen] for M tokens into shared memory as power-of-two-scaled
@@ -364,6 +398,25 @@ __global__ void __launch_bounds__(256) prestage_x3_kernel(const Args a, int K, u
   const int m = blockIdx.x, c = m / MAXM, mm = m - c * MAXM;
   const int tid = threadIdx.x;
   const int cpr = K / 8;
+  __shared__ float s_red[8];
+  __shared__ float s_nr[1];
+  Args an = a;   // this CTA's row: x from row m on, token index 0
+  an.x = reinterpret_cast<const char*>(a.x) + (size_t)m * a.ldx * (a.x_dtype == QL_F32 ? 4 : 2);
+  if (a.nw) {
+    // RMSNorm folded into the staging: the row's factor over all K, then x * r * w on load
+    float ss = gemv::row_sumsq_part(an, 0, K, tid, 256);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) s_red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < 8; ++w) t += s_red[w];
+      s_nr[0] = rsqrtf(t / (float)K + a.norm_eps);
+    }
+    __syncthreads();
+    an.nr = s_nr;
+  }
   uint2* xb = reinterpret_cast<uint2*>(xg + (long)c * chunk_bytes);
   int* sm = reinterpret_cast<int*>(xg + (long)c * chunk_bytes + sum_off);
   auto sums = [&](int, int g, int s1, int s0) {
@@ -387,7 +440,7 @@ __global__ void __launch_bounds__(256) prestage_x3_kernel(const Args a, int K, u
     if (base + (tid & ~31) < cpr) {
       float v[8];
       if (kc < cpr) {
-        gemv::load_x8(a, m, kc * 8, v);
+        gemv::load_x8(an, 0, kc * 8, v);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = 0.f;

@@ -118,6 +118,8 @@ struct GemvArgs {
   const int32_t* moe_n_active;
   long qw_estride, qz_estride, sc_estride;   // elements between consecutive experts
   int glu;   // > 0: x rows are [gate | up] glu elements apart (SwiGLU applied when staging)
+  const float* nw = nullptr;   // RMSNorm folded into the loads: not used by this kernel
+  const float* nr = nullptr;
 };
 
 // Register-resident batch of UG consecutive groups of one lane's weights, scales and zeros.
@@ -479,7 +481,7 @@ inline int pow2_floor(int v) {
 bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
-                   int* rc, void* workspace, size_t ws_bytes);
+                   int* rc, void* workspace, size_t ws_bytes, const GemvFused* fu = nullptr);
 
 // The TMA-fed GEMV when it takes the shape; else the register-fed kernel below, with the K split
 // (cluster size) picked so the grid holds ~16 warps per SM.

@@ -85,6 +85,13 @@ struct TmaGemvArgs {
   int xbulk;
   int xsize;      // bytes per element of x
   int pdl;        // launched as a programmatic dependent (x copies wait for the previous kernel)
+  // fused decode-step options (dense calls): RMSNorm of each token row over all K folded into
+  // the staging (norm_w [K], with xbulk the whole rows are copied), and a residual added to the
+  // output (res [M, ldres] fp32; may alias out: every element is read and written by one thread)
+  const float* norm_w;
+  float norm_eps;
+  const float* res;
+  long ldres;
   // dense calls of more than 4 tokens: activations staged once in global memory, blockIdx.z
   // taking tokens [z * MAXM, z * MAXM + MAXM) from chunk z at xg + z * xg_chunk (the B operand
   // of all K, then per group [S1 | S0 | fe][MAXM] at xg_sum_off)
@@ -102,6 +109,9 @@ struct XSrc {
   int x_vec;
   int M;
   int glu;   // > 0: rows are [gate | up] glu elements apart; the activation is silu(gate) * up
+  const float* nw;   // RMSNorm weight [K] folded into the loads (NULL: none)
+  const float* nr;   // per-token factor 1 / sqrt(mean(x^2) + eps), indexed by token
+  float norm_eps;
 };
 
 // Ring stage: weights, scales, zeros; with XP also the stage's B operand (4 steps x 4 lanes x
@@ -184,9 +194,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int xs_bytes = XP ? 0 : (klen_max * sstride + 15) & ~15;
   int* gsum = reinterpret_cast<int*>(smem + L::kXsOff + xs_bytes);
   const int gs_bytes = XP ? 0 : (3 * M * gstride * 4 + 15) & ~15;
-  // xbulk: the raw rows of x for this CTA's K slice, klen_max elements apart
+  // xbulk: the raw rows of x for this CTA's K slice, klen_max elements apart (with the RMSNorm
+  // option the whole rows, K apart: the norm needs every element)
   unsigned char* xraw = smem + L::kXsOff + xs_bytes + gs_bytes;
-  const int xr_bytes = a.xbulk ? (M * klen_max * a.xsize + 15) & ~15 : 0;
+  const int xr_ld = a.norm_w ? a.K : klen_max;            // elements between token rows
+  const int xr_k0 = a.norm_w ? 0 : s0 * kStageK;          // first element copied
+  const int xr_len = a.norm_w ? a.K : klen;               // elements copied per row
+  const int xr_bytes = a.xbulk ? (M * xr_ld * a.xsize + 15) & ~15 : 0;
   float* red = reinterpret_cast<float*>(smem + L::kXsOff + xs_bytes + gs_bytes + xr_bytes);
   // red: [cs ranks][MAXM tokens][cq_max * 4 columns], cs * cq_max <= Q + cs - 1, cs <= 16 (only
   // with cs > 1); kred: K-way partials (KW == 2), [SW * 32 lanes][NP * 4]
@@ -217,11 +231,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   // the bulk copy of this CTA's x slice (one copy per token row)
   auto copy_x = [&]() {
     pdl_wait();   // x may be the previous kernel's output
-    const uint32_t row_bytes = (uint32_t)(klen * a.xsize);
+    const uint32_t row_bytes = (uint32_t)(xr_len * a.xsize);
     ptx::mbar_arrive_expect_tx(bar_x, (uint32_t)M * row_bytes);
-    const char* xs = reinterpret_cast<const char*>(a.x) + (size_t)s0 * kStageK * a.xsize;
+    const char* xs = reinterpret_cast<const char*>(a.x) + (size_t)xr_k0 * a.xsize;
     for (int m = 0; m < M; ++m)
-      ptx::bulk_load(ptx::smem_addr(xraw + (size_t)m * klen_max * a.xsize), xs + (size_t)(row0 + m) * a.ldx * a.xsize,
+      ptx::bulk_load(ptx::smem_addr(xraw + (size_t)m * xr_ld * a.xsize), xs + (size_t)(row0 + m) * a.ldx * a.xsize,
                      row_bytes, bar_x);
   };
 
@@ -300,18 +314,33 @@ __global__ void __launch_bounds__(kThreads, 2)
         gsum[(3 * m + 1) * gstride + g] = s0v;
       };
       auto expo = [&](int m, int g, float fe) { gsum[(3 * m + 2) * gstride + g] = __float_as_int(fe); };
-      if (a.xbulk) {
-        // the slice of x arrives in shared memory by bulk copy; stage it from there
-        x_ok = ptx::mbar_wait(bar_x, 0, abort_flag);
-        const XSrc xsrc{xraw, nullptr, nullptr, klen_max, a.x_dtype, 1, M, 0};
-        gemv::stage_x3<BITS, GS, GS, true>(xsrc, 0, x_ok ? klen : 0, sstride, xb, sums, expo, tid, kCW * 32);
-      } else {
-        // this CTA's rows: gathered through x_rows, else x itself from row row0 on
-        const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
-        const XSrc xsrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr, a.x_perm,
-                        a.ldx, a.x_dtype, a.x_vec, M, a.glu};
-        gemv::stage_x3<BITS, GS, GS, true>(xsrc, s0 * kStageK, klen, sstride, xb, sums, expo, tid, kCW * 32);
+      if (a.xbulk) x_ok = ptx::mbar_wait(bar_x, 0, abort_flag);   // x arrives in shared memory by bulk copy
+      // this CTA's rows: the bulk copy, or x itself (gathered through x_rows, else from row row0 on)
+      const size_t x_off = a.x_rows ? 0 : (size_t)row0 * (size_t)a.ldx * (a.x_dtype == QL_F32 ? 4u : 2u);
+      XSrc xsrc = a.xbulk ? XSrc{xraw, nullptr, nullptr, xr_ld, a.x_dtype, 1, M, 0}
+                          : XSrc{reinterpret_cast<const char*>(a.x) + x_off, a.x_rows ? a.x_rows + row0 : nullptr,
+                                 a.x_perm, a.ldx, a.x_dtype, a.x_vec, M, a.glu};
+      if (a.norm_w) {
+        // RMSNorm: each token row's 1 / sqrt(mean(x^2) + eps) over all K, then x * r * w on load
+        __shared__ float sh_nr[4], sh_red[kCW][4];
+        for (int m = 0; m < M; ++m) {
+          float ss = x_ok ? gemv::row_sumsq_part(xsrc, m, a.K, tid, kCW * 32) : 0.f;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+          if (lane == 0) sh_red[warp][m] = ss;
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
+        if (tid < M) {
+          float t = 0.f;
+          for (int w = 0; w < kCW; ++w) t += sh_red[w][tid];
+          sh_nr[tid] = rsqrtf(t / (float)a.K + a.norm_eps);
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kCW * 32) : "memory");
+        xsrc.nw = a.norm_w;
+        xsrc.nr = sh_nr;
       }
+      const int kb = a.xbulk && !a.norm_w ? 0 : s0 * kStageK;   // the slice's first K in xsrc
+      gemv::stage_x3<BITS, GS, GS, true>(xsrc, kb, x_ok ? klen : 0, sstride, xb, sums, expo, tid, kCW * 32);
     }
 
     float acc[NP][4];
@@ -461,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int c = 0; c < 4; ++c) {
             float v = acc[mq][c];
             if (a.bias) v += a.bias[c0 + c];
+            if (a.res) v += a.res[(row0 + tok) * a.ldres + c0 + c];
             store_from_float(a.out, a.out_dtype, (row0 + tok) * a.ldo + c0 + c, v);
           }
         }
@@ -498,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int col = blockIdx.y * TC + oq0 * 4 + c;
         if (col < N) {
           if (a.bias) v += a.bias[col];
+          if (a.res) v += a.res[(row0 + tok) * a.ldres + col];
           store_from_float(a.out, a.out_dtype, (row0 + tok) * a.ldo + col, v);
         }
       }
@@ -557,7 +588,8 @@ constexpr int kXpTokens = 8;   // tokens per CTA when the activations are staged
 // activations and their group sums / factors (unless xp: then each stage carries its own), the
 // raw slice of x when it arrives by bulk copy (xbulk_size = bytes per element, else 0), the
 // split-K receive buffer (cs > 1) and the K-way hand-off (128-column tiles).
-size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int nstage, bool xp, int xbulk_size = 0) {
+size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int nstage, bool xp, int xbulk_size = 0,
+                bool xbulk_full_rows = false) {
   const int per = 32 / bits, tc = 32 * sw, gps = kStageK / kgs, rows = kStageK / per;
   const int np = xp ? kXpTokens / 2 : np_of(m), maxm = 2 * np;
   const size_t wsz = ((size_t)sw * rows * 128 + (size_t)gps * tc * scb + (size_t)gps * (tc / per) * 4 + 15) & ~(size_t)15;
@@ -569,7 +601,9 @@ size_t tma_smem(int bits, int kgs, int scb, int sw, int nst, int cs, int m, int 
   if (!xp) {
     b += ((size_t)nst_max * kStageK * gemv::xb3_slots(m) + 15) & ~(size_t)15;
     b += ((size_t)3 * m * (ng_max | 1) * 4 + 15) & ~(size_t)15;
-    if (xbulk_size) b += ((size_t)m * nst_max * kStageK * xbulk_size + 15) & ~(size_t)15;
+    if (xbulk_size)
+      b += ((size_t)m * (xbulk_full_rows ? (size_t)nstage * kStageK : (size_t)nst_max * kStageK) * xbulk_size + 15) &
+           ~(size_t)15;
   }
   if (cs > 1) b += (size_t)(tc + 64) * maxm * 4;
   if (sw < kCW) b += (size_t)sw * 32 * np * 4 * 4;
@@ -605,7 +639,7 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
     return -1;
   auto kern = gptq_gemv_tma_kernel<BITS, GS, NP, NST, SCB, SW, XP>;
   const size_t smem = tma_smem(BITS, GS, SCB, SW, NST, a.cs, XP ? kXpTokens : a.M, a.nstage, XP,
-                              a.xbulk ? a.xsize : 0);
+                              a.xbulk ? a.xsize : 0, a.norm_w != nullptr);
   if (smem > kMaxSmem) return -1;  // too large an activation slice: caller falls back
   static int configured_dev = -1;
   int dev = 0;
@@ -640,7 +674,7 @@ int launch_tma(const TmaGemvArgs& a, const uint32_t* qweight, const uint32_t* qz
   cfg.numAttrs = nattr;
   if constexpr (XP) {
     // stage the activations once (one CTA per token row) for every CTA of the GEMV
-    const XSrc xsrc{a.x, nullptr, a.x_perm, a.ldx, a.x_dtype, a.x_vec, a.M, 0};
+    const XSrc xsrc{a.x, nullptr, a.x_perm, a.ldx, a.x_dtype, a.x_vec, a.M, a.glu, a.norm_w, nullptr, a.norm_eps};
     prestage_x3_kernel<BITS, GS, GS, kXpTokens, 0><<<a.M, 256, 0, st>>>(xsrc, a.K, const_cast<uint8_t*>(a.xg),
                                                                        a.xg_chunk, a.xg_sum_off);
     const int rc = cuda_status(cudaGetLastError(), "gptq prestage launch");
@@ -692,7 +726,8 @@ void choose_split(TmaGemvArgs& a, int N, int m, int zdim, int sms, int ctas_per_
     const int cap = nst_cap(bits, w), half = nst_half(bits, w);
     for (int ns = cap; ns >= half; ns = (ns == cap && m > 2 && half < cap && !xp) ? half : 0) {
       for (int c = 1; c <= max_cluster && c <= 16 && c <= a.nstage; ++c) {
-        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, m, a.nstage, xp, a.xbulk ? a.xsize : 0);
+        const size_t sm = tma_smem(bits, kgs, scb, w, ns, c, m, a.nstage, xp, a.xbulk ? a.xsize : 0,
+                                   a.norm_w != nullptr);
         if (sm > (size_t)kMaxSmem) continue;
         const int fit = (int)(per_sm / (sm + 1024 + 256));
         const int per = fit < ctas_per_sm ? fit : ctas_per_sm;
@@ -740,7 +775,7 @@ size_t gemv_stage_workspace(int M, int K, int kgs) {
 bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, const int32_t* qweight,
                    const int32_t* qzeros, const void* scales, int sc_dtype, const float* bias, void* out,
                    int out_dtype, long ldo, int M, int K, int N, int gs, int bits, float zoff, cudaStream_t st,
-                   int* rc, void* workspace, size_t ws_bytes) {
+                   int* rc, void* workspace, size_t ws_bytes, const GemvFused* fu) {
   static int enabled = -1, sms = 0, ctas_per_sm = 0, max_cluster = 8;
   if (enabled < 0) {
     enabled = env_int("QL_GEMV_TMA", 1);
@@ -766,6 +801,9 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
   a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
   a.nstage = K / kStageK;
+  if (fu) {
+    a.norm_w = fu->norm_w; a.norm_eps = fu->norm_eps; a.glu = fu->glu; a.res = fu->res; a.ldres = fu->ldres;
+  }
   const size_t need = gemv_stage_workspace(M, K, kgs);
   void* ws = nullptr;
   bool owned = false;
@@ -787,7 +825,8 @@ bool gptq_gemv_tma(const void* x, int x_dtype, long ldx, const int32_t* x_perm, 
   const int zdim = need ? (M + kXpTokens - 1) / kXpTokens : 1;
   a.xsize = x_dtype == QL_F32 ? 4 : 2;
   a.pdl = (launch_flags() & QL_LAUNCH_PDL) ? 1 : 0;
-  a.xbulk = !need && x_perm == nullptr && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (ldx * a.xsize) % 16 == 0;
+  a.xbulk = !need && x_perm == nullptr && !a.glu && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+            (ldx * a.xsize) % 16 == 0;
   choose_split(a, N, need ? kXpTokens : M, zdim, sms, ctas_per_sm, max_cluster, bits, kgs, sc_dtype == QL_F32 ? 4 : 2,
                need != 0);
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(qweight);
@@ -851,3 +890,51 @@ bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* 
 }
 
 }  // namespace ql
+
+// ---------------------------------------------------------------------------------------
+// fused decode-step linear
+// ---------------------------------------------------------------------------------------
+extern "C" int ql_gptq_matmul_fused(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
+                                    const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                                    int scales_dtype, const float* bias, const float* norm_weight, float norm_eps,
+                                    int glu, const float* residual, long ld_residual, void* out, int out_dtype,
+                                    long ldo, int M, int K, int N, int gs, int bits, float zero_offset,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace ql;
+  if (bits != 4 && bits != 8) {
+    set_error("ql_gptq_matmul_fused: bits must be 4 or 8 (got %d)", bits);
+    return QL_ERR_UNSUPPORTED;
+  }
+  const int per = 32 / bits;
+  if (M < 0 || K <= 0 || N <= 0 || gs <= 0 || K % gs || K % per || N % per || ldo < N ||
+      ldx < (glu ? 2L * K : (long)K) || (glu && glu != K) || (residual && ld_residual < N) ||
+      (x_dtype != QL_F32 && x_dtype != QL_F16 && x_dtype != QL_BF16) ||
+      (out_dtype != QL_F32 && out_dtype != QL_F16 && out_dtype != QL_BF16) ||
+      (scales_dtype != QL_F32 && scales_dtype != QL_F16 && scales_dtype != QL_BF16) ||
+      (zero_offset != 0.f && zero_offset != 1.f)) {
+    set_error("ql_gptq_matmul_fused: bad arguments (M=%d K=%d N=%d gs=%d glu=%d ldx=%ld)", M, K, N, gs, glu, ldx);
+    return QL_ERR_ARG;
+  }
+  if (norm_weight && glu) {
+    set_error("ql_gptq_matmul_fused: the RMSNorm and SwiGLU prologues do not combine");
+    return QL_ERR_UNSUPPORTED;
+  }
+  if (M == 0) return QL_OK;
+  if (!x || !qweight || !qzeros || !scales || !out) {
+    set_error("ql_gptq_matmul_fused: null pointer");
+    return QL_ERR_ARG;
+  }
+  if (M > 16) {
+    set_error("ql_gptq_matmul_fused: decode-step path, M=%d > 16 (use ql_gptq_matmul)", M);
+    return QL_ERR_UNSUPPORTED;
+  }
+  const GemvFused fu{norm_weight, norm_eps, glu, residual, ld_residual};
+  int rc = QL_OK;
+  if (!gptq_gemv_tma(x, x_dtype, ldx, x_perm, qweight, qzeros, scales, scales_dtype, bias, out, out_dtype, ldo, M, K,
+                     N, gs, bits, zero_offset, (cudaStream_t)stream, &rc, workspace, workspace_bytes, &fu)) {
+    set_error("ql_gptq_matmul_fused: shape outside the fused GEMV (N %% 32 == 0, K %% 128 == 0, gs 32 / 64 / "
+              "multiple of 128, 16-byte aligned weights)");
+    return QL_ERR_UNSUPPORTED;
+  }
+  return rc;
+}

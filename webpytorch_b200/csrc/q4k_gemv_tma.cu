@@ -88,6 +88,9 @@ struct XSrc {
   int x_vec;
   int M;
   int glu;
+  const float* nw;   // RMSNorm weight folded into the loads (unused here: NULL)
+  const float* nr;
+  float norm_eps;
 };
 
 // Ring stage: the weights' TMA box, then with XP (activations staged in global memory) the
