@@ -308,6 +308,30 @@ def profile_case(name):
         y = torch.empty((M, Q4K_N), device=dev)
         for r in raws:
             ggml_matmul(x, r, "Q4_K", Q4K_K, Q4K_N, out=y)
+    elif name == "ggml_q6k":                 # ggml_gemv_kernel<Q6_K>, K=4096, N=14336, M=1, 8 copies (386 MB)
+        from webpytorch_b200 import synth
+        from webpytorch_b200.ggml import ggml_matmul
+        raws = [torch.from_numpy(synth.ggml_weights("Q6_K", Q4K_N, Q4K_K, seed=i).reshape(-1)).to(dev)
+                for i in range(8)]
+        x = torch.randn((1, Q4K_K), device=dev, generator=g)
+        for r in raws:
+            ggml_matmul(x, r, "Q6_K", Q4K_K, Q4K_N)
+    elif name in ("decode_attn", "decode_gateup"):   # decode-step kernels at the bench's 7B shape
+        from webpytorch_b200.decode import DecodeLayer, DecodeStack, fused_linear
+        c = DEC_CFG
+        H, NH, NKV, HD, I = c["H"], c["NH"], c["NKV"], c["HD"], c["I"]
+
+        def lin(K, N):
+            qw, qz, sc = rand_gptq(K, N, dev, g)
+            return QuantizedLinear(qw, qz, sc, None, K, N, K, N, GS, 4, zero_offset=1.0, device=dev)
+        lays = [DecodeLayer(lin(H, NH * HD), lin(H, NKV * HD), lin(H, NKV * HD), lin(NH * HD, H), lin(H, I),
+                            lin(H, I), lin(I, H), torch.ones(H, device=dev), torch.ones(H, device=dev))
+                for _ in range(4)]
+        st = DecodeStack(lays, H, NH, NKV, HD, c["lmax"], graph=False)
+        for kc, vc in zip(st.kc, st.vc):
+            kc.normal_(generator=g)
+            vc.normal_(generator=g)
+        st.step(torch.randn(H, device=dev, generator=g), c["pos"])
     else:
         raise SystemExit("unknown profile case %r" % name)
     torch.cuda.synchronize()
@@ -463,7 +487,7 @@ def main():
     ap.add_argument("--skip-extra", action="store_true", help="skip the config-2 and config-4 sections")
     ap.add_argument("--profile", default=None,
                     help="run one small fixed case for ncu: gemv | gemv_narrow | gemm | moe_decode | "
-                         "moe_prefill | q4k | q4k_m8")
+                         "moe_prefill | q4k | q4k_m8 | ggml_q6k | decode_attn | decode_gateup")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:

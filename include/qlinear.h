@@ -244,8 +244,8 @@ QL_API int ql_gptq_matmul_fused(const void* x, int x_dtype, long ldx, const int3
  * device (int32, so a captured graph replays for every token), caches kcache / vcache
  * [NKV, lmax, HD] fp32 (this position's rotated k and v are written), out [NH * HD] fp32 =
  * softmax(q_rot . K[0..pos]^T * scale) . V per head (key/value head h / (NH / NKV)). A position
- * outside 0 .. lmax - 1 writes NaN outputs and leaves the caches alone. Positions are split over
- * CTAs of 64; workspace (>= ql_decode_attention_workspace bytes, 256-byte aligned) holds their
+ * outside 0 .. lmax - 1 writes NaN outputs and leaves the caches alone. lmax <= 8192; HD a
+ * multiple of 8; caches 16-byte aligned. Positions are split over CTAs of 64; workspace (>= ql_decode_attention_workspace bytes, 256-byte aligned) holds their
  * partial results and one counter per head, which must be zero before the first call (the kernel
  * leaves them at zero). Calls that share a workspace must not overlap on the GPU.
  * Replaces: webtorch/lm_engine.py:66-74 (_rope, _rot) and the attention of _block

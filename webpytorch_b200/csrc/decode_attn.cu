@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
   float* qr = sm;             // [HD] rotated query
   float* kr = qr + HD;        // [HD] rotated key of position pos
   float* vr = kr + HD;        // [HD] value of position pos
-  float* sc = vr + HD;        // [kChunk] scores, then exponentials
+  float* sc = vr + HD;        // [max(kChunk, splits)] scores, then exponentials, then chunk weights
   __shared__ float red[kThreads / 32];
   __shared__ bool last;
   const int h = blockIdx.x, j = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -156,18 +156,44 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
   if (!last) return;
   __threadfence();
   const float* ph = part + (long)h * gridDim.y * (HD + 2);
-  // other CTAs' partials: read past L1 (it is not coherent with their writes)
-  float M = -3.4e38f;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(ph + (long)s * (HD + 2) + HD));
-  float L = 0.f;
-  for (int s = 0; s < nsplit; ++s)
-    L += __ldcg(ph + (long)s * (HD + 2) + HD + 1) * expf(__ldcg(ph + (long)s * (HD + 2) + HD) - M);
+  // other CTAs' partials: read past L1 (it is not coherent with their writes). The chunks'
+  // weights exp(m_s - M) / L go to shared memory (sc, free again), one thread per chunk.
+  float ms = -3.4e38f, ls = 0.f;
+  if (tid < nsplit) {
+    ms = __ldcg(ph + (long)tid * (HD + 2) + HD);
+    ls = __ldcg(ph + (long)tid * (HD + 2) + HD + 1);
+  }
+  float M = ms;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  M = red[0];
+  for (int w = 1; w < kThreads / 32; ++w) M = fmaxf(M, red[w]);
+  const float e = tid < nsplit ? expf(ms - M) : 0.f;
+  float L = e * ls;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = L;
+  if (tid < nsplit) sc[tid] = e;
+  __syncthreads();
+  L = 0.f;
+  for (int w = 0; w < kThreads / 32; ++w) L += red[w];
   const float inv = 1.0f / L;
   for (int d = tid; d < HD; d += kThreads) {
-    float o = 0.f;
-    for (int s = 0; s < nsplit; ++s)
-      o = fmaf(__ldcg(ph + (long)s * (HD + 2) + d), expf(__ldcg(ph + (long)s * (HD + 2) + HD) - M), o);
-    out[(long)h * HD + d] = o * inv;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    int s = 0;
+    for (; s + 8 <= nsplit; s += 8) {
+      float pv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) pv[u] = __ldcg(ph + (long)(s + u) * (HD + 2) + d);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) o[u & 3] = fmaf(pv[u], sc[s + u], o[u & 3]);
+    }
+    for (; s < nsplit; ++s) o[0] = fmaf(__ldcg(ph + (long)s * (HD + 2) + d), sc[s], o[0]);
+    out[(long)h * HD + d] = ((o[0] + o[1]) + (o[2] + o[3])) * inv;
   }
   if (tid == 0) counters[h] = 0u;   // ready for the next launch
 }
@@ -201,7 +227,11 @@ extern "C" int ql_decode_attention(const float* qkv, int NH, int NKV, int HD, co
   float* part = reinterpret_cast<float*>(workspace);
   unsigned int* counters = reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + need -
                                                            (size_t)NH * sizeof(unsigned int));
-  const size_t smem = (size_t)(3 * HD + kChunk) * sizeof(float);
+  const size_t smem = (size_t)(3 * HD + (nsplit > kChunk ? nsplit : kChunk)) * sizeof(float);
+  if (nsplit > kThreads) {
+    set_error("ql_decode_attention: lmax=%d is above %d positions", lmax, kThreads * kChunk);
+    return QL_ERR_UNSUPPORTED;
+  }
   const dim3 grid(NH, nsplit);
   decode_attention_kernel<<<grid, kThreads, smem, (cudaStream_t)stream>>>(qkv, NH, NKV, HD, rope_cos, rope_sin, pos,
                                                                           kcache, vcache, lmax, scale, out, part,
