@@ -316,15 +316,18 @@ QL_API int ql_moe_grouped_matmul(const void* x, int x_dtype, long ldx, const int
 
 /* The down projection of the expert FFN straight from the fused gate|up output: out[p] =
  * (silu(y[p, :K]) * y[p, K:2K]) @ W_e, the activation formed while staging (no [P, K]
- * intermediate, no separate ql_moe_act launch). Decode tiles (tile_rows 4 or 8) only;
- * returns QL_ERR_UNSUPPORTED when the call would take the tensor-core path.
+ * intermediate, no separate ql_moe_act launch), on every tile height: the decode GEMV stages
+ * it per CTA, the tensor-core GEMM in its fp16 staging pass (the same workspace as
+ * ql_moe_grouped_matmul, ql_moe_grouped_workspace(P, E, K, gs) bytes). The result is
+ * bit-identical to ql_moe_act (fp32) followed by ql_moe_grouped_matmul.
  * Replaces: webtorch/lm_engine.py:317 (exp["down"](wt.silu(exp["gate"](xe)) * exp["up"](xe))). */
 QL_API int ql_moe_grouped_matmul_swiglu(const void* y, int y_dtype, long ldy, long P, const int32_t* qweight,
                                         const int32_t* qzeros, const void* scales, int scales_dtype, int E,
                                         const int32_t* offsets, const int32_t* active, const int32_t* n_active,
                                         const int32_t* tiles, const int32_t* n_tiles, int max_tiles, int tile_rows,
                                         int max_rows_per_expert, void* out, int out_dtype, long ldo, int K, int N,
-                                        int gs, int bits, float zero_offset, void* stream);
+                                        int gs, int bits, float zero_offset, void* workspace,
+                                        size_t workspace_bytes, void* stream);
 
 QL_API int ql_moe_act(const float* y, long P, int I, void* a, int a_dtype, void* stream);
 

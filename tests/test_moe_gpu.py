@@ -179,6 +179,35 @@ def test_moe_block_empty_batch():
     assert y.shape == (0, 256)
 
 
+@pytest.mark.parametrize("H,shared,out_dtype", [(2048, False, torch.float32), (2048, True, torch.bfloat16),
+                                                 (2050, True, torch.float32), (12, False, torch.float16)])
+def test_combine_matches_ordered_sum(H, shared, out_dtype):
+    """ql_moe_combine (16-byte column path for H % 4 == 0, element path otherwise) against the
+    ordered fp32 sum sum_j w[t, j] * z[pair_row[t, j]] (+ sigmoid(g_t) * shared[t])."""
+    from webpytorch_b200 import _ffi
+    T, k = 37, 8
+    rng = np.random.default_rng(H)
+    z = rng.standard_normal((T * k, H)).astype(np.float32)
+    pair = rng.permutation(T * k).astype(np.int32).reshape(T, k)
+    w = rng.random((T, k)).astype(np.float32)
+    sh = rng.standard_normal((T, H)).astype(np.float32) if shared else None
+    gl = rng.standard_normal((T, 1)).astype(np.float32) if shared else None
+    out = torch.empty((T, H), dtype=out_dtype, device=DEV)
+    zd, pd, wd = (torch.from_numpy(a).to(DEV) for a in (z, pair, w))
+    shd = torch.from_numpy(sh).to(DEV) if shared else None
+    gld = torch.from_numpy(gl).to(DEV) if shared else None
+    _ffi.call("ql_moe_combine", zd.data_ptr(), pd.data_ptr(), wd.data_ptr(), T, k, H, _ffi.ptr(shd),
+              H if shared else 0, _ffi.ptr(gld), 1 if shared else 0, out.data_ptr(), _ffi.dtype_code(out_dtype),
+              H, _ffi.stream_ptr())
+    ref = np.zeros((T, H), np.float64)
+    for j in range(k):
+        ref += w[:, j:j + 1].astype(np.float64) * z[pair[:, j]]
+    if shared:
+        ref += sh / (1.0 + np.exp(-gl.astype(np.float64)))
+    tol = 1e-5 if out_dtype == torch.float32 else 1e-2
+    np.testing.assert_allclose(out.float().cpu().numpy(), ref, rtol=tol, atol=tol)
+
+
 def test_moe_step_replays_in_a_cuda_graph():
     exps, logits, x, _ = _synthetic_case(32, 512, 256, 4, 4, 4, seed=9)
     experts = [{p: _ql(e[p], 128, 4) for p in ("gate", "up", "down")} for e in exps]
@@ -237,6 +266,31 @@ def test_grouped_matmul_vs_dense_per_expert(E, K, N, T, k, bits, gs, xdtype, gat
         ref = experts[e]["gate"](x[torch.from_numpy(rows[offs[e]:offs[e + 1]]).long().to(DEV)])
         got = y[offs[e]:offs[e + 1]]
         assert max_rel_err(got.cpu().numpy(), ref.cpu().numpy()) < TOL, (e, offs[e + 1] - offs[e])
+
+
+@pytest.mark.parametrize("E,K,N,T,k,table,ydt", [
+    (16, 768, 256, 300, 8, "chosen", torch.float32),   # tensor-core GEMM, 16-byte staging loads
+    (16, 768, 256, 300, 8, "64", torch.float32),
+    (16, 768, 256, 300, 8, "32", torch.float16),       # scalar staging loads
+    (8, 256, 128, 5, 2, "chosen", torch.float32),      # decode GEMV tiles
+    (2, 24704, 64, 40, 1, "128", torch.float32),       # rows beyond the shared-memory staging
+])
+def test_down_swiglu_equals_act_then_down(E, K, N, T, k, table, ydt):
+    """ql_moe_grouped_matmul_swiglu (SwiGLU formed while staging) is bit-identical to ql_moe_act
+    into fp32 followed by ql_moe_grouped_matmul, on every tile height and staging path."""
+    g = torch.Generator(device=DEV).manual_seed(K + T)
+    qw = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, K // 8, N), dtype=torch.int32, device=DEV, generator=g)
+    qz = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, K // 128, N // 8), dtype=torch.int32, device=DEV, generator=g)
+    sc = (torch.rand((E, K // 128, N), device=DEV, generator=g) * 0.018 + 0.002).half()
+    dn = moe.StackedExperts.from_packed(qw, qz, sc, 128, 4)
+    logits = torch.randn((T, E), device=DEV, generator=g)
+    tr = moe.tile_rows_for(T * k, E, K, 128, T) if table == "chosen" else int(table)
+    r = moe.route(logits, k, True, tr)
+    y = (torch.randn((r.P, 2 * K), device=DEV, generator=g) * 3).to(ydt)
+    got = moe.down_swiglu(y, r, dn)
+    ref = moe.grouped_matmul(moe.act(y.float(), K), None, r, dn)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
 
 
 @pytest.fixture(scope="module")

@@ -61,7 +61,8 @@ SIGNATURES = {
                                        _c_int, _c_int, _c_int, _c_float, _vp, ctypes.c_size_t, _vp]),
     "ql_moe_grouped_matmul_swiglu": (_c_int, [_vp, _c_int, _c_long, _c_long, _vp, _vp, _vp, _c_int, _c_int, _vp,
                                               _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_int, _c_long,
-                                              _c_int, _c_int, _c_int, _c_int, _c_float, _vp]),
+                                              _c_int, _c_int, _c_int, _c_int, _c_float, _vp, ctypes.c_size_t,
+                                              _vp]),
     "ql_moe_act": (_c_int, [_vp, _c_long, _c_int, _vp, _c_int, _vp]),
     "ql_moe_combine": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_long, _vp, _c_long, _vp, _c_int,
                                 _c_long, _vp]),

@@ -79,12 +79,22 @@ __device__ __forceinline__ float absmax16(uint4 u, int x_dtype) {
 
 constexpr int kPrepSmemMax = 96 * 1024;   // rows up to this many bytes are staged through smem
 
+// SwiGLU of element k of a fused [gate | up] row y[base .. base + 2K): silu(g) * u with
+// silu(v) = v / (1 + e^-v), the expression of the MoE activation kernel (_core.py:502-503).
+__device__ __forceinline__ float swiglu_at(const void* y, int y_dtype, long base, int k, int K) {
+  const float g = load_as_float(y, y_dtype, base + k);
+  const float u = load_as_float(y, y_dtype, base + K + k);
+  return g / (1.0f + expf(-g)) * u;
+}
+
 // One CTA per row: the row is copied into shared memory with 16-byte loads (taking the row
 // maximum on the way), then gathered through the act-order permutation from shared memory.
+// With glu (== K) the row is a fused [gate | up] row of 2K values and the staged value is their
+// SwiGLU, formed once into shared memory as fp32.
 template <int BITS>
 __global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x, int x_dtype, long ldx,
                                                      const int32_t* __restrict__ perm,
-                                                     const int32_t* __restrict__ row_map, int M, int K,
+                                                     const int32_t* __restrict__ row_map, int M, int K, int glu,
                                                      __half* __restrict__ x16, int* __restrict__ row_exp) {
   extern __shared__ __align__(16) unsigned char xrow[];
   __shared__ float wmax[8];
@@ -95,7 +105,26 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x,
   const long row = row_map ? row_map[m] : m;   // row_map: MoE token gather
   const unsigned char* src = reinterpret_cast<const unsigned char*>(x) + (size_t)row * ldx * esz;
   float mx = 0.f;
-  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {   // K * esz is a multiple of 128 (K % 64 == 0)
+  if (glu) {
+    float* arow = reinterpret_cast<float*>(xrow);
+    if (x_dtype == QL_F32 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && K % 4 == 0) {
+      const float4* g4 = reinterpret_cast<const float4*>(src);
+      const float4* u4 = g4 + K / 4;
+      for (int i = tid; i < K / 4; i += blockDim.x) {
+        const float4 g = g4[i], u = u4[i];
+        const float a0 = g.x / (1.0f + expf(-g.x)) * u.x, a1 = g.y / (1.0f + expf(-g.y)) * u.y;
+        const float a2 = g.z / (1.0f + expf(-g.z)) * u.z, a3 = g.w / (1.0f + expf(-g.w)) * u.w;
+        reinterpret_cast<float4*>(arow)[i] = make_float4(a0, a1, a2, a3);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a0), fabsf(a1)), fmaxf(fabsf(a2), fabsf(a3))));
+      }
+    } else {
+      for (int k = tid; k < K; k += blockDim.x) {
+        const float v = swiglu_at(x, x_dtype, row * ldx, k, K);
+        arow[k] = v;
+        mx = fmaxf(mx, fabsf(v));
+      }
+    }
+  } else if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {   // K * esz is a multiple of 128 (K % 64 == 0)
     for (int i = tid; i < K * esz / 16; i += blockDim.x) {
       const uint4 u = reinterpret_cast<const uint4*>(src)[i];
       reinterpret_cast<uint4*>(xrow)[i] = u;
@@ -121,13 +150,14 @@ __global__ void __launch_bounds__(256) prep_x_kernel(const void* __restrict__ x,
   }
   __syncthreads();
   const float s = exp2i(-sh_e);
+  const int row_dtype = glu ? QL_F32 : x_dtype;
   for (int b = tid; b < K / 8; b += blockDim.x) {
     __align__(16) __half h[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int k = b * 8 + j;
       const int srck = perm ? perm[k] : k;
-      h[pair_pos<BITS>(j)] = __float2half_rn(load_as_float(xrow, x_dtype, srck) * s);
+      h[pair_pos<BITS>(j)] = __float2half_rn(load_as_float(xrow, row_dtype, srck) * s);
     }
     *reinterpret_cast<uint4*>(x16 + (long)m * K + b * 8) = *reinterpret_cast<uint4*>(h);
   }
@@ -138,14 +168,16 @@ template <int BITS>
 __global__ void __launch_bounds__(256) prep_x_global_kernel(const void* __restrict__ x, int x_dtype, long ldx,
                                                             const int32_t* __restrict__ perm,
                                                             const int32_t* __restrict__ row_map, int M, int K,
-                                                            __half* __restrict__ x16, int* __restrict__ row_exp) {
+                                                            int glu, __half* __restrict__ x16,
+                                                            int* __restrict__ row_exp) {
   __shared__ float wmax[8];
   __shared__ int sh_e;
   const int m = blockIdx.x;
   const int tid = threadIdx.x;
   const long base = (long)(row_map ? row_map[m] : m) * ldx;
   float mx = 0.f;
-  for (int k = tid; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(load_as_float(x, x_dtype, base + k)));
+  for (int k = tid; k < K; k += blockDim.x)
+    mx = fmaxf(mx, fabsf(glu ? swiglu_at(x, x_dtype, base, k, K) : load_as_float(x, x_dtype, base + k)));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((tid & 31) == 0) wmax[tid >> 5] = mx;
@@ -164,7 +196,8 @@ __global__ void __launch_bounds__(256) prep_x_global_kernel(const void* __restri
     for (int j = 0; j < 8; ++j) {
       const int k = b * 8 + j;
       const int src = perm ? perm[k] : k;
-      h[pair_pos<BITS>(j)] = __float2half_rn(load_as_float(x, x_dtype, base + src) * s);
+      const float v = glu ? swiglu_at(x, x_dtype, base, src, K) : load_as_float(x, x_dtype, base + src);
+      h[pair_pos<BITS>(j)] = __float2half_rn(v * s);
     }
     *reinterpret_cast<uint4*>(x16 + (long)m * K + b * 8) = *reinterpret_cast<uint4*>(h);
   }
@@ -172,8 +205,8 @@ __global__ void __launch_bounds__(256) prep_x_global_kernel(const void* __restri
 
 // Launch the activation staging for M rows.
 int launch_prep_x(int bits, const void* x, int x_dtype, long ldx, const int32_t* perm, const int32_t* row_map, int M,
-                  int K, __half* x16, int* row_exp, cudaStream_t st) {
-  const size_t bytes = (size_t)K * (x_dtype == QL_F32 ? 4 : 2);
+                  int K, __half* x16, int* row_exp, cudaStream_t st, int glu = 0) {
+  const size_t bytes = (size_t)K * (glu || x_dtype == QL_F32 ? 4 : 2);
   static int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -190,13 +223,13 @@ int launch_prep_x(int bits, const void* x, int x_dtype, long ldx, const int32_t*
   }
   if (bytes <= (size_t)kPrepSmemMax) {
     if (bits == 4)
-      prep_x_kernel<4><<<M, 256, bytes, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+      prep_x_kernel<4><<<M, 256, bytes, st>>>(x, x_dtype, ldx, perm, row_map, M, K, glu, x16, row_exp);
     else
-      prep_x_kernel<8><<<M, 256, bytes, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+      prep_x_kernel<8><<<M, 256, bytes, st>>>(x, x_dtype, ldx, perm, row_map, M, K, glu, x16, row_exp);
   } else if (bits == 4) {
-    prep_x_global_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+    prep_x_global_kernel<4><<<M, 256, 0, st>>>(x, x_dtype, ldx, perm, row_map, M, K, glu, x16, row_exp);
   } else {
-    prep_x_global_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, perm, row_map, M, K, x16, row_exp);
+    prep_x_global_kernel<8><<<M, 256, 0, st>>>(x, x_dtype, ldx, perm, row_map, M, K, glu, x16, row_exp);
   }
   return cuda_status(cudaGetLastError(), "prep_x launch");
 }
@@ -666,12 +699,14 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
 }
 
 // Grouped (MoE) GEMM over P permuted rows: x rows gathered through row_map, experts' weights
-// strided by *_estride elements, tiles from the device-built table (capacity max_tiles).
+// strided by *_estride elements, tiles from the device-built table (capacity max_tiles). With glu
+// (== K) each x row is a fused [gate | up] row of 2K values, staged as their SwiGLU.
 int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_map, int P, const int32_t* qweight,
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
                       int max_tiles, int tile_rows_n, int n_experts, void* out, int out_dtype, long ldo, int K,
-                      int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st) {
+                      int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st,
+                      int glu) {
   if (K % kSlabK != 0 || (gs % 64 != 0 && gs != 32) || N % (4 * (32 / bits)) != 0 ||
       (reinterpret_cast<uintptr_t>(qzeros) & 15)) {
     set_error("grouped GEMM: K=%d must be a multiple of 64, gs=%d a multiple of 64 or 32, N=%d of 32 (int4) / 16 "
@@ -690,7 +725,7 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
   __half* x16 = reinterpret_cast<__half*>(workspace);
   int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + (((size_t)P * K * 2 + 255) & ~(size_t)255));
   if (P == 0) return QL_OK;
-  int rc = launch_prep_x(bits, x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp, st);
+  int rc = launch_prep_x(bits, x, x_dtype, ldx, nullptr, row_map, P, K, x16, row_exp, st, glu);
   if (rc) return rc;
   GemmArgs a = {};
   a.qw = reinterpret_cast<const uint32_t*>(qweight);

@@ -338,6 +338,48 @@ __global__ void moe_combine_kernel(const float* __restrict__ z, const int32_t* _
   }
 }
 
+// The same sums (same order) four columns per thread, for H % 4 == 0 and 16-byte aligned rows:
+// CTA b covers token b / parts, columns [(b % parts) * 1024, +1024); each thread's k row loads
+// are independent 16-byte loads.
+__global__ void __launch_bounds__(256) moe_combine4_kernel(const float* __restrict__ z,
+                                                           const int32_t* __restrict__ pair_row,
+                                                           const float* __restrict__ topk_w, int k, int H, int parts,
+                                                           const float* __restrict__ shared, long lds,
+                                                           const float* __restrict__ shared_gate, long ldg,
+                                                           void* __restrict__ out, int out_dtype, long ldo) {
+  const int t = blockIdx.x / parts;
+  const int c4 = (blockIdx.x - t * parts) * blockDim.x + threadIdx.x;
+  if (c4 * 4 >= H) return;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int j = 0; j < k; ++j) {
+    const float w = topk_w[(long)t * k + j];
+    const float4 v = reinterpret_cast<const float4*>(z + (long)pair_row[(long)t * k + j] * H)[c4];
+    acc.x = fmaf(w, v.x, acc.x);
+    acc.y = fmaf(w, v.y, acc.y);
+    acc.z = fmaf(w, v.z, acc.z);
+    acc.w = fmaf(w, v.w, acc.w);
+  }
+  if (shared) {
+    float g = 1.f;
+    if (shared_gate) g = 1.0f / (1.0f + expf(-shared_gate[(long)t * ldg]));
+    const float4 v = reinterpret_cast<const float4*>(shared + (long)t * lds)[c4];
+    acc.x += g * v.x;
+    acc.y += g * v.y;
+    acc.z += g * v.z;
+    acc.w += g * v.w;
+  }
+  const long o = (long)t * ldo + 4L * c4;
+  if (out_dtype == QL_F32 && ((reinterpret_cast<uintptr_t>(out) | (uintptr_t)ldo * 4) & 15) == 0) {
+    reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o)[0] = acc;
+  } else {
+    store_from_float(out, out_dtype, o, acc.x);
+    store_from_float(out, out_dtype, o + 1, acc.y);
+    store_from_float(out, out_dtype, o + 2, acc.z);
+    store_from_float(out, out_dtype, o + 3, acc.w);
+  }
+}
+
 }  // namespace
 }  // namespace ql
 
@@ -434,6 +476,16 @@ extern "C" int ql_moe_combine(const float* z, const int32_t* pair_row, const flo
     return QL_ERR_ARG;
   }
   if (T == 0) return QL_OK;
+  const bool vec = H % 4 == 0 && (reinterpret_cast<uintptr_t>(z) & 15) == 0 &&
+                   (!shared || (lds % 4 == 0 && (reinterpret_cast<uintptr_t>(shared) & 15) == 0));
+  if (vec) {
+    const int parts = (H / 4 + 255) / 256;
+    if ((long)T * parts < 0x7fffffffL) {
+      moe_combine4_kernel<<<(unsigned)(T * parts), 256, 0, (cudaStream_t)stream>>>(
+          z, pair_row, topk_w, top_k, H, parts, shared, lds, shared_gate, ldg, out, out_dtype, ldo);
+      return cuda_status(cudaGetLastError(), "moe_combine launch");
+    }
+  }
   const long total = (long)T * H;
   const long blocks = (total + 255) / 256;
   moe_combine_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, (cudaStream_t)stream>>>(
@@ -451,7 +503,8 @@ int gptq_gemm_grouped(const void* x, int x_dtype, long ldx, const int32_t* row_m
                       const int32_t* qzeros, const void* scales, int sc_dtype, long qw_estride, long qz_estride,
                       long sc_estride, const int32_t* offsets, const int32_t* tiles, const int32_t* n_tiles,
                       int max_tiles, int tile_rows_n, int n_experts, void* out, int out_dtype, long ldo, int K,
-                      int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st);
+                      int N, int gs, int bits, float zoff, void* workspace, size_t ws_bytes, cudaStream_t st,
+                      int glu);
 size_t gptq_gemm_workspace(int M, int K);
 bool gptq_gemv_tma_grouped(const void* x, int x_dtype, long ldx, const int32_t* x_rows, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, int sc_dtype, int E, const int32_t* offsets,
@@ -539,10 +592,6 @@ static int grouped_matmul_impl(const void* x, int x_dtype, long ldx, const int32
   if (P == 0) return QL_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const long qw_es = (long)(K / per) * N, qz_es = (long)(K / gs) * (N / per), sc_es = (long)(K / gs) * N;
-  if (glu && is_gemm_tile(tile_rows) && grouped_uses_gemm(P, E, K, gs)) {
-    set_error("ql_moe_grouped_matmul_swiglu: the tensor-core path takes activations (run ql_moe_act first)");
-    return QL_ERR_UNSUPPORTED;
-  }
   if (is_gemm_tile(tile_rows) && grouped_uses_gemm(P, E, K, gs)) {
     if (!tiles || !n_tiles || max_tiles <= 0) {
       set_error("ql_moe_grouped_matmul: the tensor-core path needs the routing tile table");
@@ -550,7 +599,7 @@ static int grouped_matmul_impl(const void* x, int x_dtype, long ldx, const int32
     }
     int rc = gptq_gemm_grouped(x, x_dtype, ldx, row_token, (int)P, qweight, qzeros, scales, scales_dtype, qw_es,
                                qz_es, sc_es, offsets, tiles, n_tiles, max_tiles, tile_rows, E, out, out_dtype, ldo,
-                               K, N, gs, bits, zero_offset, workspace, workspace_bytes, st);
+                               K, N, gs, bits, zero_offset, workspace, workspace_bytes, st, glu);
     if (rc != QL_ERR_UNSUPPORTED) return rc;
   }
   const int max_active = (int)(P < E ? P : E);
@@ -582,8 +631,8 @@ extern "C" int ql_moe_grouped_matmul_swiglu(const void* y, int y_dtype, long ldy
                                             const int32_t* tiles, const int32_t* n_tiles, int max_tiles,
                                             int tile_rows, int max_rows_per_expert, void* out, int out_dtype,
                                             long ldo, int K, int N, int gs, int bits, float zero_offset,
-                                            void* stream) {
+                                            void* workspace, size_t workspace_bytes, void* stream) {
   return grouped_matmul_impl(y, y_dtype, ldy, nullptr, P, qweight, qzeros, scales, scales_dtype, E, offsets, active,
                              n_active, tiles, n_tiles, max_tiles, tile_rows, max_rows_per_expert, out, out_dtype, ldo,
-                             K, N, gs, bits, zero_offset, nullptr, 0, stream, K);
+                             K, N, gs, bits, zero_offset, workspace, workspace_bytes, stream, K);
 }

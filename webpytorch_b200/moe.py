@@ -9,10 +9,9 @@ QuantizedLinear per expert and projection.
 Here one forward is a fixed sequence of launches with no host round trip (so it can be
 captured in a CUDA graph):
   ql_moe_route            device softmax / top-k / histogram / scan / scatter
-  ql_moe_grouped_matmul   x rows gathered per expert @ stacked [gate | up] packs  -> [P, 2I]
-  ql_moe_act              silu(gate) * up                                         -> [P, I]
-  ql_moe_grouped_matmul   @ stacked down packs                                    -> [P, H]
-  (shared expert: one fused gate|up QuantizedLinear, act, down)
+  ql_moe_grouped_matmul          x rows gathered per expert @ stacked [gate | up] -> [P, 2I]
+  ql_moe_grouped_matmul_swiglu   silu(gate) * up formed while staging, @ stacked down -> [P, H]
+  (shared expert: the same two launches over one fused gate|up pack and its down)
   ql_moe_combine          weighted sum of each token's k rows (+ gated shared output)
 P = T * top_k sorted (token, expert) rows. The grouped GEMMs read each expert's row count on
 the device: decode steps (few rows per expert) run the split-K GEMV over active experts only,
@@ -26,9 +25,6 @@ from .qlinear import QuantizedLinear, _device
 __all__ = ["MoEBlock", "StackedExperts", "moe_mlp"]
 
 TILE_ROWS = 128   # rows per tile of the grouped tensor-core GEMM
-# Largest decode tile for which the down GEMV forms silu(gate) * up itself: every column tile of
-# the down projection recomputes it for its rows, which only pays off for a few rows.
-SWIGLU_FUSE_ROWS = 8
 
 
 def _as_quantized(lin, what):
@@ -163,14 +159,17 @@ def grouped_matmul(x, row_token, r, w, out_dtype=torch.float32, stream=None):
 
 def down_swiglu(y, r, w, out_dtype=torch.float32, stream=None):
     """z[P, N] = (silu(y[:, :K]) * y[:, K:]) @ W_e per expert segment, the activation formed while
-    staging (decode tile tables only)."""
+    staging (no [P, K] intermediate): per CTA in the decode GEMV, in the fp16 staging pass of the
+    tensor-core GEMM."""
     P = r.P
     z = torch.empty((P, w.N), dtype=out_dtype, device=y.device)
+    ws_bytes = _ffi.load().ql_moe_grouped_workspace(P, w.E, w.K, w.gs)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=y.device) if ws_bytes else None
     _ffi.call("ql_moe_grouped_matmul_swiglu", _ffi.ptr(y), _ffi.dtype_code(y.dtype), y.stride(0), P,
               _ffi.ptr(w.qweight), _ffi.ptr(w.qzeros), _ffi.ptr(w.scales), _ffi.dtype_code(w.scales.dtype), w.E,
               _ffi.ptr(r.offsets), _ffi.ptr(r.active), _ffi.ptr(r.n_active), _ffi.ptr(r.tiles), _ffi.ptr(r.n_tiles),
               r.max_tiles, r.tile_rows, r.T, _ffi.ptr(z), _ffi.dtype_code(z.dtype), z.stride(0), w.K, w.N, w.gs,
-              w.bits, float(w.zoff), _ffi.stream_ptr(stream))
+              w.bits, float(w.zoff), _ffi.ptr(ws), ws_bytes, _ffi.stream_ptr(stream))
     return z
 
 
@@ -241,20 +240,14 @@ class MoEBlock(torch.nn.Module):
     def expert_ffn(self, x, r, stream=None):
         """Routed experts' outputs for the sorted rows: z [P, H] fp32."""
         y = grouped_matmul(x, r.row_token, r, self.gate_up, stream=stream)
-        if r.tile_rows <= SWIGLU_FUSE_ROWS:   # small decode tiles: SwiGLU formed while staging
-            return down_swiglu(y, r, self.down, stream=stream)
-        a = act(y, self.I, stream=stream)
-        return grouped_matmul(a, None, r, self.down, stream=stream)
+        return down_swiglu(y, r, self.down, stream=stream)   # SwiGLU formed while staging
 
     def shared_ffn(self, x, stream=None):
         gu, dn = self.shared
         T = x.shape[0]
         r1 = _single_expert_routing(T, x.device, tile_rows_for(T, 1, gu.K, gu.gs, T))
         y = grouped_matmul(x, None, r1, gu, stream=stream)
-        if r1.tile_rows <= SWIGLU_FUSE_ROWS:
-            return down_swiglu(y, r1, dn, stream=stream)
-        a = act(y, self.SI, stream=stream)
-        return grouped_matmul(a, None, r1, dn, stream=stream)
+        return down_swiglu(y, r1, dn, stream=stream)
 
     def forward(self, x, out_dtype=torch.float32, stream=None):
         """x [T, H] (fp32/fp16/bf16 on the GPU) -> [T, H] in out_dtype (fp32 as the reference)."""

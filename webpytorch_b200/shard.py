@@ -87,10 +87,7 @@ class CudaBackend:
         """down(silu(gate(x)) * up(x)) for the rows x[row_src[p]] in expert-sorted order p
         (grouping from `group`); returns [n, H] in that sorted order."""
         y = _moe.grouped_matmul(x, row_src, grouping, gate_up)
-        if grouping.tile_rows <= _moe.SWIGLU_FUSE_ROWS:
-            return _moe.down_swiglu(y, grouping, down)
-        a = _moe.act(y, I)
-        return _moe.grouped_matmul(a, None, grouping, down)
+        return _moe.down_swiglu(y, grouping, down)
 
     def combine(self, z, pos_of, topk_w, T, k, H):
         out = torch.empty((T, H), dtype=torch.float32, device=z.device)
