@@ -296,7 +296,9 @@ struct SmemLayout {
   // barriers: full[NS], a_full[NS], slab_free[NS], d_full[2], d_empty[2], final
   static constexpr int kNumBars = 3 * NS + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kBytes = kMiscOff + 16 + 1024;      // + tmem slot, abort flag, alignment slack
+  static constexpr int kEpiOff = (kMiscOff + 16 + 15) & ~15;   // after the tmem slot and abort flag
+  static constexpr int kEpiBytes = 4 * 32 * 32 * 4;           // epilogue transpose, [32][32] fp32 a warp
+  static constexpr int kBytes = kEpiOff + kEpiBytes + 1024;   // + alignment slack
 };
 
 // Unpack one packed int4 word (8 values along K) for one column into 4 fp16 pairs
@@ -513,18 +515,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= kEpilogueWarp0) {
-    // ---------------- epilogue: thread = TMEM lane = output column, TMEM columns = tokens
+    // ---------------- epilogue: thread = TMEM lane = output column while draining TMEM (TMEM
+    // columns = tokens). Each 32-token chunk goes through a per-warp [32 tokens][32 columns]
+    // shared-memory transpose, after which a lane scales and stores 4 consecutive columns of one
+    // token: 8 lanes write a 128-byte row segment, 8 wide stores per chunk instead of 32 narrow.
     const int q = warp & 3;
-    const int lrow = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    float* stg = reinterpret_cast<float*>(smem + L::kEpiOff) + q * 32 * 32;
+    const int r8 = lane >> 3, c4 = (lane & 7) * 4;   // store role: rows r8 + 4i, columns c4 .. c4 + 3
+    const int osz = a.out_dtype == QL_F32 ? 4 : 2;
+    const bool wide = (a.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(a.out) & (4 * osz - 1)) == 0;
     int tcount = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tcount) {
       const int b = ND == 2 ? (tcount & 1) : 0;
       const int use = ND == 2 ? (tcount >> 1) : tcount;
       const int wt = tile % a.n_wtiles;
       const TileRows tr = tile_rows(a, tile / a.n_wtiles, BT);
-      const int n = wt * kTileN + lrow;
-      const float bias = (a.bias && n < a.N) ? a.bias[n] : 0.f;
+      const int n4 = wt * kTileN + q * 32 + c4;   // N % 16 == 0: n4 < N covers all four columns
+      float bias[4] = {0.f, 0.f, 0.f, 0.f};
+      if (a.bias && n4 < a.N) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) bias[i] = a.bias[n4 + i];
+      }
       int rexp[BT / 32];   // row exponent of token c * 32 + lane (broadcast with shuffles below)
 #pragma unroll
       for (int c = 0; c < BT / 32; ++c) {
@@ -542,13 +554,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_before();
           ptx::mbar_arrive(d_empty(b));  // accumulator drained into registers
         }
+        __syncwarp();   // the previous chunk's reads of the transpose are done
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int tok = tr.row0 + c * 32 + j;
-          const int e = __shfl_sync(0xffffffffu, rexp[c], j);
-          if (n < a.N && tok < tr.row_end) {
-            const float val = __uint_as_float(v[j]) * exp2i(e) + bias;
-            store_from_float(a.out, a.out_dtype, (long)tok * a.ldo + n, val);
+        for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = __uint_as_float(v[j]);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = 4 * i + r8;
+          const int tok = tr.row0 + c * 32 + r;
+          const float s = exp2i(__shfl_sync(0xffffffffu, rexp[c], r));
+          if (n4 < a.N && tok < tr.row_end) {
+            const float4 u = *reinterpret_cast<const float4*>(stg + r * 32 + c4);
+            const float o[4] = {u.x * s + bias[0], u.y * s + bias[1], u.z * s + bias[2], u.w * s + bias[3]};
+            const long idx = (long)tok * a.ldo + n4;
+            if (wide && a.out_dtype == QL_F32) {
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + idx) = make_float4(o[0], o[1], o[2], o[3]);
+            } else if (wide && a.out_dtype == QL_F16) {
+              uint2 h;
+              h.x = h2_as_u32(__floats2half2_rn(o[0], o[1]));
+              h.y = h2_as_u32(__floats2half2_rn(o[2], o[3]));
+              *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.out) + idx) = h;
+            } else if (wide && a.out_dtype == QL_BF16) {
+              const __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]), h1 = __floats2bfloat162_rn(o[2], o[3]);
+              uint2 h;
+              h.x = *reinterpret_cast<const uint32_t*>(&h0);
+              h.y = *reinterpret_cast<const uint32_t*>(&h1);
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + idx) = h;
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) store_from_float(a.out, a.out_dtype, idx + k, o[k]);
+            }
           }
         }
       }
@@ -620,6 +655,7 @@ int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_
     return QL_ERR_CUDA;
   }
   auto kern = gptq_gemm_tc_kernel<BITS, NS, BT, SK, DQ_ALT>;
+  static_assert(L::kBytes <= 227 * 1024, "shared memory per CTA");
   const int smem = L::kBytes;
   static int configured_dev = -1;
   static int sms = 0;
