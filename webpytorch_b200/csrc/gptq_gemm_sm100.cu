@@ -293,8 +293,9 @@ struct SmemLayout {
   static constexpr int kZBytes = 2 * (kTileN / PER) * 4;   // zeros [<= 2 groups][128 / PER]
   static constexpr int kStageBytes = (kZOff + kZBytes + 1023) & ~1023;
   static constexpr int kBarOff = NS * kStageBytes;
-  // barriers: full[NS], a_full[NS], slab_free[NS], d_full[2], d_empty[2], final
-  static constexpr int kNumBars = 3 * NS + 5;
+  // barriers: full[NS] (activations), a_full[NS], slab_free[NS], d_full[2], d_empty[2], final,
+  // w_full[NS] (packed weights, scales, zeros)
+  static constexpr int kNumBars = 4 * NS + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kEpiOff = (kMiscOff + 16 + 15) & ~15;   // after the tmem slot and abort flag
   static constexpr int kEpiBytes = 4 * 32 * 32 * 4;           // epilogue transpose, [32][32] fp32 a warp
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto d_full = [&](int b) { return bar0 + 8u * (3 * NS + b); };
   auto d_empty = [&](int b) { return bar0 + 8u * (3 * NS + 2 + b); };
   const uint32_t fin_bar = bar0 + 8u * (3 * NS + 4);
+  auto w_full = [&](int s) { return bar0 + 8u * (3 * NS + 5 + s); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 8);
 
@@ -366,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       ptx::mbar_init(full(s), 1);
+      ptx::mbar_init(w_full(s), 1);
       ptx::mbar_init(a_full(s), DQ_ALT ? kDequantWarps / 2 : kDequantWarps);
       ptx::mbar_init(slab_free(s), 1);
     }
@@ -400,7 +403,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer: activation tile, packed weights, scales, zeros per slab
     if (lane == 0) {
-      const uint32_t stage_tx = L::kXBytes + L::kWBytes + a.gb * kTileN * sc_bytes + a.gb * (kTileN / PER) * 4;
+      // the weight side of a stage has its own barrier so the dequant warps start on it while the
+      // (four times larger) activation tile is still in flight
+      const uint32_t w_tx = L::kWBytes + a.gb * kTileN * sc_bytes + a.gb * (kTileN / PER) * 4;
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -415,17 +420,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t st = sbase + s * L::kStageBytes;
           const int g0 = (kb * SK) / a.gs;
-          ptx::mbar_arrive_expect_tx(full(s), stage_tx);
+          ptx::mbar_arrive_expect_tx(w_full(s), w_tx);
+          ptx::tma_load_2d(st + L::kWOff, &tmap_w, w_full(s), wt * kTileN, wrow0 + kb * ROWS);
+          ptx::tma_load_2d(st + L::kSOff, &tmap_s, w_full(s), wt * kTileN, grow0 + g0);
+          ptx::tma_load_2d(st + L::kZOff, &tmap_z, w_full(s), wt * (kTileN / PER), grow0 + g0);
+          ptx::mbar_arrive_expect_tx(full(s), L::kXBytes);
 #pragma unroll
           for (int xb = 0; xb < SK / kSlabK; ++xb)
             ptx::tma_load_2d(st + xb * BT * 128, &tmap_x, full(s), kb * SK + xb * kSlabK, tr.row0);
-          ptx::tma_load_2d(st + L::kWOff, &tmap_w, full(s), wt * kTileN, wrow0 + kb * ROWS);
-          ptx::tma_load_2d(st + L::kSOff, &tmap_s, full(s), wt * kTileN, grow0 + g0);
-          ptx::tma_load_2d(st + L::kZOff, &tmap_z, full(s), wt * (kTileN / PER), grow0 + g0);
         }
       }
       if (!ok) {  // let the copies already in flight land before the CTA releases its smem
-        for (int j = it > NS ? it - NS : 0; j < it; ++j) ptx::mbar_wait_drain(full(j % NS), (j / NS) & 1);
+        for (int j = it > NS ? it - NS : 0; j < it; ++j) {
+          ptx::mbar_wait_drain(w_full(j % NS), (j / NS) & 1);
+          ptx::mbar_wait_drain(full(j % NS), (j / NS) & 1);
+        }
       }
     }
   } else if (warp == 1) {
@@ -474,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < nslab; ++kb, ++it) {
         if (DQ_ALT && (it & 1) != grp) continue;
         const int s = it % NS;
-        if (!ptx::mbar_wait_sleep(full(s), (it / NS) & 1, abort_flag)) goto done;
+        if (!ptx::mbar_wait_sleep(w_full(s), (it / NS) & 1, abort_flag)) goto done;
         const unsigned char* stp = smem + s * L::kStageBytes;
         const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
 #pragma unroll
