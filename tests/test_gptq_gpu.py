@@ -242,7 +242,7 @@ def test_gemm_path_desc_act_bias_ragged_n(M):
 
 
 @pytest.mark.parametrize("K,N", [(4096, 11008), (3584, 18944)])
-@pytest.mark.parametrize("M", [128, 512, 2048])
+@pytest.mark.parametrize("M", [64, 128, 512, 2048])
 def test_config3_full_size(K, N, M):
     """Config 3 (desc_act, bf16 x) at full size against the exact dequant in fp64."""
     w = synth.gptq_weights(K, N, 4, 128, seed=K + M, desc_act=True)

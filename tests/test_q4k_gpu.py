@@ -60,6 +60,23 @@ def test_config2_full_size(M):
     assert np.array_equal(W[:64].float().cpu().numpy().view(np.uint32), ref_w.view(np.uint32))
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 400, 2816), (64, 384, 1024), (128, 2048, 768), (300, 528, 4096),
+                                   (40, 37, 768)])
+@pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
+def test_tensor_core_path_vs_exact_dequant(M, N, K, xdt):
+    """M >= 16 takes the tcgen05 GEMM (super-blocks dequantised into TMEM; N % 16 != 0 stays on the
+    decode kernels): against the exact dequant in fp64 with a bias, ragged token and row tiles."""
+    rng = np.random.default_rng(M + N)
+    raw = synth.q4k_weights(N, K, rng=rng)
+    bias = rng.standard_normal(N).astype(np.float32)
+    lin = GGMLLinear(raw.tobytes(), "Q4_K", K, N, bias=bias)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(DEV).to(xdt)
+    y = lin(x)
+    W = q4k_dequant(_raw(raw), K, N).double()
+    ref = x.double() @ W.T + torch.from_numpy(bias).to(DEV).double()
+    assert max_rel_err(y.cpu().numpy(), ref.cpu().numpy()) < TOL
+
+
 @pytest.mark.parametrize("K", [768, 256, 2816])
 def test_bias_ragged_rows_and_host_io(K):
     rng = np.random.default_rng(3)

@@ -48,6 +48,9 @@ constexpr int kThreads = 512;
 constexpr int kDequantWarp0 = 4;
 constexpr int kDequantWarps = 8;
 constexpr int kEpilogueWarp0 = 12;
+constexpr int kFmtGptq = 0;          // packed GPTQ words + scale and zero rows (AutoGPTQ layout)
+constexpr int kFmtQ4K = 1;           // GGUF Q4_K super-blocks read in place: 144 bytes / 256 values
+constexpr int kQ4kBlockBytes = 144;
 
 // ---------------------------------------------------------------------------------------
 // activation staging: fp16, power-of-two row scale, act-order gather, (j, j+4) pair order
@@ -279,18 +282,21 @@ __device__ __forceinline__ TileRows tile_rows(const GemmArgs& a, int tt, int BT)
 
 // A stage covers SK values of K (64 or 128): SK / 64 activation boxes of [BT rows][64 K] fp16
 // (128-byte swizzled rows, one box after the other), the packed weights of those K, one or two
-// scale / zero rows.
-template <int BITS, int NS, int BT, int SK = kSlabK>
+// scale / zero rows. Q4_K stages hold the 64 quant bytes of each row's half super-block ([128][64],
+// 64-byte swizzled) and the rows' 16-byte block headers (d, dmin, scales).
+template <int BITS, int NS, int BT, int SK = kSlabK, int FMT = kFmtGptq>
 struct SmemLayout {
   static constexpr int PER = 32 / BITS;
   static constexpr int ROWS = SK / PER;                    // packed rows per stage (8 / 16 int4)
   static constexpr int kXBytes = BT * SK * 2;              // activation boxes, 128-byte swizzled rows
   static constexpr int kWOff = kXBytes;
-  static constexpr int kWBytes = ROWS * kTileN * 4;        // packed weights [ROWS][128]
+  // packed weights [ROWS][128] words, or (Q4_K) [128 rows][64 quant bytes]
+  static constexpr int kWBytes = FMT == kFmtQ4K ? kTileN * 64 : ROWS * kTileN * 4;
   static constexpr int kSOff = kWOff + kWBytes;
-  static constexpr int kSBytes = 2 * kTileN * 4;           // scales [<= 2 groups][128] (up to fp32)
+  // scales [<= 2 groups][128], or (Q4_K) the rows' block headers [128][16 bytes]
+  static constexpr int kSBytes = FMT == kFmtQ4K ? kTileN * 16 : 2 * kTileN * 4;
   static constexpr int kZOff = kSOff + kSBytes;
-  static constexpr int kZBytes = 2 * (kTileN / PER) * 4;   // zeros [<= 2 groups][128 / PER]
+  static constexpr int kZBytes = FMT == kFmtQ4K ? 0 : 2 * (kTileN / PER) * 4;   // zeros [<= 2][128 / PER]
   static constexpr int kStageBytes = (kZOff + kZBytes + 1023) & ~1023;
   static constexpr int kBarOff = NS * kStageBytes;
   // barriers: full[NS] (activations), a_full[NS], slab_free[NS], d_full[2], d_empty[2], final,
@@ -330,19 +336,22 @@ __device__ __forceinline__ void dq_int8(uint32_t w, uint32_t zlo, __half2 s2, ui
 // dequant work per MMA flop with one accumulator (the next tile waits for the drain).
 // SK = K per pipeline stage (64, or 128 for dense GEMMs with whole 128-value groups): a larger
 // stage halves every role's per-stage handshakes (barrier waits, TMEM-store waits, commits).
-template <int BITS, int NS, int BT, int SK, bool DQ_ALT_T>
+template <int BITS, int NS, int BT, int SK, bool DQ_ALT_T, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
     gptq_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_s, const __grid_constant__ CUtensorMap tmap_z,
                         const GemmArgs a) {
-  using L = SmemLayout<BITS, NS, BT, SK>;
+  using L = SmemLayout<BITS, NS, BT, SK, FMT>;
+  static_assert(FMT == kFmtGptq || (BITS == 4 && SK == 2 * kSlabK && DQ_ALT_T), "Q4_K: 128-value stages");
   constexpr int PER = L::PER;
   constexpr int ROWS = L::ROWS;
   constexpr int HROWS = ROWS / 2;               // packed rows per dequant half
   constexpr int TCOLS_A = SK / 2;               // TMEM columns per A stage (fp16 pairs)
   static_assert(SK == kSlabK || SK == 2 * kSlabK || SK == 4 * kSlabK, "stage K");
-  constexpr int ND = BT <= 128 ? 2 : 1;         // accumulator buffers
-  constexpr int DCOL = BT <= 128 ? 128 : BT;    // TMEM columns between accumulator buffers
+  static_assert(BT == 32 || BT == 64 || BT == 128, "token tile");
+  static_assert(!DQ_ALT_T || NS % 2 == 0, "alternating dequant groups: a stage's previous use is the group's own");
+  constexpr int ND = 2;                         // accumulator buffers
+  constexpr int DCOL = BT;                      // TMEM columns between accumulator buffers
   constexpr int A_COL = ND * DCOL;              // A stages start after the accumulators
   constexpr bool DQ_ALT = DQ_ALT_T;               // dequant groups on alternate stages
   constexpr uint32_t IDESC = ptx::idesc_f16_f32(kTileN, BT);
@@ -405,7 +414,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // the weight side of a stage has its own barrier so the dequant warps start on it while the
       // (four times larger) activation tile is still in flight
-      const uint32_t w_tx = L::kWBytes + a.gb * kTileN * sc_bytes + a.gb * (kTileN / PER) * 4;
+      const uint32_t w_tx = FMT == kFmtQ4K ? (uint32_t)(L::kWBytes + L::kSBytes)
+                                           : L::kWBytes + a.gb * kTileN * sc_bytes + a.gb * (kTileN / PER) * 4;
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
@@ -421,9 +431,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t st = sbase + s * L::kStageBytes;
           const int g0 = (kb * SK) / a.gs;
           ptx::mbar_arrive_expect_tx(w_full(s), w_tx);
-          ptx::tma_load_2d(st + L::kWOff, &tmap_w, w_full(s), wt * kTileN, wrow0 + kb * ROWS);
-          ptx::tma_load_2d(st + L::kSOff, &tmap_s, w_full(s), wt * kTileN, grow0 + g0);
-          ptx::tma_load_2d(st + L::kZOff, &tmap_z, w_full(s), wt * (kTileN / PER), grow0 + g0);
+          if constexpr (FMT == kFmtQ4K) {
+            // quant bytes of half kb & 1 of super-block kb / 2, and the block headers (x = byte
+            // offset in the row)
+            const int xb0 = (kb >> 1) * kQ4kBlockBytes;
+            ptx::tma_load_2d(st + L::kWOff, &tmap_w, w_full(s), xb0 + 16 + 64 * (kb & 1), wt * kTileN);
+            ptx::tma_load_2d(st + L::kSOff, &tmap_s, w_full(s), xb0, wt * kTileN);
+          } else {
+            ptx::tma_load_2d(st + L::kWOff, &tmap_w, w_full(s), wt * kTileN, wrow0 + kb * ROWS);
+            ptx::tma_load_2d(st + L::kSOff, &tmap_s, w_full(s), wt * kTileN, grow0 + g0);
+            ptx::tma_load_2d(st + L::kZOff, &tmap_z, w_full(s), wt * (kTileN / PER), grow0 + g0);
+          }
           ptx::mbar_arrive_expect_tx(full(s), L::kXBytes);
 #pragma unroll
           for (int xb = 0; xb < SK / kSlabK; ++xb)
@@ -485,6 +503,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = it % NS;
         if (!ptx::mbar_wait_sleep(w_full(s), (it / NS) & 1, abort_flag)) goto done;
         const unsigned char* stp = smem + s * L::kStageBytes;
+        if constexpr (FMT == kFmtQ4K) {
+          // this lane's row: d | dmin | scales[12] | qs[128]; the stage is half hb of the block,
+          // sub-blocks 4hb .. 4hb + 3 = low / high nibbles of qs chunks 2hb and 2hb + 1. Values
+          // are the reference's fp32 d*sc*q - dmin*m rounded once to fp16, in the (j, j + 4)
+          // pair order of the activation staging.
+          const uint4 hd = *reinterpret_cast<const uint4*>(stp + L::kSOff + lrow * 16);
+          const uint4* qrow = reinterpret_cast<const uint4*>(stp + L::kWOff + lrow * 64);
+          const int sw = (lrow >> 1) & 3;   // 64-byte swizzle: 16-byte chunk i sits at i ^ sw
+          const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffffu)));
+          const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+          const int hb = kb & 1;
+          uint32_t v[TCOLS_A];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint4 qa = qrow[(2 * c) ^ sw];
+            const uint4 qb = qrow[(2 * c + 1) ^ sw];
+            const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              uint32_t sc, mn;
+              q4k_scale_min(hd.y, hd.z, hd.w, 4 * hb + 2 * c + u, sc, mn);
+              const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                  // q as fp32 without a conversion instruction: 2^23 + q has q in its low
+                  // mantissa bits, and subtracting 2^23 is exact
+                  const float f0 = __int_as_float(0x4B000000u | ((qw[2 * g] >> (8 * p + 4 * u)) & 15u)) - 8388608.f;
+                  const float f1 = __int_as_float(0x4B000000u | ((qw[2 * g + 1] >> (8 * p + 4 * u)) & 15u)) - 8388608.f;
+                  v[(2 * c + u) * 16 + 4 * g + p] = h2_as_u32(__floats2half2_rn(fmaf(dl, f0, -ml), fmaf(dl, f1, -ml)));
+                }
+              }
+            }
+          }
+          const uint32_t ta = lane_addr + A_COL + s * TCOLS_A;
+          ptx::tmem_st32(ta, *reinterpret_cast<const uint32_t(*)[32]>(&v[0]));
+          ptx::tmem_st32(ta + 32, *reinterpret_cast<const uint32_t(*)[32]>(&v[32]));
+        } else {
         const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
 #pragma unroll
         for (int hh = 0; hh < (DQ_ALT ? 2 : 1); ++hh) {
@@ -516,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < TCOLS_A / 2; c += 32)
               ptx::tmem_st32(ta + c, *reinterpret_cast<const uint32_t(*)[32]>(&v[c]));
           }
+        }
         }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
@@ -634,13 +692,20 @@ bool encode(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const voi
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// n_experts: stacked weight matrices (grouped mode), 1 otherwise.
-template <int BITS, int BT, int SK = kSlabK, bool DQ_ALT = false>
+// n_experts: stacked weight matrices (grouped mode), 1 otherwise. FMT = kFmtQ4K: a.qw is the raw
+// Q4_K tensor [N rows][K / 256 blocks of 144 bytes].
+template <int BITS, int BT, int SK = kSlabK, bool DQ_ALT = false, int FMT = kFmtGptq>
 int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_t st) {
-  // ring depth: the TMEM A stages (NS * SK / 2 columns) fit beside the accumulators
-  constexpr int NS = SK == kSlabK ? (BT <= 128 ? (BITS == 4 ? 8 : 7) : 4) : (SK == 2 * kSlabK ? 4 : 2);
+  // ring depth: the TMEM A stages (NS * SK / 2 columns) fit beside the two BT-column
+  // accumulators, the stages in shared memory beside the epilogue's transpose (even with
+  // alternating dequant groups, at most 16)
+  constexpr int kStage = SmemLayout<BITS, 1, BT, SK, FMT>::kStageBytes;
+  constexpr int NS_T = (512 - 2 * BT) / (SK / 2);
+  constexpr int NS_S = (227 * 1024 - 4 * 32 * 32 * 4 - 2048 - 1024) / kStage;
+  constexpr int NS0 = NS_T < NS_S ? (NS_T < 16 ? NS_T : 16) : (NS_S < 16 ? NS_S : 16);
+  constexpr int NS = DQ_ALT ? (NS0 & ~1) : NS0;
   constexpr int PER = 32 / BITS;
-  using L = SmemLayout<BITS, NS, BT, SK>;
+  using L = SmemLayout<BITS, NS, BT, SK, FMT>;
   EncodeTiledFn enc = encode_fn();
   if (!enc) {
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled is unavailable");
@@ -652,18 +717,30 @@ int launch_gemm(const GemmArgs& a, const __half* x16, int n_experts, cudaStream_
                                   : a.sc_dtype == QL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUtensorMap tx, tw, ts, tz;
-  if (!encode(enc, &tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, a.K, a.M, (uint64_t)a.K * 2, kSlabK, BT,
-              CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode(enc, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qw, a.N, (uint64_t)n_experts * (a.K / PER),
-              (uint64_t)a.N * 4, kTileN, L::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode(enc, &ts, sdt, a.sc, a.N, (uint64_t)n_experts * G, (uint64_t)a.N * scb, kTileN, a.gb,
-              CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qz, a.N / PER, (uint64_t)n_experts * G,
-              (uint64_t)(a.N / PER) * 4, kTileN / PER, a.gb, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+  bool ok = encode(enc, &tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x16, a.K, a.M, (uint64_t)a.K * 2, kSlabK, BT,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+  if (FMT == kFmtQ4K) {
+    // two views of the rows: 64 quant bytes (one half super-block) and the 16-byte headers
+    const uint64_t row_bytes = (uint64_t)(a.K / 256) * kQ4kBlockBytes;   // a multiple of 16
+    ok = ok && encode(enc, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qw, row_bytes, (uint64_t)a.N, row_bytes, 64,
+                      kTileN, CU_TENSOR_MAP_SWIZZLE_64B) &&
+         encode(enc, &ts, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qw, row_bytes, (uint64_t)a.N, row_bytes, 16, kTileN,
+                CU_TENSOR_MAP_SWIZZLE_NONE);
+    tz = ts;   // unused by this format
+  } else {
+    ok = ok &&
+         encode(enc, &tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qw, a.N, (uint64_t)n_experts * (a.K / PER),
+                (uint64_t)a.N * 4, kTileN, L::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         encode(enc, &ts, sdt, a.sc, a.N, (uint64_t)n_experts * G, (uint64_t)a.N * scb, kTileN, a.gb,
+                CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         encode(enc, &tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.qz, a.N / PER, (uint64_t)n_experts * G,
+                (uint64_t)(a.N / PER) * 4, kTileN / PER, a.gb, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (!ok) {
     set_error("ql_gptq_matmul: cuTensorMapEncodeTiled failed");
     return QL_ERR_CUDA;
   }
-  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT, SK, DQ_ALT>;
+  auto kern = gptq_gemm_tc_kernel<BITS, NS, BT, SK, DQ_ALT, FMT>;
   static_assert(L::kBytes <= 227 * 1024, "shared memory per CTA");
   const int smem = L::kBytes;
   static int configured_dev = -1;
@@ -730,11 +807,61 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
     a.M = M; a.K = K; a.N = N; a.gs = gs; a.zoff = zoff;
     a.n_wtiles = (N + kTileN - 1) / kTileN;
     a.gb = gs == 32 ? 2 : 1;
-    a.n_ttiles = (M + 127) / 128;
-    if (K % 128 == 0 && gs % 128 == 0)   // 128-value stages (one scale row each), dequant groups alternating
+    const bool half_tile = M <= 64 && K % 128 == 0 && gs % 128 == 0;   // one 64-token tile, deeper ring
+    a.n_ttiles = half_tile ? 1 : (M + 127) / 128;
+    if (half_tile)
+      rc = bits == 4 ? launch_gemm<4, 64, 128, true>(a, x16, 1, st) : launch_gemm<8, 64, 128, true>(a, x16, 1, st);
+    else if (K % 128 == 0 && gs % 128 == 0)   // 128-value stages (one scale row each), dequant groups alternating
       rc = bits == 4 ? launch_gemm<4, 128, 128, true>(a, x16, 1, st) : launch_gemm<8, 128, 128, true>(a, x16, 1, st);
     else
       rc = bits == 4 ? launch_gemm<4, 128>(a, x16, 1, st) : launch_gemm<8, 128>(a, x16, 1, st);
+  }
+  if (owned) {
+    const int rc2 = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(workspace)");
+    if (!rc) rc = rc2;
+  }
+  return rc;
+}
+
+// GGUF Q4_K GEMM (M >= kQ4kGemmMinM): the same pipeline with the Q4_K dequant role reading each
+// row's super-blocks in place. Tiles of 32 / 64 / 128 tokens by M. *handled = false leaves the
+// call to the decode kernels (N not a multiple of 16, M below the threshold).
+int q4k_gemm_sm100(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
+                   int out_dtype, long ldo, int M, int K, int N, void* workspace, size_t ws_bytes, cudaStream_t st,
+                   bool* handled) {
+  *handled = false;
+  static int min_m = -1;
+  if (min_m < 0) min_m = env_int("QL_Q4K_GEMM_MIN_M", 16);
+  if (M < min_m || K % 256 != 0 || N % 16 != 0) return QL_OK;
+  *handled = true;
+  const size_t need = gptq_gemm_workspace(M, K);
+  void* ws = workspace;
+  bool owned = false;
+  if (ws == nullptr || ws_bytes < need) {
+    if (ws != nullptr) {
+      set_error("ql_q4k_matmul: workspace of %zu bytes is smaller than the %zu needed", ws_bytes, need);
+      return QL_ERR_ARG;
+    }
+    int rc = stream_alloc(&ws, need, st, "ql_q4k_matmul: workspace");
+    if (rc) return rc;
+    owned = true;
+  }
+  __half* x16 = reinterpret_cast<__half*>(ws);
+  int* row_exp = reinterpret_cast<int*>(reinterpret_cast<char*>(ws) + (((size_t)M * K * 2 + 255) & ~(size_t)255));
+  int rc = launch_prep_x(4, x, x_dtype, ldx, nullptr, nullptr, M, K, x16, row_exp, st);
+  if (!rc) {
+    GemmArgs a = {};
+    a.qw = reinterpret_cast<const uint32_t*>(raw);
+    a.bias = bias; a.row_exp = row_exp;
+    a.out = out; a.ldo = ldo; a.out_dtype = out_dtype;
+    a.M = M; a.K = K; a.N = N; a.gs = 256; a.zoff = 0.f; a.sc_dtype = QL_F16;
+    a.n_wtiles = (N + kTileN - 1) / kTileN;
+    a.gb = 1;
+    const int bt = M <= 32 ? 32 : M <= 64 ? 64 : 128;
+    a.n_ttiles = (M + bt - 1) / bt;
+    rc = bt == 32 ? launch_gemm<4, 32, 128, true, kFmtQ4K>(a, x16, 1, st)
+         : bt == 64 ? launch_gemm<4, 64, 128, true, kFmtQ4K>(a, x16, 1, st)
+                    : launch_gemm<4, 128, 128, true, kFmtQ4K>(a, x16, 1, st);
   }
   if (owned) {
     const int rc2 = cuda_status(cudaFreeAsync(ws, st), "cudaFreeAsync(workspace)");

@@ -37,20 +37,6 @@ __device__ __forceinline__ float f16_bits_to_float(uint32_t h) {
   return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
 }
 
-// 6-bit scale and min of sub-block j from the 12 scale bytes held in three words
-// s0 = bytes 0..3, s1 = bytes 4..7, s2 = bytes 8..11 (get_scale_min_k4).
-__device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, uint32_t& sc,
-                                              uint32_t& m) {
-  if (j < 4) {
-    sc = (s0 >> (8 * j)) & 63u;
-    m = (s1 >> (8 * j)) & 63u;
-  } else {
-    const int i = j - 4;
-    sc = ((s2 >> (8 * i)) & 0x0Fu) | (((s0 >> (8 * i + 6)) & 3u) << 4);
-    m = ((s2 >> (8 * i + 4)) & 0x0Fu) | (((s1 >> (8 * i + 6)) & 3u) << 4);
-  }
-}
-
 __global__ void q4k_dequant_kernel(const uint8_t* __restrict__ raw, float* __restrict__ W, long nblocks) {
   // one thread per (block, 32-value sub-block)
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < nblocks * 8; i += (long)gridDim.x * blockDim.x) {
@@ -383,6 +369,10 @@ bool q4k_gemv_tma(const void* x, int x_dtype, long ldx, const uint8_t* raw, cons
                   int out_dtype, long ldo, int M, int K, int N, cudaStream_t st, int* rc, void* workspace,
                   size_t ws_bytes);
 size_t q4k_stage_workspace(int M, int K);
+int q4k_gemm_sm100(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
+                   int out_dtype, long ldo, int M, int K, int N, void* workspace, size_t ws_bytes, cudaStream_t st,
+                   bool* handled);
+size_t gptq_gemm_workspace(int M, int K);
 }
 
 using namespace ql;
@@ -420,6 +410,9 @@ static int q4k_matmul_impl(const void* x, int x_dtype, long ldx, const uint8_t* 
   }
   cudaStream_t st = (cudaStream_t)stream;
   int rc = QL_OK;
+  bool handled = false;
+  rc = q4k_gemm_sm100(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, workspace, ws_bytes, st, &handled);
+  if (handled) return rc;
   if (q4k_gemv_tma(x, x_dtype, ldx, raw, bias, out, out_dtype, ldo, M, K, N, st, &rc, workspace, ws_bytes)) return rc;
   for (int m0 = 0; m0 < M; m0 += 16) {
     const int mc = (M - m0) < 16 ? (M - m0) : 16;
@@ -438,7 +431,8 @@ extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t
 
 extern "C" size_t ql_q4k_matmul_workspace(int M, int K) {
   if (M <= 0 || K <= 0 || K % kBlkVals != 0) return 0;
-  return q4k_stage_workspace(M, K);
+  const size_t a = q4k_stage_workspace(M, K), b = gptq_gemm_workspace(M, K);   // decode / tensor-core path
+  return a > b ? a : b;
 }
 
 extern "C" int ql_q4k_matmul_ws(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias,

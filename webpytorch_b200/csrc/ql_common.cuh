@@ -160,4 +160,18 @@ __device__ __forceinline__ void mma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 6-bit scale and min of sub-block j from the 12 scale bytes held in three words
+// s0 = bytes 0..3, s1 = bytes 4..7, s2 = bytes 8..11 (get_scale_min_k4).
+__device__ __forceinline__ void q4k_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, uint32_t& sc,
+                                              uint32_t& m) {
+  if (j < 4) {
+    sc = (s0 >> (8 * j)) & 63u;
+    m = (s1 >> (8 * j)) & 63u;
+  } else {
+    const int i = j - 4;
+    sc = ((s2 >> (8 * i)) & 0x0Fu) | (((s0 >> (8 * i + 6)) & 3u) << 4);
+    m = ((s2 >> (8 * i + 4)) & 0x0Fu) | (((s1 >> (8 * i + 6)) & 3u) << 4);
+  }
+}
+
 }  // namespace ql
