@@ -66,7 +66,7 @@ def peaks():
 
 MOE_E, MOE_TOPK, MOE_H, MOE_I = 128, 8, 2048, 768
 MOE_TOKENS = (1, 32, 256, 2048)
-Q4K_K, Q4K_N, Q4K_MS, Q4K_COPIES = 4096, 14336, (1, 8, 64), 8
+Q4K_K, Q4K_N, Q4K_MS, Q4K_COPIES = 4096, 14336, (1, 8, 16, 64, 512), 8
 
 
 def rand_gptq(K, N, dev, g, E=None, bits=4):
@@ -194,7 +194,7 @@ def bench_moe_ep(dev, g, world, timed):
 
 
 def bench_q4k(dev, g, hbm):
-    """Config 2: Q4_K dequant-GEMV/GEMM, K=4096, N=14336, fp32 x, M in {1, 8, 64}; rotating copies."""
+    """Config 2: Q4_K dequant-GEMV/GEMM, K=4096, N=14336, fp32 x, M in Q4K_MS; rotating copies."""
     torch = torch_mod()
     from webpytorch_b200.ggml import ggml_matmul
     raws = [rand_q4k(Q4K_N, Q4K_K, dev, g) for _ in range(Q4K_COPIES)]
@@ -300,10 +300,10 @@ def profile_case(name):
         x = torch.randn((T, MOE_H), device=dev, generator=g).to(torch.bfloat16)
         for _ in range(2):
             blk(x)
-    elif name in ("q4k", "q4k_m8"):          # q4k_gemv_tma_kernel, config 2, M=1 / 8, 8 copies (264 MB)
-        from webpytorch_b200.ggml import ggml_matmul
+    elif name in ("q4k", "q4k_m8", "q4k_m64"):   # config 2, 8 copies (264 MB): q4k_gemv_tma_kernel at M=1 / 8,
+        from webpytorch_b200.ggml import ggml_matmul   # the tensor-core path (gptq_gemm_tc_kernel<Q4_K>) at M=64
         raws = [rand_q4k(Q4K_N, Q4K_K, dev, g) for _ in range(Q4K_COPIES)]
-        M = 1 if name == "q4k" else 8
+        M = {"q4k": 1, "q4k_m8": 8, "q4k_m64": 64}[name]
         x = torch.randn((M, Q4K_K), device=dev, generator=g)
         y = torch.empty((M, Q4K_N), device=dev)
         for r in raws:
@@ -487,7 +487,7 @@ def main():
     ap.add_argument("--skip-extra", action="store_true", help="skip the config-2 and config-4 sections")
     ap.add_argument("--profile", default=None,
                     help="run one small fixed case for ncu: gemv | gemv_narrow | gemm | moe_decode | "
-                         "moe_prefill | q4k | q4k_m8 | ggml_q6k | decode_attn | decode_gateup")
+                         "moe_prefill | q4k | q4k_m8 | q4k_m64 | ggml_q6k | decode_attn | decode_gateup")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile:

@@ -514,9 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffffu)));
           const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
           const int hb = kb & 1;
-          uint32_t v[TCOLS_A];
+          const uint32_t ta = lane_addr + A_COL + s * TCOLS_A;
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < 2; ++c) {   // 32 TMEM columns per qs chunk, stored as soon as formed
+            uint32_t v[32];
             const uint4 qa = qrow[(2 * c) ^ sw];
             const uint4 qb = qrow[(2 * c + 1) ^ sw];
             const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
@@ -533,14 +534,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                   // mantissa bits, and subtracting 2^23 is exact
                   const float f0 = __int_as_float(0x4B000000u | ((qw[2 * g] >> (8 * p + 4 * u)) & 15u)) - 8388608.f;
                   const float f1 = __int_as_float(0x4B000000u | ((qw[2 * g + 1] >> (8 * p + 4 * u)) & 15u)) - 8388608.f;
-                  v[(2 * c + u) * 16 + 4 * g + p] = h2_as_u32(__floats2half2_rn(fmaf(dl, f0, -ml), fmaf(dl, f1, -ml)));
+                  v[u * 16 + 4 * g + p] = h2_as_u32(__floats2half2_rn(fmaf(dl, f0, -ml), fmaf(dl, f1, -ml)));
                 }
               }
             }
+            ptx::tmem_st32(ta + 32 * c, v);
           }
-          const uint32_t ta = lane_addr + A_COL + s * TCOLS_A;
-          ptx::tmem_st32(ta, *reinterpret_cast<const uint32_t(*)[32]>(&v[0]));
-          ptx::tmem_st32(ta + 32, *reinterpret_cast<const uint32_t(*)[32]>(&v[32]));
         } else {
         const uint32_t* wsm = reinterpret_cast<const uint32_t*>(stp + L::kWOff);
 #pragma unroll
