@@ -164,7 +164,8 @@ QL_API int ql_q4k_dequant(const uint8_t* raw, float* W, int N, int K, void* stre
 /*
  * y[M, N] = x[M, K] @ W[N, K]^T (+ bias) with W decoded from the raw Q4_K bytes inside the
  * kernel (no load-time re-layout). x of x_dtype with row stride ldx; out of out_dtype with
- * row stride ldo; bias NULL or fp32 [N]. raw must be 16-byte aligned; K % 256 == 0.
+ * row stride ldo; bias NULL or fp32 [N]. raw must be 16-byte aligned; K % 256 == 0. From 16
+ * tokens on (N % 16 == 0) the call runs the tcgen05 GEMM, below that the decode GEMV.
  * Replaces: webtorch/_core.py:3720-3734 (ggml_matmul) with the Q4_K decode of
  *           _core.py:3061-3068,3116-3133, called from GGMLLinear.forward _core.py:4399-4406.
  */
@@ -172,7 +173,8 @@ QL_API int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t* ra
                          void* out, int out_dtype, long ldo, int M, int K, int N, void* stream);
 
 /* Bytes of device workspace ql_q4k_matmul_ws needs for M tokens of a K-input weight (calls of
- * more than 4 tokens stage their activations once in it; 0 below that).
+ * more than 4 tokens stage their activations once in it, from 16 tokens on as the tensor-core
+ * path's fp16 rows; 0 below 5 tokens).
  * No counterpart in the reference (its WebGPU buffers are allocated per call). */
 QL_API size_t ql_q4k_matmul_workspace(int M, int K);
 

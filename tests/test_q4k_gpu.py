@@ -77,6 +77,25 @@ def test_tensor_core_path_vs_exact_dequant(M, N, K, xdt):
     assert max_rel_err(y.cpu().numpy(), ref.cpu().numpy()) < TOL
 
 
+@pytest.mark.parametrize("M", [3, 8, 16, 64])
+def test_workspace_entry_matches(M):
+    """ql_q4k_matmul_ws with a workspace of ql_q4k_matmul_workspace(M, K) bytes gives the same
+    result as ql_q4k_matmul (which takes its staging from the stream-ordered allocator)."""
+    from webpytorch_b200 import _ffi
+    N, K = 256, 1024
+    raw = _raw(synth.q4k_weights(N, K, seed=M))
+    x = torch.randn((M, K), device=DEV, generator=torch.Generator(device=DEV).manual_seed(M))
+    ref = ggml_matmul(x, raw, "Q4_K", K, N)
+    nbytes = int(_ffi.fn("ql_q4k_matmul_workspace")(M, K))
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=DEV)
+    out = torch.empty((M, N), device=DEV)
+    _ffi.call("ql_q4k_matmul_ws", x.data_ptr(), _ffi.dtype_code(x.dtype), x.stride(0), raw.data_ptr(), None,
+              out.data_ptr(), _ffi.dtype_code(out.dtype), out.stride(0), M, K, N, ws.data_ptr(), nbytes,
+              _ffi.stream_ptr())
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
 @pytest.mark.parametrize("K", [768, 256, 2816])
 def test_bias_ragged_rows_and_host_io(K):
     rng = np.random.default_rng(3)

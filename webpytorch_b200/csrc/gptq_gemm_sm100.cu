@@ -825,13 +825,17 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
 // GGUF Q4_K GEMM (M >= kQ4kGemmMinM): the same pipeline with the Q4_K dequant role reading each
 // row's super-blocks in place. Tiles of 32 / 64 / 128 tokens by M. *handled = false leaves the
 // call to the decode kernels (N not a multiple of 16, M below the threshold).
+int q4k_gemm_min_m() {
+  static int min_m = -1;
+  if (min_m < 0) min_m = env_int("QL_Q4K_GEMM_MIN_M", 16);
+  return min_m;
+}
+
 int q4k_gemm_sm100(const void* x, int x_dtype, long ldx, const uint8_t* raw, const float* bias, void* out,
                    int out_dtype, long ldo, int M, int K, int N, void* workspace, size_t ws_bytes, cudaStream_t st,
                    bool* handled) {
   *handled = false;
-  static int min_m = -1;
-  if (min_m < 0) min_m = env_int("QL_Q4K_GEMM_MIN_M", 16);
-  if (M < min_m || K % 256 != 0 || N % 16 != 0) return QL_OK;
+  if (M < q4k_gemm_min_m() || K % 256 != 0 || N % 16 != 0) return QL_OK;
   *handled = true;
   const size_t need = gptq_gemm_workspace(M, K);
   void* ws = workspace;

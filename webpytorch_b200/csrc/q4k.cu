@@ -373,6 +373,7 @@ int q4k_gemm_sm100(const void* x, int x_dtype, long ldx, const uint8_t* raw, con
                    int out_dtype, long ldo, int M, int K, int N, void* workspace, size_t ws_bytes, cudaStream_t st,
                    bool* handled);
 size_t gptq_gemm_workspace(int M, int K);
+int q4k_gemm_min_m();
 }
 
 using namespace ql;
@@ -431,7 +432,8 @@ extern "C" int ql_q4k_matmul(const void* x, int x_dtype, long ldx, const uint8_t
 
 extern "C" size_t ql_q4k_matmul_workspace(int M, int K) {
   if (M <= 0 || K <= 0 || K % kBlkVals != 0) return 0;
-  const size_t a = q4k_stage_workspace(M, K), b = gptq_gemm_workspace(M, K);   // decode / tensor-core path
+  const size_t a = q4k_stage_workspace(M, K);                                  // decode path
+  const size_t b = M >= q4k_gemm_min_m() ? gptq_gemm_workspace(M, K) : 0;     // tensor-core path
   return a > b ? a : b;
 }
 
