@@ -341,14 +341,51 @@ def profile_case(name):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled in the background."""
+    """SM clocks, power and throttle reasons sampled in the background during the timed region:
+    through NVML every millisecond when pynvml is importable (the timed regions are a few ms),
+    else with nvidia-smi. Read-only queries; no GPU setting is touched."""
 
     def __init__(self, index, period_ms=50):
         self.index, self.period_ms = index, period_ms
         self.samples = []
         self.proc = None
+        self.nvml = None
+        self.stop = False
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:   # the CUDA device's own GPU (CUDA ordinals and NVML indices can differ)
+            pr = torch_mod().cuda.get_device_properties(self.index)
+            bus = "%08x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId_v2(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def _poll(self):
+        nv, h = self.nvml
+        R = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+             nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                flags = ["Active" if rs & r else "Not Active" for r in R]
+                self.samples.append((time.time(), ["", str(sm), str(mx), str(pw), hex(rs)] + flags))
+            except Exception:
+                return
+            time.sleep(0.001)
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self.th = threading.Thread(target=self._poll, daemon=True)
+            self.th.start()
+            return self
+        except Exception:
+            self.nvml = None
         q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -372,6 +409,10 @@ class ClockSampler:
         return time.time()
 
     def __exit__(self, *a):
+        if self.nvml is not None:
+            self.stop = True
+            self.th.join(timeout=2)
+            return
         if self.proc is not None:
             time.sleep(self.period_ms / 1000.0 * 2)
             self.proc.terminate()
