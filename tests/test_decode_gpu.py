@@ -96,6 +96,21 @@ def test_graph_replay_equals_eager():
         assert torch.equal(ya, yb), pos
 
 
+@pytest.mark.parametrize("graph", [False, True])
+def test_programmatic_launch_equals_plain(graph):
+    """The step chained by programmatic dependent launch (the default) gives bit-identical
+    results to plain launches: every kernel waits for the previous one's outputs."""
+    layers, _, (H, NH, NKV, HD) = _model(seed=5)
+    a = DecodeStack(layers, H, NH, NKV, HD, 8, graph=graph, pdl=False)
+    b = DecodeStack(layers, H, NH, NKV, HD, 8, graph=graph, pdl=True)
+    rng = np.random.default_rng(6)
+    for pos in range(3):
+        e = rng.standard_normal(H).astype(np.float32)
+        ya = a.step(e, pos).clone()
+        yb = b.step(e, pos).clone()
+        assert torch.equal(ya, yb), pos
+
+
 def test_position_outside_cache_rejected():
     layers, _, (H, NH, NKV, HD) = _model(L=1)
     s = DecodeStack(layers, H, NH, NKV, HD, 4, graph=False)

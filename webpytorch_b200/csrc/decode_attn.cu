@@ -37,6 +37,11 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(
   __shared__ bool last;
   const int h = blockIdx.x, j = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int group = NH / NKV, g = h / group;
+  // launched as a programmatic dependent: q, k, v and the position are the previous kernel's
+  // output (every CTA waits before anything else, so this grid never completes ahead of it);
+  // the next kernel (the O projection) may then start streaming its weights
+  pdl_wait();
+  pdl_trigger();
   const int pos = *pos_ptr;
   const int half = HD / 2;
   if (pos < 0 || pos >= lmax) {   // a position outside the cache: NaN output, nothing written
@@ -232,9 +237,19 @@ extern "C" int ql_decode_attention(const float* qkv, int NH, int NKV, int HD, co
     set_error("ql_decode_attention: lmax=%d is above %d positions", lmax, kThreads * kChunk);
     return QL_ERR_UNSUPPORTED;
   }
-  const dim3 grid(NH, nsplit);
-  decode_attention_kernel<<<grid, kThreads, smem, (cudaStream_t)stream>>>(qkv, NH, NKV, HD, rope_cos, rope_sin, pos,
-                                                                          kcache, vcache, lmax, scale, out, part,
-                                                                          counters);
-  return cuda_status(cudaGetLastError(), "ql_decode_attention launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(NH, nsplit);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  if (launch_flags() & QL_LAUNCH_PDL) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_attention_kernel, qkv, NH, NKV, HD, rope_cos, rope_sin, pos,
+                                        kcache, vcache, lmax, scale, out, part, counters),
+                     "ql_decode_attention launch");
 }

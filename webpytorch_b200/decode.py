@@ -14,7 +14,9 @@ the layers, the captured command list is replayed; llm.py:1796-1814). Per layer:
     x  = rms(h, post_ln)               fused into the gate | up GEMV
     h  = h + (silu(g) * u) @ Wdown     SwiGLU formed while the down GEMV stages [g | u]; residual
 
-Five launches per layer, all of this library's kernels; buffers are fixed so the step replays.
+Five launches per layer, all of this library's kernels, chained by programmatic dependent launch
+(each may start streaming its weights while the previous one finishes); buffers are fixed so the
+step replays.
 """
 import math
 
@@ -100,7 +102,7 @@ class DecodeStack:
     replays the captured graph (captured on the first call), returning the last hidden state
     [1, H] (a view of the step's buffer)."""
 
-    def __init__(self, layers, H, NH, NKV, HD, lmax, theta=1e6, eps=1e-6, device=None, graph=True):
+    def __init__(self, layers, H, NH, NKV, HD, lmax, theta=1e6, eps=1e-6, device=None, graph=True, pdl=True):
         self.layers = layers
         self.H, self.NH, self.NKV, self.HD, self.lmax, self.eps = H, NH, NKV, HD, lmax, float(eps)
         dev = layers[0].qkv.qweight.device if device is None else torch.device(device)
@@ -121,6 +123,9 @@ class DecodeStack:
         self.att_ws = torch.zeros(int(_ffi.fn("ql_decode_attention_workspace")(NH, HD, lmax)), dtype=torch.uint8,
                                   device=dev)
         self.use_graph = graph
+        # programmatic dependent launch: each kernel of the step may start (and stream its weights)
+        # while the previous one finishes; every kernel waits for the previous one's outputs
+        self.pdl = bool(pdl)
         self.graph = None
         self.stream = None
 
@@ -128,6 +133,13 @@ class DecodeStack:
         return 5 * len(self.layers)
 
     def _forward(self, stream=None):
+        prev = _ffi.set_launch_flags(_ffi.LAUNCH_PDL if self.pdl else 0)
+        try:
+            return self._layers(stream)
+        finally:
+            _ffi.set_launch_flags(prev)
+
+    def _layers(self, stream=None):
         h = self.h
         for i, lay in enumerate(self.layers):
             fused_linear(h, lay.qkv, norm_weight=lay.in_ln, norm_eps=self.eps, out=self.qkv, stream=stream)
