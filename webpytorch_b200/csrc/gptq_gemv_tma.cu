@@ -165,6 +165,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   int M = a.M, e = 0;
   long row0 = 0;
   if (a.g_offsets) {
+    // the table is written by the routing kernel: under programmatic dependent launch it can be
+    // read only once that kernel has completed (this CTA's weights depend on it anyway)
+    pdl_wait();
     const int tz = blockIdx.z;
     if (tz >= *a.g_n_tiles) return;
     e = a.g_tiles[2 * tz];
