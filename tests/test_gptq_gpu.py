@@ -211,10 +211,10 @@ def test_empty_batch():
 
 
 # ---------------------------------------------------------------------------------------
-# tensor-core prefill path (M >= 64)
+# tensor-core prefill path (M >= 17)
 # ---------------------------------------------------------------------------------------
 @pytest.mark.parametrize("bits,gs", [(4, 128), (8, 128), (4, 32), (4, 64), (8, 32)])
-@pytest.mark.parametrize("M", [64, 128, 129, 300])
+@pytest.mark.parametrize("M", [17, 40, 64, 128, 129, 300])
 def test_gemm_path_vs_oracle(bits, gs, M):
     K, N = 512, 384
     w = synth.gptq_weights(K, N, bits, gs, seed=M + bits + gs)

@@ -41,7 +41,7 @@ def _noalloc(x, qw, qz, sc, K, N, gs, bits, zoff, out):
                                         (640, 2048, 384, 8),
                                         (1, 4096, 1024, 4),      # decode path, up to 4 tokens: no scratch
                                         (12, 1024, 512, 8),      # decode path, 5-16 tokens: staged activations
-                                        (40, 2048, 384, 4)])     # in the scratch, one 16-token chunk at a time
+                                        (40, 2048, 384, 4)])     # in the scratch; 40 tokens: tensor-core path
 def test_noalloc_matches_regular_entry_point_twice(M, K, N, bits):
     w = synth.gptq_weights(K, N, bits, 128, seed=M + K)
     qw = torch.from_numpy(w["qweight"]).to(DEV)

@@ -768,7 +768,10 @@ size_t gptq_gemm_workspace(int M, int K) {
 // True when a call of this shape takes the tensor-core (large-M) path below.
 bool gemm_path_taken(int M, int K, int gs) {
   static int min_m = -1;
-  if (min_m < 0) min_m = env_int("QL_GEMM_MIN_M", 64);
+  // measured: from 17 tokens on the tensor-core path beats the decode GEMV's 8-token slices
+  // (M = 24 / 32 / 48 on 4096x11008: 24.7 / 24.8 / 25.8 us against 36.7 / 42.8 / 65.9); up to 16
+  // tokens (the decode range) the GEMV keeps its per-group 23-bit activation staging
+  if (min_m < 0) min_m = env_int("QL_GEMM_MIN_M", 17);
   return M >= min_m && K % kSlabK == 0 && (gs % 64 == 0 || gs == 32);
 }
 
@@ -827,6 +830,9 @@ int gptq_gemm_sm100(const void* x, int x_dtype, long ldx, const int32_t* x_perm,
 // call to the decode kernels (N not a multiple of 16, M below the threshold).
 int q4k_gemm_min_m() {
   static int min_m = -1;
+  // below 16 tokens the decode GEMV stays, for its activation precision next to outlier channels
+  // (this path stages x as fp16 with one exponent per row), although M = 8 / 12 measured
+  // 33.7 / 34.0 us here against 35.2 / 53.5 through it
   if (min_m < 0) min_m = env_int("QL_Q4K_GEMM_MIN_M", 16);
   return min_m;
 }
